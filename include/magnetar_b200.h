@@ -1,0 +1,297 @@
+/*
+ * magnetar_b200.h — C ABI of the B200-native packed-weight matmul Provider.
+ *
+ * A drop-in for the quantized-matmul Kernels of the reference CPU Provider
+ * (astorise/Magnetar-provider-CPU, `NativeCpuProvider` / `NativeCpuExecutor`,
+ * src/native/mod.rs).  The entry points mirror the Rust traits `Provider` and
+ * `ProviderExecutionApi` (defined in the crate `magnetar-provider-api`,
+ * implemented by the reference at src/native/mod.rs:565-947) with plain
+ * pointers and sizes, so a thin Rust `extern "C"` adapter can implement those
+ * traits over this library (INTEGRATION.md shows the binding).
+ *
+ * All entry points are thread-safe.  Tensors cross the boundary as host f32
+ * buffers (copied in and out; the caller keeps ownership) or, for the
+ * low-level `mgb_qmatmul*` family, as device pointers.  Every status other
+ * than MGB_OK leaves a reason in `mgb_last_error()` (thread-local).
+ */
+#ifndef MAGNETAR_B200_H
+#define MAGNETAR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MGB_ABI_VERSION 1
+#define MGB_MAX_RANK 8
+
+/* Status codes.  The kernel errors follow `KernelError` (src/lib.rs:2193-2230,
+ * :2445-2456, :3052-3057); MGB_DECLINED is `PackedWeightWrite::Declined`
+ * (src/native/mod.rs:638-653); MGB_MEMORY_DENIED is
+ * `MemoryError::AllocationDenied` (src/lib.rs:1769-1771). */
+typedef enum mgb_status {
+    MGB_OK = 0,
+    MGB_DECLINED = 1,
+    MGB_EXECUTION_FAILED = 2,
+    MGB_DTYPE_UNSUPPORTED = 3,
+    MGB_ATTRIBUTE_UNSUPPORTED = 4,
+    MGB_KERNEL_NOT_FOUND = 5,
+    MGB_TIMEOUT = 6,
+    MGB_MEMORY_DENIED = 7,
+    MGB_UNKNOWN_HANDLE = 8,
+    MGB_NOT_FOUND = 9,
+    MGB_INVALID_ARGUMENT = 10,
+    MGB_CUDA_ERROR = 11,
+    MGB_NCCL_ERROR = 12,
+    MGB_UNSUPPORTED = 13
+} mgb_status;
+
+/* Packed block formats.  Codes follow the reference's `FORMATS` order
+ * (src/native/quant.rs:71-87).  This Provider stores Q8_0, Q4_K, IQ4_NL and
+ * Q4_0 and declines the rest (the Runtime then loads those weights as f32). */
+enum {
+    MGB_FORMAT_Q8_0 = 0,
+    MGB_FORMAT_Q4_K = 1,
+    MGB_FORMAT_Q6_K = 2,
+    MGB_FORMAT_Q2_K = 3,
+    MGB_FORMAT_Q3_K = 4,
+    MGB_FORMAT_IQ4_NL = 5,
+    MGB_FORMAT_IQ4_XS = 6,
+    MGB_FORMAT_IQ2_XXS = 7,
+    MGB_FORMAT_IQ2_XS = 8,
+    MGB_FORMAT_IQ2_S = 9,
+    MGB_FORMAT_IQ3_XXS = 10,
+    MGB_FORMAT_IQ3_S = 11,
+    MGB_FORMAT_Q5_K = 12,
+    MGB_FORMAT_Q4_0 = 13
+};
+
+enum { MGB_DTYPE_F32 = 0, MGB_DTYPE_F16 = 1, MGB_DTYPE_BF16 = 2 };
+enum { MGB_KERNEL_AUTO = 0, MGB_KERNEL_GEMV = 1, MGB_KERNEL_GEMM = 2 };
+enum { MGB_CANCELLATION_TIMEOUT_ONLY = 1 };
+enum { MGB_HEALTH_AVAILABLE = 0, MGB_HEALTH_UNAVAILABLE = 1 };
+enum { MGB_VALUE_ABSENT = 0, MGB_VALUE_OPAQUE = 1 };
+
+/* Observation kinds (`KernelObservationKind`, src/lib.rs:2367-2402, :3387-3401). */
+enum {
+    MGB_OBS_PROVIDER_REGISTERED = 0,
+    MGB_OBS_DEVICE_DETECTED = 1,
+    MGB_OBS_DISPATCH_STARTED = 2,
+    MGB_OBS_DISPATCH_COMPLETED = 3,
+    MGB_OBS_DISPATCH_FAILED = 4,
+    MGB_OBS_TIMEOUT = 5
+};
+
+typedef struct mgb_provider mgb_provider;
+
+/* Provider controls, read once per Provider like the reference's environment
+ * controls (src/native/mod.rs:8-31, :505-522). */
+typedef struct mgb_settings {
+    int32_t packed_weights;   /* MAGNETAR_B200_PACKED_WEIGHTS (0 declines packed weights), default 1 */
+    int32_t int8_activations; /* MAGNETAR_B200_INT8_ACTIVATIONS, default 0 (f32 activations) */
+    int32_t device;           /* MAGNETAR_B200_DEVICE, CUDA ordinal, default 0 */
+    int32_t profile;          /* MAGNETAR_B200_PROFILE=1 times every Kernel by name */
+    int32_t kernel;           /* MAGNETAR_B200_KERNEL=auto|gemv|gemm (MGB_KERNEL_*) */
+} mgb_settings;
+
+typedef struct mgb_provider_metadata {
+    const char *name;         /* "magnetar:provider/b200-native" */
+    const char *version;
+    const char *vendor;
+    const char *description;
+} mgb_provider_metadata;
+
+/* `native_cpu_device()` counterpart (src/native/mod.rs:825-842). */
+typedef struct mgb_device_descriptor {
+    char id[64];              /* "cuda-b200:<ordinal>" */
+    char name[128];
+    char architecture[32];    /* "sm_100a" */
+    uint32_t compute_units;   /* SMs */
+    uint64_t memory_bytes;
+    uint32_t max_concurrent_operations;
+    uint64_t max_workspace_bytes;
+} mgb_device_descriptor;
+
+/* `KernelAdvertisement` for the Kernels this Provider executes
+ * (`baseline_advertisement`, src/lib.rs:1350-1373): rank 2, f32 in and out,
+ * contiguous, cancellation TimeoutOnly. */
+typedef struct mgb_kernel_advertisement {
+    const char *name;         /* "matmul", "matmul-bias", "matmul-residual" */
+    const char *operator_family;
+    int32_t rank;
+    int32_t input_dtype;
+    int32_t output_dtype;
+    int32_t cancellation;
+} mgb_kernel_advertisement;
+
+/* Attributes of one Kernel invocation (`KernelInvocation::attributes`). */
+typedef struct mgb_kernel_attrs {
+    int32_t transpose_a;
+    int32_t transpose_b;
+    int32_t accumulation_dtype; /* MGB_DTYPE_F32; any other value is rejected (src/lib.rs:2445-2456) */
+    int64_t deadline_ms;        /* < 0 none; 0 already elapsed -> MGB_TIMEOUT (src/lib.rs:2372-2380) */
+} mgb_kernel_attrs;
+
+/* `KernelResult` of a completed invocation. */
+typedef struct mgb_kernel_result {
+    int32_t status;           /* MGB_OK or the kernel's error code */
+    char reason[256];
+} mgb_kernel_result;
+
+typedef struct mgb_observation {
+    uint64_t sequence;
+    int32_t kind;             /* MGB_OBS_* */
+    char kernel[48];
+    char detail[112];
+} mgb_observation;
+
+/* ---- errors -------------------------------------------------------------------------- */
+
+/* The last failure's reason on this thread (reference wording where one exists). */
+const char *mgb_last_error(void);
+const char *mgb_status_name(int32_t status);
+
+/* ---- identity / lifecycle (`Provider`, src/native/mod.rs:901-947) -------------------- */
+
+int32_t mgb_abi_version(void);
+/* `native_cpu_provider_metadata()` counterpart (src/native/mod.rs:813-821). */
+void mgb_provider_get_metadata(mgb_provider_metadata *out);
+/* `NativeCpuExecutor::new()` environment parsing (src/native/mod.rs:505-522). */
+mgb_status mgb_settings_from_env(mgb_settings *out);
+/* `NativeCpuExecutor::with_settings` (src/native/mod.rs:525-544); settings NULL = from env. */
+mgb_status mgb_provider_create(const mgb_settings *settings, mgb_provider **out);
+/* Releases every device allocation; prints the profile when enabled (mod.rs:476-496). */
+void mgb_provider_destroy(mgb_provider *provider);
+/* `Provider::initialize` (src/native/mod.rs:928-938): records ProviderRegistered
+ * and DeviceDetected observations. */
+mgb_status mgb_provider_initialize(mgb_provider *provider);
+/* `Provider::shutdown` (src/native/mod.rs:940-942). */
+mgb_status mgb_provider_shutdown(mgb_provider *provider);
+/* `Provider::health` (src/native/mod.rs:909-911). */
+int32_t mgb_provider_health(mgb_provider *provider);
+/* `Provider::devices` (src/native/mod.rs:919-921). */
+mgb_status mgb_provider_device(mgb_provider *provider, mgb_device_descriptor *out);
+/* `Provider::kernel_advertisements` (src/native/mod.rs:848-864). */
+size_t mgb_kernel_advertisement_count(void);
+mgb_status mgb_kernel_advertisement_get(size_t index, mgb_kernel_advertisement *out);
+
+/* ---- tensor storage (`ProviderExecutionApi`, src/native/mod.rs:629-811) -------------- */
+
+/* `write_tensor` (mod.rs:629-636): stores an f32 tensor, forgetting any packed
+ * weight under `id`. */
+mgb_status mgb_write_tensor(mgb_provider *provider, const char *id, const uint64_t *shape,
+                            int32_t rank, const float *data);
+/* `write_packed_weight_tensor` (mod.rs:638-653): copies the checkpoint's block
+ * bytes to the device.  *stored = 1 (Stored) or 0 (Declined: packed weights
+ * disabled, or a format this Provider does not execute).  `transposed` = 1 when
+ * the stored rows are the output columns (logical [stored_cols, stored_rows]). */
+mgb_status mgb_write_packed_weight(mgb_provider *provider, const char *id, int32_t format,
+                                   uint64_t stored_rows, uint64_t stored_cols,
+                                   int32_t transposed, const void *bytes, uint64_t len,
+                                   int32_t *stored);
+/* `read_tensor` (src/lib.rs:1615-1620): f32 values in logical shape; a packed
+ * weight reads back dequantised (bit-exact to the reference `decode`).
+ * shape_out has room for MGB_MAX_RANK entries; MGB_NOT_FOUND when absent. */
+mgb_status mgb_read_tensor(mgb_provider *provider, const char *id, float *out,
+                           uint64_t capacity, uint64_t *shape_out, int32_t *rank_out);
+/* `resident_shape` (src/lib.rs:1748-1753): logical shape. */
+mgb_status mgb_resident_shape(mgb_provider *provider, const char *id, uint64_t *shape_out,
+                              int32_t *rank_out);
+/* `release_tensor` (mod.rs:659-662). */
+mgb_status mgb_release_tensor(mgb_provider *provider, const char *id, int32_t *was_present);
+/* `NativeCpuExecutor::is_packed` (mod.rs:556-558). */
+int32_t mgb_is_packed(mgb_provider *provider, const char *id);
+/* `read_tensor_value` (mod.rs:695-702): MGB_VALUE_OPAQUE for resident ids. */
+mgb_status mgb_read_tensor_value(mgb_provider *provider, const char *id, int32_t *kind);
+/* `write_tensor_value(id, Opaque)` (mod.rs:704-721): stores nothing; a packed
+ * weight stays resident. */
+mgb_status mgb_write_tensor_value_opaque(mgb_provider *provider, const char *id);
+/* `copy_tensor_admitted` (mod.rs:746-765): `to` takes a copy of `from`,
+ * replacing whatever `to` held, a packed weight included. */
+mgb_status mgb_copy_tensor(mgb_provider *provider, const char *from, const char *to);
+/* Free / total device bytes, for the caller's admission ledger
+ * (`write_tensor_admitted`, src/lib.rs:1713-1738). */
+mgb_status mgb_device_memory(mgb_provider *provider, uint64_t *free_bytes,
+                             uint64_t *total_bytes);
+/* Packed weights expanded to f32 (count), as the reference's profile reports
+ * (`NativeState::expand`, mod.rs:196-204). */
+uint64_t mgb_materialization_count(mgb_provider *provider);
+
+/* ---- execution (`submit_kernel` / `complete_kernel`, mod.rs:598-627,
+ *      src/lib.rs:2301-2356) --------------------------------------------------------- */
+
+/* Validates and enqueues one Kernel invocation on the Provider's stream and
+ * returns its handle.  inputs[0] = activations [m, k] (f32 tensor id),
+ * inputs[1] = weight (packed or f32 id), inputs[2] = bias ("matmul-bias") or
+ * residual ("matmul-residual").  The result (success or the Kernel's error) is
+ * observed exactly once through mgb_complete_kernel. */
+mgb_status mgb_submit_kernel(mgb_provider *provider, const char *kernel,
+                             const mgb_kernel_attrs *attrs, const char *const *inputs,
+                             int32_t n_inputs, const char *output, uint64_t *handle);
+/* Waits for the invocation and consumes its result; a second call for the
+ * same handle returns MGB_UNKNOWN_HANDLE (single consumption, src/lib.rs:2337-2356). */
+mgb_status mgb_complete_kernel(mgb_provider *provider, uint64_t handle,
+                               mgb_kernel_result *result);
+
+/* ---- observations (`observations`, src/lib.rs:1848-1868) ---------------------------- */
+
+size_t mgb_observation_count(mgb_provider *provider);
+/* Oldest first, at most 4096 kept (KERNEL_OBSERVATION_LOG_CAPACITY, src/lib.rs:171). */
+mgb_status mgb_observations(mgb_provider *provider, mgb_observation *out, size_t capacity,
+                            size_t *written);
+
+/* ---- low-level device entry points (the kernels behind the Provider) ---------------- */
+
+/* The kernels read a packed matrix in its *device layout*: the checkpoint's
+ * ggml blocks rearranged into a quant plane (each 32-value run's quants in 16
+ * or 32 aligned bytes, value pairs adjacent) followed by a scale plane (Q4_K:
+ * the 16-byte d/dmin/scales header per super-block; Q8_0, IQ4_NL, Q4_0: the
+ * f16 scale per block).  Same bits, same byte count as the ggml blocks.
+ * `mgb_write_packed_weight` performs this rearrangement itself. */
+uint64_t mgb_packed_bytes(int32_t format, uint64_t stored_rows, uint64_t stored_cols);
+/* ggml blocks (device memory, `stored_rows` rows of `stored_cols` values) ->
+ * device layout in `out` (device memory of mgb_packed_bytes bytes). */
+mgb_status mgb_repack(int32_t format, const void *ggml_blocks, uint64_t stored_rows,
+                      uint64_t stored_cols, void *out, void *stream);
+/* Scratch bytes `mgb_qmatmul` needs for this shape (0 when none). */
+uint64_t mgb_qmatmul_workspace_bytes(int32_t format, uint64_t m, uint64_t n, uint64_t k);
+/* y[m, n] = x[m, k] * W^T on `stream`, W (device layout, 16-byte aligned)
+ * with its n stored rows the output columns (`packed_matmul`,
+ * src/native/mod.rs:109-152).  Device pointers.  `addend` (may be NULL) is added to y:
+ * addend_len == n broadcasts one row (matmul-bias), == m*n adds elementwise
+ * (matmul-residual).  Replaces `matmul_columns` (src/native/quant.rs:430-598). */
+mgb_status mgb_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, const float *x,
+                       uint64_t m, float *y, const float *addend, uint64_t addend_len,
+                       void *workspace, uint64_t workspace_bytes, void *stream);
+/* Stored-order f32 values of a packed matrix (device layout), bit-exact to the reference
+ * `dequantize_row` (src/native/quant.rs:1700-1711) on every stored row. */
+mgb_status mgb_dequantize(int32_t format, const void *w, uint64_t stored_rows,
+                          uint64_t stored_cols, float *out, void *stream);
+/* y[m, stored_cols] = x[m, stored_rows] * W (device layout) for a weight whose
+ * stored rows are the input rows (`packed_axpy`, src/native/mod.rs:154-194; `axpy_columns`,
+ * src/native/quant.rs:1658-1689). */
+mgb_status mgb_qmatmul_input_major(int32_t format, const void *w, uint64_t stored_rows,
+                                   uint64_t stored_cols, const float *x, uint64_t m, float *y,
+                                   void *stream);
+/* Dense f32 y = op(a) * op(b) with the reference matmul's transposes
+ * (`matmul`, src/lib.rs:262-318). */
+mgb_status mgb_matmul_f32(const float *a, uint64_t a_rows, uint64_t a_cols, const float *b,
+                          uint64_t b_rows, uint64_t b_cols, int32_t transpose_a,
+                          int32_t transpose_b, float *out, void *stream);
+/* Reads and clears the device error code the low-level kernels of `device`
+ * record instead of trapping (1 = a bounded wait expired; 0 = none).
+ * Synchronises with the device.  No counterpart in the reference (its kernels
+ * run synchronously on the calling thread). */
+mgb_status mgb_take_device_error(int32_t device, int32_t *code);
+/* Int8 activation quantisation (`quantize_rows`, src/native/quant.rs:350-378):
+ * values[len], scales[len/32], sums[len/32][2]. */
+mgb_status mgb_quantize_rows(const float *x, uint64_t len, int8_t *values, float *scales,
+                             int32_t *sums, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MAGNETAR_B200_H */

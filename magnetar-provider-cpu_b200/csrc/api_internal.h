@@ -1,0 +1,27 @@
+// Host-side helpers shared by api.cpp and provider.cpp.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/magnetar_b200.h"
+
+namespace mgb {
+
+// Records `fmt` as this thread's last error and returns `status`.
+mgb_status fail(mgb_status status, const char *fmt, ...);
+mgb_status cuda_fail(cudaError_t e, const char *what);
+void clear_error();
+
+bool format_supported(int32_t format);
+uint64_t ggml_bytes(int32_t format, uint64_t rows, uint64_t cols);
+mgb_status check_packed_shape(int32_t format, uint64_t rows, uint64_t cols);
+int *device_error_flag(int device);
+
+mgb_status validate_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, const float *x,
+                            uint64_t m, float *y);
+mgb_status run_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, const float *x,
+                       uint64_t m, float *y, const float *addend, int addend_mode, void *workspace,
+                       uint64_t workspace_bytes, int *err, int kernel_pref, cudaStream_t stream);
+
+}  // namespace mgb

@@ -1,0 +1,148 @@
+// Shared device-side definitions of the B200 packed-weight matmul Provider:
+// format codes, the device layout of packed matrices, exact f16 decoding and
+// the bounded mbarrier / bulk-copy PTX wrappers the kernels are built on.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mgb {
+
+// Format codes: the reference's `FORMATS` order (src/native/quant.rs:71-87).
+enum Format : int { Q8_0 = 0, Q4_K = 1, IQ4_NL = 5, Q4_0 = 13 };
+
+constexpr int RUN = 32;  // values per run (src/native/quant.rs:19)
+
+__host__ __device__ inline bool supported(int f) {
+  return f == Q8_0 || f == Q4_K || f == IQ4_NL || f == Q4_0;
+}
+__host__ __device__ inline int block_elements(int f) { return f == Q4_K ? 256 : 32; }
+__host__ __device__ inline int block_bytes(int f) {
+  return f == Q4_K ? 144 : (f == Q8_0 ? 34 : 18);
+}
+
+// Device layout of an [n stored rows x k stored cols] packed matrix: the
+// quant plane (n rows of `qs_row` bytes: one 16-byte run of nibble pairs for
+// the 4-bit formats, 32 bytes per run for Q8_0) followed by the scale plane
+// (n rows of k/16 bytes: Q4_K's 16-byte d/dmin/scales header per 256 values,
+// or one f16 scale per 32 values).  The byte count equals the ggml blocks'.
+struct Layout {
+  uint64_t n, k, qs_row, sc_row, qs_bytes, total;
+  __host__ __device__ Layout(int f, uint64_t n_, uint64_t k_) : n(n_), k(k_) {
+    qs_row = f == Q8_0 ? k : k / 2;
+    sc_row = k / 16;
+    qs_bytes = n * qs_row;
+    total = qs_bytes + n * sc_row;
+  }
+};
+
+// The reference's run quant value for a 4-bit index (IQ4_NL's non-linear
+// codebook; Q4_0's q - 8).  The IQ4_NL values are the ggml format constant.
+__host__ __device__ inline int iq4nl_value(int i) {
+  const int8_t t[16] = {-127, -104, -83, -65, -49, -35, -22, -10,
+                        1,    13,   25,  38,  53,  69,  89,  113};
+  return t[i & 15];
+}
+
+__device__ __forceinline__ float f16_bits_to_f32(uint32_t bits) {
+  // cvt.f32.f16 is exact for every finite and infinite f16.
+  return __half2float(__ushort_as_half((unsigned short)(bits & 0xffffu)));
+}
+
+// get_scale_min_k4 (src/native/quant.rs:46-57) on the 12 packed scale bytes
+// held as three little-endian words s0 = bytes 0..3, s1 = 4..7, s2 = 8..11.
+__device__ __forceinline__ void scale_min_k4(int j, uint32_t s0, uint32_t s1, uint32_t s2,
+                                             uint32_t &sc, uint32_t &m) {
+  if (j < 4) {
+    sc = (s0 >> (8 * j)) & 63;
+    m = (s1 >> (8 * j)) & 63;
+  } else {
+    const int i = j - 4;
+    const uint32_t b8 = (s2 >> (8 * i)) & 0xff;   // q[j + 4]
+    const uint32_t bl = (s0 >> (8 * i)) & 0xff;   // q[j - 4]
+    const uint32_t bh = (s1 >> (8 * i)) & 0xff;   // q[j]
+    sc = (b8 & 0xf) | ((bl >> 6) << 4);
+    m = (b8 >> 4) | ((bh >> 6) << 4);
+  }
+}
+
+// ---- device error flag -------------------------------------------------------------
+// Kernels never trap: a bounded wait that gives up records a code here and the
+// kernel returns; the host maps it to MGB_TIMEOUT.
+enum DeviceError : int { ERR_NONE = 0, ERR_WAIT_TIMEOUT = 1, ERR_BAD_SHAPE = 2 };
+
+__device__ __forceinline__ void record_error(int *flag, int code) {
+  if (flag) atomicCAS(flag, 0, code);
+}
+
+// ---- shared-memory addresses, mbarriers and bulk copies (PTX) -----------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for phase `parity` of `bar` with an iteration bound (each try_wait
+// itself suspends for a hardware time slice).  Returns false, after recording
+// ERR_WAIT_TIMEOUT, when the bound is exceeded; the caller then returns.
+constexpr uint32_t WAIT_BOUND = 1u << 22;
+
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err) {
+  for (uint32_t i = 0; i < WAIT_BOUND; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (err && (i & 1023) == 1023 && *(volatile int *)err != 0) return false;
+  }
+  record_error(err, ERR_WAIT_TIMEOUT);
+  return false;
+}
+
+// 1-D bulk copy global -> shared, completing `bytes` on `bar`.  Both addresses
+// 16-byte aligned, bytes a multiple of 16 (no multicast).
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
+                                         uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__host__ __device__ inline uint64_t ceil_div(uint64_t a, uint64_t b) { return (a + b - 1) / b; }
+
+}  // namespace mgb

@@ -1,0 +1,546 @@
+// Prefill GEMM for packed weights on sm_100a (tcgen05 + TMEM + TMA):
+// y[m, n] = x[m, k] * W^T, W in the device layout (quant plane + scale plane),
+// bf16 operands, f32 accumulation in tensor memory.  Replaces the reference's
+// packed matmul for many activation rows (`packed_matmul`,
+// src/native/mod.rs:109-152 -> `columns_q4k_avx2`, src/native/quant.rs:673-744).
+//
+// CTA tile: BM activation rows (1 or 2 accumulators of 128 rows) x BN weight
+// rows (the MMA N, <= 256, a multiple of 16), K in steps of 64 (one 128-byte
+// swizzle atom of bf16).  Warp roles, 192 threads:
+//   warp 0   TMA producer: per K step one or two bf16 activation boxes
+//            (SWIZZLE_128B, straight into the UMMA operand layout) and the
+//            packed W quant and scale boxes (no swizzle), all on full[s].
+//            Owns the TMEM allocation.
+//   warp 1   one thread issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32) per
+//            16-wide K slice and commits each stage to empty[s].
+//   warps 2-5  dequantise the staged packed W into the bf16 B operand
+//            (K-major, SWIZZLE_128B written by hand), fence the async proxy and
+//            arrive on wready[s]; after the last stage they drain TMEM with
+//            tcgen05.ld and write y (+ the optional addend).
+// No TMA multicast anywhere: every CTA loads its own tiles from local HBM.
+// Every wait is bounded; on expiry the kernel records ERR_WAIT_TIMEOUT, skips
+// the remaining work, waits (bounded) for its own copies and MMAs, frees TMEM
+// and returns.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mgb {
+
+namespace {
+
+constexpr int KSTEP = 64;        // bf16 values per 128-byte row of a stage
+constexpr int NUM_THREADS = 192;
+constexpr int DQ_THREADS = 128;  // warps 2..5
+
+struct GemmParams {
+  int m, n, k;
+  int bn;            // weight rows per CTA (MMA N)
+  int stages;
+  int qbytes;        // packed quant bytes per weight row per K step (32 or 64)
+  uint32_t a_bytes;  // per stage
+  uint32_t b_bytes;
+  uint32_t wq_bytes;
+  uint32_t ws_bytes;
+  uint32_t stage_bytes;
+  uint32_t tx_bytes;  // bytes the TMA boxes of one stage deliver
+  int addend_mode;
+  const float *addend;
+  float *y;
+  int *err;
+};
+
+// ---- tcgen05 / TMA PTX ---------------------------------------------------------------
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_map(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+  // K-major, SWIZZLE_128B: 8-row groups 1024 bytes apart (SBO), LBO unused (1),
+  // version 1 (sm_100), layout type 2.
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ uint32_t instr_desc_bf16(int m, int n) {
+  // D f32 (bits 4-5 = 1), A bf16 (7-9 = 1), B bf16 (10-12 = 1), both K-major,
+  // N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float v[8]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---- dequantisation of one 32-value run into 64 bytes of bf16 ----------------------
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// 4-bit nibble pairs (byte i = values 2i, 2i+1) with value = s * q - mn,
+// written as 4 uint4 (8 bf16 each) into out[].
+__device__ __forceinline__ void dq_nib_linear(const uint4 &qs, float s, float mn, uint4 out[4]) {
+  // f = 0.5 + q/256  =>  s*q - mn = f * 256 s - (128 s + mn)
+  const float a = 256.f * s, c = -(128.f * s + mn);
+  const uint32_t words[4] = {qs.x, qs.y, qs.z, qs.w};
+#pragma unroll
+  for (int wd = 0; wd < 4; ++wd) {
+    const uint32_t lo = words[wd] & 0x0F0F0F0Fu, hi = (words[wd] >> 4) & 0x0F0F0F0Fu;
+    uint32_t p[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float f0 = __uint_as_float(__byte_perm(lo, 0x3F000000u, 0x7054u | ((uint32_t)i << 8)));
+      const float f1 = __uint_as_float(__byte_perm(hi, 0x3F000000u, 0x7054u | ((uint32_t)i << 8)));
+      p[i] = pack_bf16(fmaf(f0, a, c), fmaf(f1, a, c));
+    }
+    out[wd] = make_uint4(p[0], p[1], p[2], p[3]);
+  }
+}
+
+// Biased bytes (b + 128, byte order = value order) times d.
+__device__ __forceinline__ void dq_bytes(const uint32_t u[8], float d, uint4 out[4]) {
+#pragma unroll
+  for (int wd = 0; wd < 8; wd += 2) {
+    uint32_t p[4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int i = 0; i < 4; i += 2) {
+        const float f0 = __uint_as_float(__byte_perm(u[wd + h], 0x4B000000u, 0x7650u | (uint32_t)i)) - 8388736.0f;
+        const float f1 = __uint_as_float(__byte_perm(u[wd + h], 0x4B000000u, 0x7650u | (uint32_t)(i + 1))) - 8388736.0f;
+        p[2 * h + i / 2] = pack_bf16(f0 * d, f1 * d);
+      }
+    out[wd / 2] = make_uint4(p[0], p[1], p[2], p[3]);
+  }
+}
+
+__device__ __forceinline__ void iq4_lookup2(uint32_t v, const uint32_t t[4], uint32_t &o0,
+                                            uint32_t &o1) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t s = (v >> (16 * h)) & 0xFFFFu;
+    const uint32_t sel = s & 0x7777u;
+    const uint32_t low = __byte_perm(t[0], t[1], sel);
+    const uint32_t high = __byte_perm(t[2], t[3], sel);
+    const uint32_t r = __byte_perm(low, high, 0x3210u | ((s & 0x8888u) >> 1));
+    if (h == 0) o0 = r; else o1 = r;
+  }
+}
+
+template <int FMT>
+__device__ __forceinline__ void dequant_run(const uint8_t *wq_row, const uint8_t *ws_row, int kt,
+                                            int j, const uint32_t lut[4], uint4 out[4]) {
+  const int sub = (kt & 3) * 2 + j;  // run index within the 8 runs the scale box covers
+  if (FMT == Q4_K) {
+    const uint4 qs = *reinterpret_cast<const uint4 *>(wq_row + j * 16);
+    const uint4 h = *reinterpret_cast<const uint4 *>(ws_row);
+    const float d = f16_bits_to_f32(h.x), dmin = f16_bits_to_f32(h.x >> 16);
+    uint32_t sc, mn;
+    scale_min_k4(sub, h.y, h.z, h.w, sc, mn);
+    dq_nib_linear(qs, d * (float)sc, dmin * (float)mn, out);
+  } else if (FMT == Q4_0) {
+    const uint4 qs = *reinterpret_cast<const uint4 *>(wq_row + j * 16);
+    const uint32_t hb = *reinterpret_cast<const uint16_t *>(ws_row + 2 * sub);
+    const float d = f16_bits_to_f32(hb);
+    dq_nib_linear(qs, d, 8.f * d, out);
+  } else if (FMT == Q8_0) {
+    const uint4 a = *reinterpret_cast<const uint4 *>(wq_row + j * 32);
+    const uint4 b = *reinterpret_cast<const uint4 *>(wq_row + j * 32 + 16);
+    const uint32_t hb = *reinterpret_cast<const uint16_t *>(ws_row + 2 * sub);
+    const uint32_t u[8] = {a.x ^ 0x80808080u, a.y ^ 0x80808080u, a.z ^ 0x80808080u,
+                           a.w ^ 0x80808080u, b.x ^ 0x80808080u, b.y ^ 0x80808080u,
+                           b.z ^ 0x80808080u, b.w ^ 0x80808080u};
+    dq_bytes(u, f16_bits_to_f32(hb), out);
+  } else {  // IQ4_NL
+    const uint4 qs = *reinterpret_cast<const uint4 *>(wq_row + j * 16);
+    const uint32_t hb = *reinterpret_cast<const uint16_t *>(ws_row + 2 * sub);
+    uint32_t u[8];
+    const uint32_t words[4] = {qs.x, qs.y, qs.z, qs.w};
+#pragma unroll
+    for (int wd = 0; wd < 4; ++wd) iq4_lookup2(words[wd], lut, u[2 * wd], u[2 * wd + 1]);
+    dq_bytes(u, f16_bits_to_f32(hb), out);
+  }
+}
+
+// ---- the kernel ----------------------------------------------------------------------
+
+template <int FMT, int SUBS>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_wq,
+                const __grid_constant__ CUtensorMap map_ws, const GemmParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte align the operand area (SWIZZLE_128B atoms).
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int S = p.stages;
+  uint8_t *stage0 = smem;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)S * p.stage_bytes);
+  uint64_t *full = bars;              // TMA bytes landed (activation + packed W)
+  uint64_t *wready = bars + S;        // bf16 W operand written (128 arrivals)
+  uint64_t *empty = bars + 2 * S;     // MMA finished reading the stage
+  uint64_t *done = bars + 3 * S;      // all MMAs finished
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * S + 1);
+  int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * p.bn;
+  const int m0 = blockIdx.y * (128 * SUBS);
+  const int KT = p.k / KSTEP;
+  constexpr uint32_t TMEM_COLS = SUBS == 2 ? 512 : 256;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&wready[s], DQ_THREADS);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_map(&map_a);
+    prefetch_map(&map_wq);
+    prefetch_map(&map_ws);
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int issued = 0;
+      for (int kt = 0; kt < KT; ++kt) {
+        const int s = kt % S;
+        const uint32_t round = kt / S;
+        if (kt >= S && !mbar_wait(&empty[s], (round - 1) & 1, p.err)) {
+          *(volatile int *)abort_flag = 1;
+          break;
+        }
+        if (*(volatile int *)abort_flag) break;
+        uint8_t *st = stage0 + (size_t)s * p.stage_bytes;
+        mbar_arrive_expect_tx(&full[s], p.tx_bytes);
+        for (int sub = 0; sub < SUBS; ++sub)
+          tma_load_2d(st + sub * 16384, &map_a, kt * KSTEP, m0 + sub * 128, &full[s]);
+        tma_load_2d(st + p.a_bytes + p.b_bytes, &map_wq, kt * p.qbytes, n0, &full[s]);
+        tma_load_2d(st + p.a_bytes + p.b_bytes + p.wq_bytes, &map_ws, (kt / 4) * 16, n0, &full[s]);
+        issued = kt + 1;
+      }
+      // every copy this thread issued has landed before the CTA may exit
+      for (int kt = (issued > S ? issued - S : 0); kt < issued; ++kt)
+        mbar_wait(&full[kt % S], (kt / S) & 1, nullptr);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = instr_desc_bf16(128, p.bn);
+      bool ok = true;
+      int committed = 0;
+      for (int kt = 0; kt < KT && ok; ++kt) {
+        const int s = kt % S;
+        const uint32_t ph = (kt / S) & 1;
+        if (!mbar_wait(&full[s], ph, p.err) || !mbar_wait(&wready[s], ph, p.err)) {
+          ok = false;
+          *(volatile int *)abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        uint8_t *st = stage0 + (size_t)s * p.stage_bytes;
+        const uint32_t a_addr = smem_u32(st), b_addr = smem_u32(st + p.a_bytes);
+#pragma unroll
+        for (int sub = 0; sub < SUBS; ++sub)
+#pragma unroll
+          for (int kk = 0; kk < KSTEP / 16; ++kk)
+            mma_bf16(tmem_base + sub * 256, smem_desc_sw128(a_addr + sub * 16384 + kk * 32),
+                     smem_desc_sw128(b_addr + kk * 32), idesc, (kt | kk) != 0);
+        mma_commit(&empty[s]);
+        committed = kt + 1;
+      }
+      mma_commit(done);  // arrives once every MMA issued above has completed
+      (void)committed;
+    }
+  } else {
+    // ---------------- dequantise W, then the epilogue ----------------
+    const int t = threadIdx.x - 64;  // 0..127
+    uint32_t lut[4] = {0, 0, 0, 0};
+    if (FMT == IQ4_NL) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint32_t v = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) v |= (uint32_t)((iq4nl_value(4 * i + b) + 128) & 0xff) << (8 * b);
+        lut[i] = v;
+      }
+    }
+    const int items = p.bn * 2;  // (weight row, run) pairs per stage
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % S;
+      const uint32_t ph = (kt / S) & 1;
+      if (*(volatile int *)abort_flag) break;
+      // this stage's B slot is free once the MMA of round (kt / S) - 1 released it
+      if ((kt >= S && !mbar_wait(&empty[s], ((kt / S) - 1) & 1, p.err)) ||
+          !mbar_wait(&full[s], ph, p.err)) {
+        *(volatile int *)abort_flag = 1;
+        break;
+      }
+      uint8_t *st = stage0 + (size_t)s * p.stage_bytes;
+      uint8_t *bt = st + p.a_bytes;
+      const uint8_t *wq = st + p.a_bytes + p.b_bytes;
+      const uint8_t *ws = wq + p.wq_bytes;
+      for (int it = t; it < items; it += DQ_THREADS) {
+        const int row = it >> 1, j = it & 1;
+        uint4 out[4];
+        dequant_run<FMT>(wq + row * p.qbytes, ws + row * 16, kt, j, lut, out);
+        uint8_t *dst_row = bt + row * 128;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int chunk = j * 4 + c;
+          *reinterpret_cast<uint4 *>(dst_row + ((chunk ^ (row & 7)) << 4)) = out[c];
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&wready[s]);
+    }
+    // epilogue: TMEM lanes of this warp's quarter -> y rows
+    const bool finished = mbar_wait(done, 0, p.err);
+    tc_fence_after();
+    // tcgen05.ld is warp-collective: the whole warp drains TMEM or none of it
+    if (__all_sync(0xffffffffu, finished && !*(volatile int *)abort_flag)) {
+      const int quarter = warp & 3;
+      for (int sub = 0; sub < SUBS; ++sub) {
+        const int row = m0 + sub * 128 + quarter * 32 + lane;
+        for (int c = 0; c < p.bn; c += 8) {
+          float v[8];
+          tmem_ld8(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * 256 + c), v);
+          if (row < p.m) {
+            const int col = n0 + c;
+            float *yr = p.y + (size_t)row * p.n;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              if (col + e < p.n) {
+                float o = v[e];
+                if (p.addend_mode == 1) o = o + p.addend[col + e];
+                else if (p.addend_mode == 2) o = o + p.addend[(size_t)row * p.n + col + e];
+                yr[col + e] = o;
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ---- host side ---------------------------------------------------------------------------
+
+__global__ void f32_to_bf16_kernel(const float *__restrict__ x, __nv_bfloat16 *__restrict__ out,
+                                   uint64_t n) {
+  const uint64_t n4 = n / 4;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n4;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4 *>(x)[i];
+    uint2 o;
+    o.x = pack_bf16(v.x, v.y);
+    o.y = pack_bf16(v.z, v.w);
+    reinterpret_cast<uint2 *>(out)[i] = o;
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void *p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+bool make_map_2d(CUtensorMap *map, CUtensorMapDataType dtype, int elem_bytes, const void *base,
+                 uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                 uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  (void)elem_bytes;
+  return fn(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct TileChoice {
+  int subs, bn, stages;
+};
+
+TileChoice choose_tiles(uint64_t m, uint64_t n, int sms) {
+  TileChoice t;
+  t.subs = m > 128 ? 2 : 1;
+  const uint64_t mt = ceil_div(m, 128 * (uint64_t)t.subs);
+  uint64_t bn = ceil_div(n * mt, (uint64_t)sms);
+  bn = ceil_div(bn, 16) * 16;
+  if (bn < 32) bn = 32;
+  if (bn > 256) bn = 256;
+  t.bn = (int)bn;
+  t.stages = 0;
+  return t;
+}
+
+}  // namespace
+
+uint64_t gemm_workspace_bytes(int, uint64_t m, uint64_t, uint64_t k) {
+  return ceil_div(m * k * 2, 256) * 256;
+}
+
+bool gemm_supported(int fmt, uint64_t m, uint64_t n, uint64_t k) {
+  return supported(fmt) && m >= 1 && n >= 1 && k % 256 == 0 && k >= 256 && m < (1u << 30) &&
+         n < (1u << 30) && k < (1u << 24);
+}
+
+cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const float *x, uint64_t m,
+                        float *y, const float *addend, int addend_mode, void *workspace,
+                        uint64_t workspace_bytes, int *err, int sms, cudaStream_t stream) {
+  if (!gemm_supported(fmt, m, n, k) || workspace_bytes < gemm_workspace_bytes(fmt, m, n, k) ||
+      (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 15))
+    return cudaErrorInvalidValue;
+  __nv_bfloat16 *xb = static_cast<__nv_bfloat16 *>(workspace);
+  {
+    const uint64_t n4 = m * k / 4;
+    uint64_t blocks = ceil_div(n4, 256);
+    if (blocks > (uint64_t)sms * 16) blocks = (uint64_t)sms * 16;
+    f32_to_bf16_kernel<<<(unsigned)blocks, 256, 0, stream>>>(x, xb, m * k);
+  }
+  const Layout L(fmt, n, k);
+  TileChoice t = choose_tiles(m, n, sms);
+  GemmParams p;
+  p.m = (int)m;
+  p.n = (int)n;
+  p.k = (int)k;
+  p.bn = t.bn;
+  p.qbytes = fmt == Q8_0 ? 64 : 32;
+  p.a_bytes = 16384u * t.subs;
+  p.b_bytes = (uint32_t)t.bn * 128u;
+  p.wq_bytes = (uint32_t)ceil_div((uint64_t)t.bn * p.qbytes, 1024) * 1024;
+  p.ws_bytes = (uint32_t)ceil_div((uint64_t)t.bn * 16, 1024) * 1024;
+  p.stage_bytes = p.a_bytes + (uint32_t)ceil_div(p.b_bytes, 1024) * 1024 + p.wq_bytes + p.ws_bytes;
+  // b_bytes region rounded to 1024 so the packed boxes stay 1024-aligned
+  p.b_bytes = (uint32_t)ceil_div(p.b_bytes, 1024) * 1024;
+  p.tx_bytes = p.a_bytes + (uint32_t)t.bn * (uint32_t)p.qbytes + (uint32_t)t.bn * 16u;
+  const uint32_t budget = 220 * 1024;
+  int stages = (int)((budget - 1024 - 256) / p.stage_bytes);
+  if (stages > 6) stages = 6;
+  if (stages < 2) return cudaErrorInvalidValue;
+  p.stages = stages;
+  p.addend_mode = addend_mode;
+  p.addend = addend;
+  p.y = y;
+  p.err = err;
+
+  CUtensorMap map_a, map_wq, map_ws;
+  if (!make_map_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xb, k, m, k * 2, KSTEP, 128,
+                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map_2d(&map_wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, L.qs_row, n, L.qs_row,
+                   (uint32_t)p.qbytes, (uint32_t)t.bn, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !make_map_2d(&map_ws, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1,
+                   static_cast<const uint8_t *>(w) + L.qs_bytes, L.sc_row, n, L.sc_row, 16,
+                   (uint32_t)t.bn, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+
+  const size_t smem = (size_t)stages * p.stage_bytes + 1024 /*align slack*/ + 256 /*barriers*/;
+  dim3 grid((unsigned)ceil_div(n, (uint64_t)t.bn), (unsigned)ceil_div(m, 128ull * t.subs));
+  cudaError_t e = cudaSuccess;
+#define MGB_GEMM_LAUNCH(F, SUBS)                                                               \
+  do {                                                                                         \
+    auto kern = gemm_kernel<F, SUBS>;                                                          \
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \
+    if (e != cudaSuccess) return e;                                                            \
+    kern<<<grid, NUM_THREADS, smem, stream>>>(map_a, map_wq, map_ws, p);                       \
+  } while (0)
+#define MGB_GEMM_FMT(F)                          \
+  case F:                                        \
+    if (t.subs == 2) MGB_GEMM_LAUNCH(F, 2);      \
+    else MGB_GEMM_LAUNCH(F, 1);                  \
+    break;
+  switch (fmt) {
+    MGB_GEMM_FMT(Q4_K)
+    MGB_GEMM_FMT(Q8_0)
+    MGB_GEMM_FMT(IQ4_NL)
+    MGB_GEMM_FMT(Q4_0)
+    default:
+      return cudaErrorInvalidValue;
+  }
+#undef MGB_GEMM_FMT
+#undef MGB_GEMM_LAUNCH
+  return cudaGetLastError();
+}
+
+}  // namespace mgb

@@ -1,0 +1,171 @@
+// Device layout of packed matrices: ggml blocks -> (quant plane, scale plane),
+// and the bit-exact dequantisation of that layout back to f32.
+//
+// Dequantised values equal the reference `decode` + `dequantize_row`
+// (src/native/quant.rs:100-195, :1700-1711) bit for bit: every product and
+// difference is rounded on its own (__fmul_rn / __fsub_rn, never an FMA), as
+// Rust evaluates `scale * q - min` with `scale = d * sc`, `min = dmin * m`.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mgb {
+
+// One thread per 32-value run: gathers the run's quants from its ggml block and
+// writes them as 16 (or 32) bytes holding values (2i, 2i+1) in byte i.
+__global__ void repack_kernel(int fmt, const uint8_t *__restrict__ src, uint64_t n, uint64_t k,
+                              uint8_t *__restrict__ dst) {
+  const uint64_t runs_per_row = k / RUN;
+  const uint64_t total = n * runs_per_row;
+  const Layout L(fmt, n, k);
+  for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < total;
+       t += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t row = t / runs_per_row, u = t % runs_per_row;
+    const uint64_t row_bytes = k / block_elements(fmt) * block_bytes(fmt);
+    const uint8_t *row_src = src + row * row_bytes;
+    uint8_t *qs = dst + row * L.qs_row;
+    uint8_t *sc = dst + L.qs_bytes + row * L.sc_row;
+    if (fmt == Q4_K) {
+      const uint64_t b = u / 8;
+      const int j = (int)(u % 8);
+      const uint8_t *blk = row_src + b * 144;
+      const uint8_t *chunk = blk + 16 + 32 * (j / 2);
+      const int shift = 4 * (j % 2);
+      uint32_t words[4];
+      for (int w = 0; w < 4; ++w) {
+        uint32_t v = 0;
+        for (int i = 0; i < 4; ++i) {
+          const int e = 2 * (4 * w + i);
+          const uint32_t lo = (chunk[e] >> shift) & 0xF, hi = (chunk[e + 1] >> shift) & 0xF;
+          v |= (lo | (hi << 4)) << (8 * i);
+        }
+        words[w] = v;
+      }
+      *reinterpret_cast<uint4 *>(qs + u * 16) = make_uint4(words[0], words[1], words[2], words[3]);
+      if (j == 0)
+        for (int i = 0; i < 16; ++i) sc[b * 16 + i] = blk[i];
+    } else if (fmt == Q8_0) {
+      const uint8_t *blk = row_src + u * 34;
+      for (int i = 0; i < 32; ++i) qs[u * 32 + i] = blk[2 + i];
+      sc[u * 2] = blk[0];
+      sc[u * 2 + 1] = blk[1];
+    } else {  // IQ4_NL, Q4_0: ggml byte l holds indices l (low) and l + 16 (high)
+      const uint8_t *blk = row_src + u * 18;
+      for (int i = 0; i < 16; ++i) {
+        const int e0 = 2 * i, e1 = 2 * i + 1;
+        const uint32_t v0 = e0 < 16 ? (blk[2 + e0] & 0xF) : (blk[2 + e0 - 16] >> 4);
+        const uint32_t v1 = e1 < 16 ? (blk[2 + e1] & 0xF) : (blk[2 + e1 - 16] >> 4);
+        qs[u * 16 + i] = (uint8_t)(v0 | (v1 << 4));
+      }
+      sc[u * 2] = blk[0];
+      sc[u * 2 + 1] = blk[1];
+    }
+  }
+}
+
+// The 32 quant values of run `u` of `row` (as ints) and the run's scale and min.
+__device__ __forceinline__ void decode_run(int fmt, const uint8_t *__restrict__ w, const Layout &L,
+                                           uint64_t row, uint64_t u, int q[32], float &scale,
+                                           float &min) {
+  const uint8_t *sc = w + L.qs_bytes + row * L.sc_row;
+  if (fmt == Q8_0) {
+    const uint4 a = *reinterpret_cast<const uint4 *>(w + row * L.qs_row + u * 32);
+    const uint4 b = *reinterpret_cast<const uint4 *>(w + row * L.qs_row + u * 32 + 16);
+    const uint32_t words[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    for (int i = 0; i < 32; ++i) q[i] = (int)(int8_t)((words[i / 4] >> (8 * (i % 4))) & 0xff);
+    scale = f16_bits_to_f32(sc[u * 2] | (sc[u * 2 + 1] << 8));
+    min = 0.0f;
+    return;
+  }
+  const uint4 v = *reinterpret_cast<const uint4 *>(w + row * L.qs_row + u * 16);
+  const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+  for (int i = 0; i < 32; ++i) {
+    const uint32_t nib = (words[i / 8] >> (4 * (i % 8))) & 0xF;
+    q[i] = fmt == Q4_K ? (int)nib : (fmt == Q4_0 ? (int)nib - 8 : iq4nl_value((int)nib));
+  }
+  if (fmt == Q4_K) {
+    const uint4 h = *reinterpret_cast<const uint4 *>(sc + (u / 8) * 16);
+    const float d = f16_bits_to_f32(h.x), dmin = f16_bits_to_f32(h.x >> 16);
+    uint32_t s, m;
+    scale_min_k4((int)(u % 8), h.y, h.z, h.w, s, m);
+    scale = __fmul_rn(d, (float)s);
+    min = __fmul_rn(dmin, (float)m);
+  } else {
+    scale = f16_bits_to_f32(sc[u * 2] | (sc[u * 2 + 1] << 8));
+    min = 0.0f;
+  }
+}
+
+__global__ void dequantize_kernel(int fmt, const uint8_t *__restrict__ w, uint64_t n, uint64_t k,
+                                  float *__restrict__ out) {
+  const Layout L(fmt, n, k);
+  const uint64_t runs_per_row = k / RUN, total = n * runs_per_row;
+  for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < total;
+       t += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t row = t / runs_per_row, u = t % runs_per_row;
+    int q[32];
+    float scale, min;
+    decode_run(fmt, w, L, row, u, q, scale, min);
+    float4 *o = reinterpret_cast<float4 *>(out + row * k + u * RUN);
+    for (int i = 0; i < 8; ++i) {
+      float v[4];
+      for (int e = 0; e < 4; ++e) v[e] = __fsub_rn(__fmul_rn(scale, (float)q[4 * i + e]), min);
+      o[i] = make_float4(v[0], v[1], v[2], v[3]);
+    }
+  }
+}
+
+// Input-major product (`axpy_columns`, src/native/quant.rs:1658-1689): W's
+// stored rows are the k input rows, y[m, n_cols].  One thread per (output row
+// r, output column c); sums x[r, j] * value(j, c) over j in order, skipping
+// x == 0 like the reference.
+__global__ void input_major_kernel(int fmt, const uint8_t *__restrict__ w, uint64_t k_rows,
+                                   uint64_t n_cols, const float *__restrict__ x, uint64_t m,
+                                   float *__restrict__ y) {
+  const Layout L(fmt, k_rows, n_cols);
+  const uint64_t total = m * n_cols;
+  for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < total;
+       t += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t r = t / n_cols, c = t % n_cols;
+    const uint64_t u = c / RUN;
+    const int i = (int)(c % RUN);
+    float acc = 0.0f;
+    for (uint64_t j = 0; j < k_rows; ++j) {
+      const float a = x[r * k_rows + j];
+      if (a == 0.0f) continue;
+      int q[32];
+      float scale, min;
+      decode_run(fmt, w, L, j, u, q, scale, min);
+      const float v = __fsub_rn(__fmul_rn(scale, (float)q[i]), min);
+      acc = __fadd_rn(acc, __fmul_rn(a, v));
+    }
+    y[t] = acc;
+  }
+}
+
+static int grid_for(uint64_t work, int threads) {
+  uint64_t blocks = ceil_div(work, threads);
+  return (int)(blocks > 65535 * 4 ? 65535 * 4 : (blocks ? blocks : 1));
+}
+
+cudaError_t launch_repack(int fmt, const void *src, uint64_t n, uint64_t k, void *dst,
+                          cudaStream_t stream) {
+  repack_kernel<<<grid_for(n * (k / RUN), 256), 256, 0, stream>>>(
+      fmt, static_cast<const uint8_t *>(src), n, k, static_cast<uint8_t *>(dst));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dequantize(int fmt, const void *w, uint64_t n, uint64_t k, float *out,
+                              cudaStream_t stream) {
+  dequantize_kernel<<<grid_for(n * (k / RUN), 256), 256, 0, stream>>>(
+      fmt, static_cast<const uint8_t *>(w), n, k, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_input_major(int fmt, const void *w, uint64_t k_rows, uint64_t n_cols,
+                               const float *x, uint64_t m, float *y, cudaStream_t stream) {
+  input_major_kernel<<<grid_for(m * n_cols, 256), 256, 0, stream>>>(
+      fmt, static_cast<const uint8_t *>(w), k_rows, n_cols, x, m, y);
+  return cudaGetLastError();
+}
+
+}  // namespace mgb

@@ -1,0 +1,82 @@
+"""The C-ABI library on the CPU-only container: it loads, exports every
+function include/magnetar_b200.h declares, answers the identity queries and
+fails cleanly (no crash, a status and a reason) where a GPU is needed."""
+
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+
+import magnetar_b200 as mgb
+
+
+def test_library_exports_every_header_function():
+    lib = mgb.lib()
+    declared = mgb.header_functions()
+    assert len(declared) >= 35, declared
+    missing = [f for f in declared if not hasattr(lib, f)]
+    assert not missing, missing
+    # and the Python mirror binds exactly what the header declares
+    assert sorted(mgb._SIGNATURES) == declared
+
+
+def test_identity_and_advertisements():
+    assert mgb.lib().mgb_abi_version() == 1
+    md = mgb.metadata()
+    assert md["name"] == "magnetar:provider/b200-native"
+    assert md["name"] != "magnetar:provider/reference-cpu"
+    ads = mgb.kernel_advertisements()
+    assert [a["name"] for a in ads] == ["matmul", "matmul-bias", "matmul-residual"]
+    assert all(a["rank"] == 2 and a["cancellation"] == 1 for a in ads)
+
+
+def test_status_names_and_packed_sizes():
+    assert mgb.status_name(mgb.DECLINED) == "declined"
+    assert mgb.status_name(mgb.TIMEOUT) == "kernel-timeout"
+    # device layout bytes equal the ggml block bytes
+    assert mgb.packed_bytes(mgb.Q4_K, 4096, 4096) == 9_437_184
+    assert mgb.packed_bytes(mgb.Q8_0, 14336, 4096) == 62_390_272
+    assert mgb.packed_bytes(mgb.IQ4_NL, 14336, 4096) == 33_030_144
+    assert mgb.packed_bytes(mgb.Q6_K, 1, 256) == 0  # declined format
+    assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 1, 4096, 4096) == 0
+    assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 512, 14336, 4096) == 512 * 4096 * 2
+
+
+def test_settings_from_env(monkeypatch):
+    monkeypatch.setenv("MAGNETAR_B200_PACKED_WEIGHTS", "0")
+    monkeypatch.setenv("MAGNETAR_B200_INT8_ACTIVATIONS", "1")
+    monkeypatch.setenv("MAGNETAR_B200_KERNEL", "gemm")
+    monkeypatch.setenv("MAGNETAR_B200_DEVICE", "3")
+    s = mgb.settings_from_env()
+    assert (s.packed_weights, s.int8_activations, s.kernel, s.device) == (0, 1, mgb.KERNEL_GEMM, 3)
+    monkeypatch.delenv("MAGNETAR_B200_PACKED_WEIGHTS")
+    monkeypatch.delenv("MAGNETAR_B200_INT8_ACTIVATIONS")
+    monkeypatch.delenv("MAGNETAR_B200_KERNEL")
+    s = mgb.settings_from_env()
+    assert (s.packed_weights, s.int8_activations, s.kernel) == (1, 0, mgb.KERNEL_AUTO)
+
+
+def test_provider_create_fails_cleanly_without_gpu():
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    with pytest.raises(mgb.MgbError) as info:
+        mgb.B200Provider()
+    assert info.value.status == mgb.CUDA_ERROR
+    assert "CUDA device" in str(info.value)
+
+
+def test_null_arguments_are_rejected_without_device_work():
+    lib = mgb.lib()
+    assert lib.mgb_provider_create(None, None) == mgb.INVALID_ARGUMENT
+    assert lib.mgb_take_device_error(0, None) == mgb.INVALID_ARGUMENT
+    assert lib.mgb_kernel_advertisement_get(99, ctypes.byref(mgb.Advertisement())) == \
+        mgb.INVALID_ARGUMENT
+    # a format the Provider does not execute, or a ragged shape, is refused up front
+    assert lib.mgb_qmatmul(mgb.Q6_K, None, 1, 256, None, 1, None, None, 0, None, 0, None) == \
+        mgb.UNSUPPORTED
+    assert lib.mgb_qmatmul(mgb.Q4_K, None, 1, 96, None, 1, None, None, 0, None, 0, None) == \
+        mgb.EXECUTION_FAILED
+    assert "activations have 96 columns" in mgb.last_error()

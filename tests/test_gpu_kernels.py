@@ -1,0 +1,200 @@
+"""GPU parity of the B200 kernels against the CPU oracle, through the C ABI.
+
+Tolerances, normalised as the reference does
+(src/native/tests.rs:91-103: |a - e| <= tol * max(1, max|e|)):
+  dequantisation          bit-exact
+  GEMV (f32, m <= 2)      1e-3
+  tensor-core GEMM (bf16) 5e-3
+"""
+
+from __future__ import annotations
+
+import pathlib
+
+import numpy as np
+import pytest
+
+import magnetar_b200 as mgb
+import synthetic
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = pathlib.Path(__file__).resolve().parent / "golden" / "dequant_gguf.npz"
+FORMATS = [mgb.Q4_K, mgb.Q8_0, mgb.IQ4_NL, mgb.Q4_0]
+GEMV_TOL, GEMM_TOL = 1e-3, 5e-3
+
+
+@pytest.fixture(scope="module")
+def torch_cuda(cuda_device):
+    import torch
+
+    torch.cuda.set_device(cuda_device)
+    return torch
+
+
+def _device_layout(torch, fmt, ggml: np.ndarray, rows: int, cols: int):
+    src = torch.from_numpy(np.ascontiguousarray(ggml)).cuda()
+    out = torch.empty(mgb.packed_bytes(fmt, rows, cols), dtype=torch.uint8, device="cuda")
+    mgb.repack(fmt, src.data_ptr(), rows, cols, out.data_ptr(),
+               torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    return out
+
+
+def _qmatmul(torch, fmt, wdev, n, k, x: np.ndarray, addend: np.ndarray | None = None):
+    m = x.shape[0]
+    xd = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).cuda()
+    yd = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    ws_bytes = mgb.qmatmul_workspace_bytes(fmt, m, n, k)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+    ad = None
+    if addend is not None:
+        ad = torch.from_numpy(np.ascontiguousarray(addend, dtype=np.float32)).cuda()
+    mgb.qmatmul(fmt, wdev.data_ptr(), n, k, xd.data_ptr(), m, yd.data_ptr(),
+                ad.data_ptr() if ad is not None else 0, ad.numel() if ad is not None else 0,
+                ws.data_ptr(), ws_bytes, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert mgb.take_device_error(torch.cuda.current_device()) == 0
+    return yd.cpu().numpy()
+
+
+def _same_bits(a, b):
+    nan = np.isnan(a)
+    assert np.array_equal(nan, np.isnan(b))
+    return np.array_equal(a[~nan].view(np.uint32), b[~nan].view(np.uint32))
+
+
+@pytest.mark.parametrize("name", ["q4_k", "q8_0", "iq4_nl", "q4_0"])
+@pytest.mark.parametrize("source", ["reference_generator", "random_bytes"])
+def test_dequantize_bit_exact_to_gguf_and_oracle(torch_cuda, oracle, name, source):
+    torch = torch_cuda
+    golden = np.load(GOLDEN)
+    key = f"{name}__{source}"
+    fmt, rows, cols = (int(v) for v in golden[key + "__meta"])
+    data = golden[key + "__bytes"]
+    wdev = _device_layout(torch, fmt, data, rows, cols)
+    out = torch.empty((rows, cols), dtype=torch.float32, device="cuda")
+    mgb.dequantize(fmt, wdev.data_ptr(), rows, cols, out.data_ptr())
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    assert _same_bits(got, golden[key + "__expected"])
+    assert _same_bits(got, oracle.dequantize(fmt, data, rows, cols))
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+def test_dequantize_full_size_bit_exact(torch_cuda, oracle, fmt):
+    torch = torch_cuda
+    n, k = 4096, 4096
+    w = synthetic.packed_weights(fmt, n, k, seed=3)
+    wdev = _device_layout(torch, fmt, w, n, k)
+    out = torch.empty((n, k), dtype=torch.float32, device="cuda")
+    mgb.dequantize(fmt, wdev.data_ptr(), n, k, out.data_ptr())
+    torch.cuda.synchronize()
+    assert _same_bits(out.cpu().numpy(), oracle.dequantize(fmt, w, n, k))
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("n,k", [(37, 512), (5, 96), (300, 8192), (64, 14336)])
+def test_gemv_parity(torch_cuda, oracle, fmt, m, n, k):
+    if fmt == mgb.Q4_K and k % 256:
+        pytest.skip("Q4_K needs whole 256-value super-blocks")
+    torch = torch_cuda
+    w = oracle.test_packed(fmt, n, k, 21)  # the reference's own test generator
+    x = oracle.test_activations(m, k, m)
+    wdev = _device_layout(torch, fmt, w, n, k)
+    y = _qmatmul(torch, fmt, wdev, n, k, x)
+    ref = oracle.packed_matmul(fmt, w, n, k, x)
+    err = oracle.assert_close(y, ref, GEMV_TOL, f"gemv fmt {fmt} m {m} n {n} k {k}")
+    assert err < 1e-5  # f32 accumulation: far inside the tolerance
+
+
+@pytest.mark.parametrize("fmt", [mgb.Q4_K])
+def test_gemv_config0_q4k_4096(torch_cuda, oracle, fmt):
+    torch = torch_cuda
+    n = k = 4096
+    w = synthetic.packed_weights(fmt, n, k)
+    x = synthetic.activations(1, k)
+    wdev = _device_layout(torch, fmt, w, n, k)
+    y = _qmatmul(torch, fmt, wdev, n, k, x)
+    y2 = _qmatmul(torch, fmt, wdev, n, k, x)
+    assert np.array_equal(y, y2), "GEMV is deterministic"
+    oracle.assert_close(y, oracle.packed_matmul(fmt, w, n, k, x), GEMV_TOL, "config 0")
+
+
+@pytest.mark.parametrize("fmt", [mgb.Q8_0, mgb.IQ4_NL])
+@pytest.mark.parametrize("m", [1, 8])
+def test_config2_mixed_formats(torch_cuda, oracle, fmt, m):
+    torch = torch_cuda
+    n, k = 14336, 4096
+    w = synthetic.packed_weights(fmt, n, k)
+    x = synthetic.activations(m, k)
+    wdev = _device_layout(torch, fmt, w, n, k)
+    y = _qmatmul(torch, fmt, wdev, n, k, x)
+    tol = GEMV_TOL if m <= 2 else GEMM_TOL
+    oracle.assert_close(y, oracle.packed_matmul(fmt, w, n, k, x), tol, f"config 2 fmt {fmt} m {m}")
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("m", [3, 9, 64, 130, 300])
+def test_gemm_parity(torch_cuda, oracle, fmt, m):
+    torch = torch_cuda
+    n, k = 300, 512
+    w = oracle.test_packed(fmt, n, k, 31)
+    x = oracle.test_activations(m, k, m)
+    wdev = _device_layout(torch, fmt, w, n, k)
+    y = _qmatmul(torch, fmt, wdev, n, k, x)
+    oracle.assert_close(y, oracle.packed_matmul(fmt, w, n, k, x), GEMM_TOL, f"gemm fmt {fmt} m {m}")
+
+
+def test_gemm_config1_sampled_columns(torch_cuda, oracle):
+    """Config 1 (X[512,4096] x Q4_K W[14336 x 4096]) at full size on the GPU;
+    the oracle checks 320 output columns spread over every column tile,
+    including the last, against all 512 rows."""
+    torch = torch_cuda
+    fmt, m, n, k = mgb.Q4_K, 512, 14336, 4096
+    w = synthetic.packed_weights(fmt, n, k)
+    x = synthetic.activations(m, k)
+    wdev = _device_layout(torch, fmt, w, n, k)
+    y = _qmatmul(torch, fmt, wdev, n, k, x)
+    assert np.isfinite(y).all()
+    cols = np.unique(np.concatenate([np.linspace(0, n - 1, 300).astype(np.int64),
+                                     np.arange(n - 20, n)]))
+    sub = synthetic.row_slice(fmt, w, k, cols)
+    ref = oracle.packed_matmul(fmt, sub, len(cols), k, x)
+    err = oracle.assert_close(y[:, cols], ref, GEMM_TOL, "config 1")
+    assert err > 0  # bf16 operands do round
+    y2 = _qmatmul(torch, fmt, wdev, n, k, x)
+    assert np.array_equal(y, y2), "GEMM is deterministic (no split-K atomics)"
+
+
+@pytest.mark.parametrize("m", [1, 2, 64])
+def test_addend_epilogues(torch_cuda, oracle, m):
+    torch = torch_cuda
+    fmt, n, k = mgb.Q4_K, 96, 512
+    w = oracle.test_packed(fmt, n, k, 5)
+    x = oracle.test_activations(m, k, 9)
+    wdev = _device_layout(torch, fmt, w, n, k)
+    tol = GEMV_TOL if m <= 2 else GEMM_TOL
+    base = oracle.packed_matmul(fmt, w, n, k, x)
+    bias = np.linspace(-3, 3, n, dtype=np.float32)
+    oracle.assert_close(_qmatmul(torch, fmt, wdev, n, k, x, bias), oracle.add(base, bias), tol)
+    resid = oracle.test_activations(m, n, 11)
+    oracle.assert_close(_qmatmul(torch, fmt, wdev, n, k, x, resid), oracle.add(resid, base), tol)
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+def test_input_major_parity(torch_cuda, oracle, fmt):
+    torch = torch_cuda
+    rows, cols = 64, 256  # stored rows = input rows
+    w = oracle.test_packed(fmt, rows, cols, 61)
+    wdev = _device_layout(torch, fmt, w, rows, cols)
+    for m in (1, 4):
+        x = oracle.test_activations(m, rows, 62)
+        x[0, 3] = 0.0  # the reference skips zero activations
+        xd = torch.from_numpy(x).cuda()
+        yd = torch.empty((m, cols), dtype=torch.float32, device="cuda")
+        mgb.qmatmul_input_major(fmt, wdev.data_ptr(), rows, cols, xd.data_ptr(), m, yd.data_ptr())
+        torch.cuda.synchronize()
+        ref = oracle.packed_axpy(fmt, w, rows, cols, x)
+        assert np.array_equal(yd.cpu().numpy(), ref)  # same order, same roundings
