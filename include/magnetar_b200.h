@@ -265,6 +265,13 @@ uint64_t mgb_qmatmul_workspace_bytes(int32_t format, uint64_t m, uint64_t n, uin
 mgb_status mgb_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, const float *x,
                        uint64_t m, float *y, const float *addend, uint64_t addend_len,
                        void *workspace, uint64_t workspace_bytes, void *stream);
+/* The tensor-core GEMM alone for activations already in bf16: y[m, n] =
+ * xb[m, k] (bf16, 16-byte aligned) * W^T, f32 accumulation, no scratch.
+ * Needs k % 256 == 0.  For callers whose producer emits bf16 (no counterpart
+ * in the reference, which only takes f32 activations). */
+mgb_status mgb_qmatmul_bf16(int32_t format, const void *w, uint64_t n, uint64_t k,
+                            const void *xb, uint64_t m, float *y, const float *addend,
+                            uint64_t addend_len, void *stream);
 /* Stored-order f32 values of a packed matrix (device layout), bit-exact to the reference
  * `dequantize_row` (src/native/quant.rs:1700-1711) on every stored row. */
 mgb_status mgb_dequantize(int32_t format, const void *w, uint64_t stored_rows,

@@ -193,6 +193,32 @@ mgb_status mgb_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, co
                      device_error_flag(dev), MGB_KERNEL_AUTO, static_cast<cudaStream_t>(stream));
 }
 
+mgb_status mgb_qmatmul_bf16(int32_t format, const void *w, uint64_t n, uint64_t k, const void *xb,
+                            uint64_t m, float *y, const float *addend, uint64_t addend_len,
+                            void *stream) {
+  if (!format_supported(format))
+    return fail(MGB_UNSUPPORTED, "packed format %d is not executed by this Provider", format);
+  if (!gemm_supported(format, m, n, k))
+    return fail(MGB_UNSUPPORTED, "tensor-core GEMM needs k %% 256 == 0 (got %llu)",
+                (unsigned long long)k);
+  if (!w || !xb || !y) return fail(MGB_INVALID_ARGUMENT, "null device pointer");
+  if ((reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(xb) & 15))
+    return fail(MGB_INVALID_ARGUMENT, "weight and activation pointers must be 16-byte aligned");
+  int mode = 0;
+  if (addend) {
+    if (addend_len == n) mode = 1;
+    else if (addend_len == m * n) mode = 2;
+    else return fail(MGB_INVALID_ARGUMENT, "addend has %llu values, expected %llu or %llu",
+                     (unsigned long long)addend_len, (unsigned long long)n,
+                     (unsigned long long)(m * n));
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t e = launch_gemm_bf16(format, w, n, k, xb, m, y, addend, mode, device_error_flag(dev),
+                                   device_sms(dev), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MGB_OK : cuda_fail(e, "GEMM launch");
+}
+
 mgb_status mgb_dequantize(int32_t format, const void *w, uint64_t stored_rows, uint64_t stored_cols,
                           float *out, void *stream) {
   mgb_status s = check_packed_shape(format, stored_rows, stored_cols);

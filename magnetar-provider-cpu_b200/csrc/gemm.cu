@@ -479,6 +479,15 @@ cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const fl
     if (blocks > (uint64_t)sms * 16) blocks = (uint64_t)sms * 16;
     f32_to_bf16_kernel<<<(unsigned)blocks, 256, 0, stream>>>(x, xb, m * k);
   }
+  return launch_gemm_bf16(fmt, w, n, k, xb, m, y, addend, addend_mode, err, sms, stream);
+}
+
+cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, const void *xb,
+                             uint64_t m, float *y, const float *addend, int addend_mode, int *err,
+                             int sms, cudaStream_t stream) {
+  if (!gemm_supported(fmt, m, n, k) || (reinterpret_cast<uintptr_t>(w) & 15) ||
+      (reinterpret_cast<uintptr_t>(xb) & 15))
+    return cudaErrorInvalidValue;
   const Layout L(fmt, n, k);
   TileChoice t = choose_tiles(m, n, sms);
   GemmParams p;

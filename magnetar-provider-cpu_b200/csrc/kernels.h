@@ -27,6 +27,11 @@ cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const fl
                         void *workspace, uint64_t workspace_bytes, int *err, int sms,
                         cudaStream_t stream);
 
+// the GEMM alone on bf16 activations xb[m, k] (no conversion pass)
+cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, const void *xb,
+                             uint64_t m, float *y, const float *addend, int addend_mode, int *err,
+                             int sms, cudaStream_t stream);
+
 // dense.cu
 cudaError_t launch_matmul_f32(const float *a, uint64_t a_rows, uint64_t a_cols, const float *b,
                               uint64_t b_rows, uint64_t b_cols, int transpose_a, int transpose_b,

@@ -118,6 +118,7 @@ _SIGNATURES = {
     "mgb_repack": ([_i32, _vp, _u64, _u64, _vp, _vp], _i32),
     "mgb_qmatmul_workspace_bytes": ([_i32, _u64, _u64, _u64], _u64),
     "mgb_qmatmul": ([_i32, _vp, _u64, _u64, _vp, _u64, _vp, _vp, _u64, _vp, _u64, _vp], _i32),
+    "mgb_qmatmul_bf16": ([_i32, _vp, _u64, _u64, _vp, _u64, _vp, _vp, _u64, _vp], _i32),
     "mgb_dequantize": ([_i32, _vp, _u64, _u64, _vp, _vp], _i32),
     "mgb_qmatmul_input_major": ([_i32, _vp, _u64, _u64, _vp, _u64, _vp, _vp], _i32),
     "mgb_matmul_f32": ([_vp, _u64, _u64, _vp, _u64, _u64, _i32, _i32, _vp, _vp], _i32),
@@ -183,6 +184,12 @@ def qmatmul(fmt: int, w_ptr: int, n: int, k: int, x_ptr: int, m: int, y_ptr: int
             workspace_bytes: int = 0, stream: int = 0) -> None:
     check(lib().mgb_qmatmul(fmt, w_ptr, n, k, x_ptr, m, y_ptr, addend_ptr or None, addend_len,
                             workspace_ptr or None, workspace_bytes, stream or None))
+
+
+def qmatmul_bf16(fmt: int, w_ptr: int, n: int, k: int, xb_ptr: int, m: int, y_ptr: int,
+                 addend_ptr: int = 0, addend_len: int = 0, stream: int = 0) -> None:
+    check(lib().mgb_qmatmul_bf16(fmt, w_ptr, n, k, xb_ptr, m, y_ptr, addend_ptr or None,
+                                 addend_len, stream or None))
 
 
 def dequantize(fmt: int, w_ptr: int, rows: int, cols: int, out_ptr: int, stream: int = 0) -> None:
