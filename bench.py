@@ -1,0 +1,396 @@
+#!/usr/bin/env python
+"""Headline benchmark of the B200 packed-weight matmul Provider.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload: Q4_K prefill GEMM, f32 activations
+X[512, 4096] ~ N(0, 1) times Q4_K W[14336 x 4096] (random blocks with
+f16 d, dmin ~ U(1e-3, 1e-2)), f32 output.  A step is one call of the path
+over one batch.  Metric: TFLOP/s (2*M*N*K per step), whole job.
+
+- value: device-resident inputs, the low-level C entry `mgb_qmatmul`
+  (f32 -> bf16 activation pass + tcgen05 GEMM), CUDA events on the launching
+  stream, inputs rotated over enough distinct sets to exceed 3x L2.
+- e2e: the same metric through the Provider C ABI with host buffers:
+  write_tensor from pinned memory (H2D), submit_kernel("matmul"),
+  complete_kernel, read_tensor into pinned memory (D2H), every step.
+- roofline: the GEMM kernel alone (`mgb_qmatmul_bf16`), FLOPs per launch over
+  its event-timed average duration, against MEASURED_PEAKS.json's burst bf16.
+- gemv: config 0 (Q4_K decode GEMV 1x4096 x 4096x4096) weight GB/s, as the
+  second half of the BASELINE metric.
+- cpu_baseline: the reference's own CPU path (int8 activations, AVX2 kernels,
+  persistent pool), restated in C (oracle/cpu_baseline.c), on a sample of
+  the same workload, on every host core.
+N > 1 (torchrun): tensor parallel along N (each rank holds 14336/N weight
+rows), outputs all-gathered over NCCL; strong scaling, max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+PKG = ROOT / "magnetar-provider-cpu_b200"
+for _p in (ROOT, PKG):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+M, K, N = 512, 4096, 14336
+GEMV_N = GEMV_K = 4096
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+METRIC = "Q4_K prefill GEMM TFLOP/s (X[512,4096] f32 x Q4_K W[14336x4096] -> f32)"
+WORKLOAD = "config1: Q4_K prefill GEMM M=512 K=4096 N=14336 (Llama-3-8B FFN gate/up)"
+
+
+def peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return json.loads(path.read_text()), "measured"
+        except ValueError:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profile_traffic(name: str) -> float | None:
+    """DRAM bytes per launch from a committed ncu summary (profiles/<name>.md:
+    a line `dram_bytes_per_launch: <int>`), or None."""
+    path = ROOT / "profiles" / f"{name}.md"
+    if not path.exists():
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", path.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled every 100 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(gpu_index)], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.file.flush()
+        rows = []
+        for line in pathlib.Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+
+        sm = [num(r[1]) for r in rows if num(r[1])]
+        sm_max = max((num(r[2]) or 0) for r in rows)
+        loaded = [s for s in sm if s and s > 0.5 * sm_max] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": sm_max,
+                "reasons": reasons, "samples": len(rows), "samples_under_load": len(loaded),
+                "power_w_max": max((num(r[3]) or 0) for r in rows)}
+
+
+# ---------------------------------------------------------------------------------------
+# the reference arm: the reference's own CPU path on the host cores
+# ---------------------------------------------------------------------------------------
+
+
+def cpu_baseline(steps: int, warmup: int, budget_s: float = 20.0) -> dict:
+    """Times the CPU port of the reference's default path (int8 activations,
+    AVX2 Q4_K kernel, pool over all host threads) on a column sample of config 1."""
+    import numpy as np
+
+    import synthetic
+    from oracle import oracle
+
+    threads = os.cpu_count() or 1
+    x = synthetic.activations(M, K)
+    full = synthetic.packed_weights(synthetic.Q4_K, N, K)
+    ncols = 256
+    cols = np.arange(ncols)
+    w = synthetic.row_slice(synthetic.Q4_K, full, K, cols)
+    t0 = time.perf_counter()
+    oracle.baseline_packed_matmul(synthetic.Q4_K, w, ncols, K, x, int8=True, threads=threads)
+    one = time.perf_counter() - t0
+    # size the sample so each timed call takes about budget / (steps + warmup) seconds
+    target = max(0.05, budget_s / max(1, steps + warmup))
+    ncols = int(min(N, max(64, ncols * target / max(one, 1e-6))) // 64 * 64) or 64
+    w = synthetic.row_slice(synthetic.Q4_K, full, K, np.arange(ncols))
+    for _ in range(warmup):
+        oracle.baseline_packed_matmul(synthetic.Q4_K, w, ncols, K, x, int8=True, threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        oracle.baseline_packed_matmul(synthetic.Q4_K, w, ncols, K, x, int8=True, threads=threads)
+    dt = (time.perf_counter() - t0) / steps
+    flops = 2.0 * M * ncols * K
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"M={M} K={K}, first {ncols} of {N} output columns per call, "
+                      f"{steps} timed calls of {dt * 1e3:.1f} ms after {warmup} warm-up",
+            "ms_per_call": dt * 1e3}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # under torchrun only rank 0 runs the CPU arm
+    steps = max(1, min(args.steps, 20))
+    warmup = max(1, min(args.warmup, 3))
+    cb = cpu_baseline(steps, warmup)
+    line = {"metric": METRIC, "value": cb["value"], "unit": "TFLOP/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": warmup, "ms_per_step": cb["ms_per_call"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8 x u4 dots, f32 accumulate", "data": "synthetic", "impl": "reference",
+            "config": {"workload": WORKLOAD, "m": M, "k": K, "n": N, "format": "Q4_K",
+                       "parallelism": "cpu-threads"},
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------
+# the B200 arm
+# ---------------------------------------------------------------------------------------
+
+
+def run_b200(args) -> None:
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import magnetar_b200 as mgb
+    import synthetic
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    if N % world:
+        raise SystemExit(f"N={N} does not split over {world} ranks")
+    n_loc = N // world
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    fmt = mgb.Q4_K
+
+    # weights: this rank's stored rows, in the device layout, rotated over R copies
+    full = synthetic.packed_weights(fmt, N, K)
+    w_loc = synthetic.row_slice(fmt, full, K, np.arange(rank * n_loc, (rank + 1) * n_loc))
+    del full
+    w_bytes = mgb.packed_bytes(fmt, n_loc, K)
+    set_bytes = w_bytes + M * K * 4 + M * n_loc * 4
+    R = max(2, -(-3 * L2_BYTES // set_bytes))
+    ggml = torch.from_numpy(w_loc).to(dev)
+    W = []
+    for _ in range(R):
+        buf = torch.empty(w_bytes, dtype=torch.uint8, device=dev)
+        mgb.repack(fmt, ggml.data_ptr(), n_loc, K, buf.data_ptr(), sp)
+        W.append(buf)
+    del ggml
+    x_host = synthetic.activations(M, K)
+    X = [torch.from_numpy(x_host).to(dev) for _ in range(R)]
+    Y = [torch.empty((M, n_loc), dtype=torch.float32, device=dev) for _ in range(R)]
+    ws_bytes = mgb.qmatmul_workspace_bytes(fmt, M, n_loc, K)
+    WS = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    gathered = torch.empty((world, M, n_loc), dtype=torch.float32, device=dev) if world > 1 else None
+    Y_full = torch.empty((M, N), dtype=torch.float32, device=dev) if world > 1 else None
+
+    def step(i: int) -> None:
+        s = i % R
+        mgb.qmatmul(fmt, W[s].data_ptr(), n_loc, K, X[s].data_ptr(), M, Y[s].data_ptr(),
+                    workspace_ptr=WS.data_ptr(), workspace_bytes=ws_bytes, stream=sp)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered.view(-1), Y[s].view(-1))
+            Y_full.view(M, world, n_loc).copy_(gathered.transpose(0, 1))
+
+    def timed(fn, steps: int, warmup: int) -> float:
+        for i in range(warmup):
+            fn(i)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(steps):
+            fn(i)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        ms = t0.elapsed_time(t1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    visible = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    sampler = ClockSampler(visible[local] if local < len(visible) else str(local))
+    total_ms = timed(step, args.steps, args.warmup)
+    ms_step = total_ms / args.steps
+    flops = 2.0 * M * N * K
+    value = flops / (ms_step * 1e-3) / 1e12
+
+    # roofline: the GEMM kernel alone on bf16 activations
+    XB = [x.to(torch.bfloat16) for x in X]
+
+    def gemm_only(i: int) -> None:
+        s = i % R
+        mgb.qmatmul_bf16(fmt, W[s].data_ptr(), n_loc, K, XB[s].data_ptr(), M, Y[s].data_ptr(),
+                         stream=sp)
+
+    gemm_ms = timed(gemm_only, args.steps, args.warmup) / args.steps
+    clocks = sampler.stop()
+    pk, pk_kind = peaks()
+    achieved = 2.0 * M * n_loc * K / (gemm_ms * 1e-3) / 1e12
+    traffic = profile_traffic("gemm_q4k_config1")
+    roofline = {"bound": "tensor", "kernel": "gemm_kernel<Q4_K> (tcgen05, bf16 x bf16 -> f32)",
+                "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": achieved / pk["bf16_tflops"], "peak_kind": f"{pk_kind} burst bf16",
+                "traffic": traffic, "ms_per_launch": gemm_ms,
+                "flops_per_launch": 2.0 * M * n_loc * K}
+
+    # e2e through the Provider's C ABI with pinned host buffers
+    prov = mgb.B200Provider(device=local)
+    assert prov.write_packed_weight_tensor("w", fmt, n_loc, K, True, w_loc) == "Stored"
+    xh = torch.from_numpy(x_host).pin_memory()
+    yh = torch.empty((M, n_loc), dtype=torch.float32).pin_memory()
+
+    def e2e_step(_i: int) -> None:
+        prov.write_tensor_ptr("x", (M, K), xh.data_ptr())
+        h = prov.submit_kernel("matmul", ["x", "w"], "y")
+        r = prov.complete_kernel(h)
+        if not r.ok:
+            raise RuntimeError(r.reason)
+        prov.read_tensor_into("y", yh.data_ptr(), M * n_loc)
+
+    e2e_steps = max(3, min(args.steps, 50))
+    for i in range(max(3, args.warmup)):
+        e2e_step(i)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    prov.close()
+    e2e = {"value": flops / e2e_s / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": M * K * 4 * world,
+           "d2h_bytes_per_step": M * N * 4, "ms_per_step": e2e_s * 1e3, "steps": e2e_steps,
+           "path": "mgb_write_tensor (pinned) -> mgb_submit_kernel(matmul) -> "
+                   "mgb_complete_kernel -> mgb_read_tensor (pinned); wall clock",
+           "timing": "wall clock per rank, max over ranks"}
+
+    # second half of the metric: config 0 decode GEMV weight GB/s (rank 0's GPU)
+    gemv = None
+    if rank == 0:
+        gw = synthetic.packed_weights(fmt, GEMV_N, GEMV_K)
+        gb = mgb.packed_bytes(fmt, GEMV_N, GEMV_K)
+        RV = max(2, -(-3 * L2_BYTES // gb))
+        src = torch.from_numpy(gw).to(dev)
+        GW = []
+        for _ in range(RV):
+            b = torch.empty(gb, dtype=torch.uint8, device=dev)
+            mgb.repack(fmt, src.data_ptr(), GEMV_N, GEMV_K, b.data_ptr(), sp)
+            GW.append(b)
+        gx = torch.from_numpy(synthetic.activations(1, GEMV_K)).to(dev)
+        gy = torch.empty((1, GEMV_N), dtype=torch.float32, device=dev)
+
+        def gemv_step(i: int) -> None:
+            mgb.qmatmul(fmt, GW[i % RV].data_ptr(), GEMV_N, GEMV_K, gx.data_ptr(), 1,
+                        gy.data_ptr(), stream=sp)
+
+        saved_world, world = world, 1  # single-GPU timing, no collectives
+        gsteps = max(args.steps, 200)
+        g_ms = timed(gemv_step, gsteps, max(args.warmup, 10)) / gsteps
+        world = saved_world
+        algo = gb + GEMV_K * 4 + GEMV_N * 4
+        gbs = algo / (g_ms * 1e-3) / 1e9
+        gemv = {"metric": "Q4_K decode GEMV weight GB/s (config0: x[1,4096] x W[4096x4096])",
+                "value": gbs, "unit": "GB/s", "us_per_launch": g_ms * 1e3,
+                "algorithmic_bytes": algo, "frac": gbs / pk["hbm_gbs"],
+                "peak": pk["hbm_gbs"], "peak_kind": f"{pk_kind} HBM copy",
+                "l2": f"{RV} rotating weight copies ({RV * gb / 1e6:.0f} MB > 3x L2)",
+                "traffic": profile_traffic("gemv_q4k_config0")}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(steps=10, warmup=1)
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16 operands, f32 accumulate", "data": "synthetic",
+                "config": {"workload": WORKLOAD, "m": M, "k": K, "n": N, "format": "Q4_K",
+                           "n_per_rank": n_loc, "parallelism": f"tp{world}",
+                           "l2": f"{R} rotating input sets of {set_bytes / 1e6:.0f} MB "
+                                 f"({R * set_bytes / 1e6:.0f} MB > 3x 126 MB L2)",
+                           "step": "mgb_qmatmul: f32->bf16 activation pass + tcgen05 GEMM"
+                                   + (" + NCCL all-gather of output columns" if world > 1 else "")},
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": 2 * args.steps, "clocks": clocks, "gemv": gemv}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -299,6 +299,19 @@ class B200Provider:
         check(lib().mgb_write_tensor(self._h, id.encode(), shape, a.ndim,
                                      a.ctypes.data if a.size else None))
 
+    def write_tensor_ptr(self, id: str, shape: tuple[int, ...], host_ptr: int) -> None:
+        """`write_tensor` from a raw host pointer (e.g. a pinned buffer)."""
+        sh = (ctypes.c_uint64 * max(1, len(shape)))(*shape)
+        check(lib().mgb_write_tensor(self._h, id.encode(), sh, len(shape), host_ptr))
+
+    def read_tensor_into(self, id: str, host_ptr: int, capacity: int) -> list[int]:
+        """`read_tensor` into a raw host pointer of `capacity` floats; returns the shape."""
+        sh = (ctypes.c_uint64 * MAX_RANK)()
+        rank = ctypes.c_int32(0)
+        check(lib().mgb_read_tensor(self._h, id.encode(), host_ptr, capacity, sh,
+                                    ctypes.byref(rank)))
+        return [int(sh[i]) for i in range(rank.value)]
+
     def write_packed_weight_tensor(self, id: str, fmt: int, stored_rows: int, stored_cols: int,
                                    transposed: bool, data: np.ndarray) -> str:
         b = np.ascontiguousarray(data, dtype=np.uint8)

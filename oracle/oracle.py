@@ -64,6 +64,40 @@ def lib() -> ctypes.CDLL:
     return _lib
 
 
+def baseline() -> ctypes.CDLL:
+    """The CPU-baseline port of the reference's default packed path (int8
+    activations, AVX2 kernels, persistent pool; oracle/cpu_baseline.c)."""
+    global _baseline
+    if _baseline is None:
+        if not BASELINE_PATH.exists():
+            build()
+        L = ctypes.CDLL(str(BASELINE_PATH))
+        L.cpb_set_threads.argtypes = [ctypes.c_int]
+        L.cpb_set_threads.restype = ctypes.c_int
+        for name in ("cpb_packed_matmul", "cpb_packed_matmul_f32"):
+            fn = getattr(L, name)
+            fn.argtypes = [ctypes.c_int, _u8p, _u64, _u64, _f32p, _u64, _u64, _f32p]
+            fn.restype = ctypes.c_int
+        _baseline = L
+    return _baseline
+
+
+def baseline_packed_matmul(fmt: int, data: np.ndarray, stored_rows: int, stored_cols: int,
+                           x: np.ndarray, int8: bool = True, threads: int = 1) -> np.ndarray:
+    """Times the reference's own CPU path: y[m, stored_rows] (int8 activations by default)."""
+    L = baseline()
+    L.cpb_set_threads(threads)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    data = np.ascontiguousarray(data, dtype=np.uint8)
+    m, k = x.shape
+    y = np.empty((m, stored_rows), dtype=np.float32)
+    fn = L.cpb_packed_matmul if int8 else L.cpb_packed_matmul_f32
+    rc = fn(fmt, _p(data, _u8p), stored_rows, stored_cols, _p(x, _f32p), m, k, _p(y, _f32p))
+    if rc:
+        raise ValueError("cpu baseline: shape or format rejected")
+    return y
+
+
 def _p(a: np.ndarray, t):
     return a.ctypes.data_as(t)
 

@@ -183,3 +183,24 @@ def test_bias_broadcast(oracle):
     assert oracle.add(a, b).tolist() == [[10, 21, 32], [13, 24, 35]]
     with pytest.raises(ValueError):
         oracle.add(a, np.ones(4, np.float32))
+
+
+@pytest.mark.parametrize("fmt", [0, 1, 5, 13])
+@pytest.mark.parametrize("threads", [1, 4])
+def test_cpu_baseline_port_matches_the_oracle(oracle, fmt, threads):
+    # the timed CPU arm (AVX2 restatement + pool) agrees with the scalar oracle
+    # the way the reference's own test does (src/native/tests.rs:134-154)
+    k, n = 512, 37
+    w = oracle.test_packed(fmt, n, k, 21)
+    dense = oracle.dequantize(fmt, w, n, k)
+    for m in (1, 3, 9):
+        a = oracle.test_activations(m, k, m)
+        got = oracle.baseline_packed_matmul(fmt, w, n, k, a, int8=True, threads=threads)
+        oracle.assert_close(got, oracle.matmul(oracle.int8_rounded(a), dense, False, True), 2e-5)
+        got32 = oracle.baseline_packed_matmul(fmt, w, n, k, a, int8=False, threads=threads)
+        assert np.array_equal(got32, oracle.matmul(a, dense, False, True))
+    if fmt != 1:  # odd run counts take the paired kernels' tail (src/native/tests.rs:156-174)
+        w = oracle.test_packed(fmt, 5, 96, 23)
+        a = oracle.test_activations(2, 96, 7)
+        oracle.assert_close(oracle.baseline_packed_matmul(fmt, w, 5, 96, a, threads=threads),
+                            oracle.packed_matmul(fmt, w, 5, 96, a, int8=True), 2e-5)
