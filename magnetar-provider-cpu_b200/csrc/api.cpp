@@ -101,7 +101,8 @@ mgb_status run_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, co
   for (uint64_t r = 0; r < m; r += 2) {
     const uint64_t rows = m - r < 2 ? m - r : 2;
     const float *add = addend_mode == 2 ? addend + r * n : addend;
-    e = launch_gemv(format, w, n, k, x + r * k, rows, y + r * n, add, addend_mode, sms, stream);
+    e = launch_gemv(format, w, n, k, x + r * k, rows, y + r * n, add, addend_mode, err, sms,
+                    stream);
     if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
   }
   return MGB_OK;

@@ -6,14 +6,14 @@
 //
 // CTA tile: BM activation rows (1 or 2 accumulators of 128 rows) x BN weight
 // rows (the MMA N, <= 256, a multiple of 16), K in steps of 64 (one 128-byte
-// swizzle atom of bf16).  Warp roles, 192 threads:
+// swizzle atom of bf16).  Warp roles, 320 threads:
 //   warp 0   TMA producer: per K step one or two bf16 activation boxes
 //            (SWIZZLE_128B, straight into the UMMA operand layout) and the
 //            packed W quant and scale boxes (no swizzle), all on full[s].
 //            Owns the TMEM allocation.
 //   warp 1   one thread issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32) per
 //            16-wide K slice and commits each stage to empty[s].
-//   warps 2-5  dequantise the staged packed W into the bf16 B operand
+//   warps 2-9  dequantise the staged packed W into the bf16 B operand
 //            (K-major, SWIZZLE_128B written by hand), fence the async proxy and
 //            arrive on wready[s]; after the last stage they drain TMEM with
 //            tcgen05.ld and write y (+ the optional addend).
@@ -32,9 +32,10 @@ namespace mgb {
 
 namespace {
 
-constexpr int KSTEP = 64;        // bf16 values per 128-byte row of a stage
-constexpr int NUM_THREADS = 192;
-constexpr int DQ_THREADS = 128;  // warps 2..5
+constexpr int KSTEP = 64;                    // bf16 values per 128-byte row of a stage
+constexpr int DQ_WARPS = 8;                  // warps 2..9: dequantise, then the epilogue
+constexpr int DQ_THREADS = 32 * DQ_WARPS;
+constexpr int NUM_THREADS = 64 + DQ_THREADS;
 
 struct GemmParams {
   int m, n, k;
@@ -126,10 +127,12 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 }
 
 // 4-bit nibble pairs (byte i = values 2i, 2i+1) with value = s * q - mn,
-// written as 4 uint4 (8 bf16 each) into out[].
+// written as 4 uint4 (8 bf16 each) into out[].  f = 0.5 + q/256 (one prmt
+// per value) and s*q - mn = f * 256 s - (128 s + mn): one packed f32x2 FMA
+// per value pair, one cvt.rn.bf16x2 per pair.
 __device__ __forceinline__ void dq_nib_linear(const uint4 &qs, float s, float mn, uint4 out[4]) {
-  // f = 0.5 + q/256  =>  s*q - mn = f * 256 s - (128 s + mn)
   const float a = 256.f * s, c = -(128.f * s + mn);
+  const float2 a2 = make_float2(a, a), c2 = make_float2(c, c);
   const uint32_t words[4] = {qs.x, qs.y, qs.z, qs.w};
 #pragma unroll
   for (int wd = 0; wd < 4; ++wd) {
@@ -139,7 +142,8 @@ __device__ __forceinline__ void dq_nib_linear(const uint4 &qs, float s, float mn
     for (int i = 0; i < 4; ++i) {
       const float f0 = __uint_as_float(__byte_perm(lo, 0x3F000000u, 0x7054u | ((uint32_t)i << 8)));
       const float f1 = __uint_as_float(__byte_perm(hi, 0x3F000000u, 0x7054u | ((uint32_t)i << 8)));
-      p[i] = pack_bf16(fmaf(f0, a, c), fmaf(f1, a, c));
+      const float2 v = __ffma2_rn(make_float2(f0, f1), a2, c2);
+      p[i] = pack_bf16(v.x, v.y);
     }
     out[wd] = make_uint4(p[0], p[1], p[2], p[3]);
   }
@@ -316,7 +320,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else {
     // ---------------- dequantise W, then the epilogue ----------------
-    const int t = threadIdx.x - 64;  // 0..127
+    const int t = threadIdx.x - 64;  // 0..DQ_THREADS-1
     uint32_t lut[4] = {0, 0, 0, 0};
     if (FMT == IQ4_NL) {
 #pragma unroll
@@ -356,15 +360,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       fence_proxy_async_smem();
       mbar_arrive(&wready[s]);
     }
-    // epilogue: TMEM lanes of this warp's quarter -> y rows
+    // epilogue: TMEM lanes of this warp's quarter -> y rows; the two warps of
+    // a quarter take alternate 8-column chunks
     const bool finished = mbar_wait(done, 0, p.err);
     tc_fence_after();
     // tcgen05.ld is warp-collective: the whole warp drains TMEM or none of it
     if (__all_sync(0xffffffffu, finished && !*(volatile int *)abort_flag)) {
       const int quarter = warp & 3;
+      const int half = (warp - 2) / 4;
       for (int sub = 0; sub < SUBS; ++sub) {
         const int row = m0 + sub * 128 + quarter * 32 + lane;
-        for (int c = 0; c < p.bn; c += 8) {
+        for (int c = 8 * half; c < p.bn; c += 16) {
           float v[8];
           tmem_ld8(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * 256 + c), v);
           if (row < p.m) {

@@ -4,18 +4,26 @@
 // `columns_iq4nl_avx2` (src/native/quant.rs:604-744, :1438-1483) with the f32
 // semantics of its scalar path (:559-597).
 //
-// Work split: one CTA owns a contiguous range of output rows (stored rows of
-// W).  Thread t owns run t of K (32 values) for the whole kernel: its
-// activations live in registers, so the only memory stream is W itself, read
-// once with 128-bit loads (each warp reads 512 contiguous quant bytes per
-// row).  Per row every thread produces a partial dot product; warps reduce with
-// shuffles and a fixed-order shared-memory pass produces y (deterministic).
+// Main kernel (k % 256 == 0), persistent and bulk-copy staged:
+//   warp 0      one thread streams the CTA's rows of both planes of W (the
+//               quant plane and the scale plane; consecutive rows are
+//               contiguous, so one cp.async.bulk per plane per stage) into a
+//               ring of shared-memory stages, starting before anything else:
+//               the bytes in flight cost no registers.
+//   warps 1..   consumer teams of ceil(k / 1024) warps; thread u of a team owns
+//               run u of K (32 values) for the whole kernel, its activations
+//               in registers, and reads its 16 (Q8_0: 32) quant bytes of each
+//               staged row from shared memory.  Per row the team reduces its
+//               partial sums with shuffles and a fixed-order pass over its
+//               warps (deterministic), and one thread writes y.
+// Programmatic dependent launch: the producer starts streaming weights
+// immediately (they never depend on an earlier kernel); consumers execute
+// griddepcontrol.wait before reading x or writing y.
 //
 // Quant -> f32 without integer-to-float conversions:
-//   4-bit q: prmt places q in bits 16..19 of 0x3F000000, i.e. the float
-//            0.5 + q/256.  With t = sum((0.5 + q/256) x) over the run and
-//            X = sum(x) over the run (computed once per thread),
-//            sum(q x) = 256 t - 128 X.
+//   4-bit q: prmt places q in bits 16..19 of 0x3F000000, the float
+//            0.5 + q/256.  With t = sum((0.5 + q/256) x) and X = sum(x) over
+//            the run (computed once per thread), sum(q x) = 256 t - 128 X.
 //   8-bit q: prmt places (q + 128) in the low byte of 0x4B000000, the float
 //            2^23 + q + 128; subtracting 2^23 + 128 is exact.
 // Products accumulate with the packed fma.rn.f32x2 (two values per issue).
@@ -36,6 +44,17 @@ __device__ __forceinline__ uint32_t ld_nc_u16(const void *p) {
   unsigned short v;
   asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(p));
   return v;
+}
+
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void named_barrier(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 // 0.5 + q/256 for the 4-bit value in byte i of `v` (bits 0..3 of that byte).
@@ -67,8 +86,8 @@ __device__ __forceinline__ float dot_nib_run(const uint4 &qs, const float *xr) {
   return acc.x + acc.y;
 }
 
-// sum over a run of (b + 128) * x for the biased bytes of 8 words (byte
-// order = value order); returns sum(b * x) exactly shifted back.
+// sum over a run of b * x for the +128-biased bytes of 8 words (byte order =
+// value order).
 __device__ __forceinline__ float dot_byte_words(const uint32_t *u, const float *xr) {
   const float2 bias = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
   float2 acc = make_float2(0.f, 0.f);
@@ -101,21 +120,63 @@ __device__ __forceinline__ void iq4_lookup(uint32_t v, const uint32_t t[4], uint
   }
 }
 
-template <int FMT, int MR, int R, int MAXT>
-__global__ void __launch_bounds__(MAXT, 1)
-    gemv_kernel(const uint8_t *__restrict__ w, int n, int k, const float *__restrict__ x,
-                float *__restrict__ y, const float *__restrict__ addend, int addend_mode,
-                int rows_per_cta) {
-  __shared__ float red[2][32][R * MR];
-  const Layout L(FMT, (uint64_t)n, (uint64_t)k);
-  const int runs = k / RUN;
-  const int u = threadIdx.x;
-  const bool active = u < runs;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nwarps = blockDim.x >> 5;
+__device__ __forceinline__ void iq4_table(uint32_t lut[4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t v = 0;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) v |= (uint32_t)((iq4nl_value(4 * i + b) + 128) & 0xff) << (8 * b);
+    lut[i] = v;
+  }
+}
 
-  float xr[MR][32];
-  float X[MR];
+// The partial dot products of one run of one row with MR activation rows.
+// qa (and qb for Q8_0) hold the run's quant bytes; hd the Q4_K header of its
+// super-block; dh the f16 scale of the other formats; j the run's index in
+// its super-block.
+template <int FMT, int MR>
+__device__ __forceinline__ void run_partials(const uint4 &qa, const uint4 &qb, const uint4 &hd,
+                                             uint32_t dh, int j, const float (&xr)[MR][32],
+                                             const float (&X)[MR], const uint32_t lut[4],
+                                             float (&part)[MR]) {
+  if (FMT == Q4_K) {
+    const float d = f16_bits_to_f32(hd.x), dmin = f16_bits_to_f32(hd.x >> 16);
+    uint32_t sc, mn;
+    scale_min_k4(j, hd.y, hd.z, hd.w, sc, mn);
+    const float s = d * (float)sc, mv = dmin * (float)mn;
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      const float t = dot_nib_run(qa, xr[m]);
+      part[m] = (256.f * s) * t - (128.f * s + mv) * X[m];
+    }
+  } else if (FMT == Q4_0) {
+    const float d = f16_bits_to_f32(dh);
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      const float t = dot_nib_run(qa, xr[m]);
+      part[m] = d * (256.f * t - 136.f * X[m]);
+    }
+  } else if (FMT == Q8_0) {
+    const float d = f16_bits_to_f32(dh);
+    const uint32_t ub[8] = {qa.x ^ 0x80808080u, qa.y ^ 0x80808080u, qa.z ^ 0x80808080u,
+                            qa.w ^ 0x80808080u, qb.x ^ 0x80808080u, qb.y ^ 0x80808080u,
+                            qb.z ^ 0x80808080u, qb.w ^ 0x80808080u};
+#pragma unroll
+    for (int m = 0; m < MR; ++m) part[m] = d * dot_byte_words(ub, xr[m]);
+  } else {  // IQ4_NL
+    const float d = f16_bits_to_f32(dh);
+    uint32_t ub[8];
+    const uint32_t words[4] = {qa.x, qa.y, qa.z, qa.w};
+#pragma unroll
+    for (int wd = 0; wd < 4; ++wd) iq4_lookup(words[wd], lut, ub[2 * wd], ub[2 * wd + 1]);
+#pragma unroll
+    for (int m = 0; m < MR; ++m) part[m] = d * dot_byte_words(ub, xr[m]);
+  }
+}
+
+template <int MR>
+__device__ __forceinline__ void load_x(const float *__restrict__ x, int k, int u, bool active,
+                                       float (&xr)[MR][32], float (&X)[MR]) {
 #pragma unroll
   for (int m = 0; m < MR; ++m) {
     X[m] = 0.f;
@@ -130,90 +191,205 @@ __global__ void __launch_bounds__(MAXT, 1)
       X[m] += (v.x + v.y) + (v.z + v.w);
     }
   }
+}
 
-  uint32_t lut[4] = {0, 0, 0, 0};
-  if (FMT == IQ4_NL) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint32_t v = 0;
-#pragma unroll
-      for (int b = 0; b < 4; ++b) v |= (uint32_t)((iq4nl_value(4 * i + b) + 128) & 0xff) << (8 * b);
-      lut[i] = v;
+// ---- main kernel: bulk-copy staged, persistent ----------------------------------------
+
+struct GemvStaged {
+  int n, k;
+  int teams, team_warps;  // consumer geometry
+  int rows_per_team;      // rows per team per stage
+  int stages;
+  int rows_per_cta;
+  uint32_t stage_bytes, qs_stage_bytes;
+  int addend_mode;
+  const float *addend;
+  float *y;
+  int *err;
+};
+
+template <int FMT, int MR, int MAXT>
+__global__ void __launch_bounds__(MAXT, 1)
+    gemv_staged_kernel(const uint8_t *__restrict__ w, const float *__restrict__ x,
+                       const GemvStaged p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const Layout L(FMT, (uint64_t)p.n, (uint64_t)p.k);
+  const int S = p.stages;
+  const int TR = p.teams * p.rows_per_team;  // rows per stage
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * p.stage_bytes);
+  uint64_t *empty = full + S;
+  float *red = reinterpret_cast<float *>(empty + S);  // [2][teams][team_warps][RPT*MR]
+  const int consumer_warps = p.teams * p.team_warps;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = blockIdx.x * p.rows_per_cta;
+  const int r1 = min(p.n, r0 + p.rows_per_cta);
+  const int nstages = r1 > r0 ? (r1 - r0 + TR - 1) / TR : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], consumer_warps);
     }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      grid_launch_dependents();
+      int issued = 0;
+      for (int g = 0; g < nstages; ++g) {
+        const int s = g % S;
+        if (g >= S && !mbar_wait(&empty[s], ((g / S) - 1) & 1, p.err)) break;
+        const int row = r0 + g * TR;
+        const int rows = min(TR, r1 - row);
+        uint8_t *st = smem + (size_t)s * p.stage_bytes;
+        const uint32_t qb = (uint32_t)(rows * L.qs_row), sb = (uint32_t)(rows * L.sc_row);
+        mbar_arrive_expect_tx(&full[s], qb + sb);
+        bulk_g2s(st, w + (size_t)row * L.qs_row, qb, &full[s]);
+        bulk_g2s(st + p.qs_stage_bytes, w + L.qs_bytes + (size_t)row * L.sc_row, sb, &full[s]);
+        issued = g + 1;
+      }
+      // every copy issued has landed before the CTA may exit
+      for (int g = (issued > S ? issued - S : 0); g < issued; ++g)
+        mbar_wait(&full[g % S], (g / S) & 1, nullptr);
+    }
+    return;
   }
 
+  // ---------------- consumers ----------------
+  const int cw = warp - 1;
+  const int team = cw / p.team_warps, tw = cw % p.team_warps;
+  const int u = tw * 32 + lane;  // this thread's run of K
+  const int runs = p.k / RUN;
+  const bool active = u < runs;
+  const int team_threads = p.team_warps * 32;
+  const int RPT = p.rows_per_team;
+
+  grid_dependency_wait();  // x may be the previous kernel's output
+  float xr[MR][32];
+  float X[MR];
+  load_x<MR>(x, p.k, u, active, xr, X);
+  uint32_t lut[4] = {0, 0, 0, 0};
+  if (FMT == IQ4_NL) iq4_table(lut);
+
+  constexpr int MAX_RPT = 4;
+  // A wait that gives up records the error and the thread stops waiting, but
+  // it keeps stepping through every stage so its team's named barriers match.
+  bool ok = true;
+  for (int g = 0; g < nstages; ++g) {
+    const int s = g % S;
+    ok = ok && mbar_wait(&full[s], (g / S) & 1, p.err);
+    const uint8_t *st = smem + (size_t)s * p.stage_bytes;
+    const int row0 = r0 + g * TR;
+    float part[MAX_RPT][MR];
+#pragma unroll
+    for (int i = 0; i < MAX_RPT; ++i) {
+#pragma unroll
+      for (int m = 0; m < MR; ++m) part[i][m] = 0.f;
+      const int lr = team * RPT + i;  // row within the stage
+      if (ok && i < RPT && active && row0 + lr < r1) {
+        const uint8_t *qrow = st + (size_t)lr * L.qs_row;
+        const uint8_t *srow = st + p.qs_stage_bytes + (size_t)lr * L.sc_row;
+        uint4 qa, qb = make_uint4(0, 0, 0, 0), hd = make_uint4(0, 0, 0, 0);
+        uint32_t dh = 0;
+        if (FMT == Q8_0) {
+          qa = *reinterpret_cast<const uint4 *>(qrow + u * 32);
+          qb = *reinterpret_cast<const uint4 *>(qrow + u * 32 + 16);
+        } else {
+          qa = *reinterpret_cast<const uint4 *>(qrow + u * 16);
+        }
+        if (FMT == Q4_K) hd = *reinterpret_cast<const uint4 *>(srow + (u >> 3) * 16);
+        else dh = *reinterpret_cast<const uint16_t *>(srow + u * 2);
+        float pm[MR];
+        run_partials<FMT, MR>(qa, qb, hd, dh, u & 7, xr, X, lut, pm);
+#pragma unroll
+        for (int m = 0; m < MR; ++m) part[i][m] = pm[m];
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the stage's bytes
+    float *rb = red + ((size_t)(g & 1) * p.teams + team) * p.team_warps * (MAX_RPT * MR);
+#pragma unroll
+    for (int i = 0; i < MAX_RPT; ++i)
+#pragma unroll
+      for (int m = 0; m < MR; ++m) {
+        if (i >= RPT) continue;
+        float v = part[i][m];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == 0) rb[tw * (MAX_RPT * MR) + i * MR + m] = v;
+      }
+    named_barrier(1 + team, team_threads);
+    const int t = tw * 32 + lane;
+    if (t < RPT * MR) {
+      const int i = t / MR, m = t % MR;
+      const int row = row0 + team * RPT + i;
+      if (row < r1) {
+        float sum = 0.f;
+        for (int wi = 0; wi < p.team_warps; ++wi) sum += rb[wi * (MAX_RPT * MR) + i * MR + m];
+        if (p.addend_mode == 1) sum = sum + p.addend[row];
+        else if (p.addend_mode == 2) sum = sum + p.addend[(size_t)m * p.n + row];
+        p.y[(size_t)m * p.n + row] = sum;
+      }
+    }
+  }
+}
+
+// ---- fallback kernel for k % 256 != 0 (ragged scale planes): direct loads -------------
+
+template <int FMT, int MR, int R, int MAXT>
+__global__ void __launch_bounds__(MAXT, 1)
+    gemv_simple_kernel(const uint8_t *__restrict__ w, int n, int k, const float *__restrict__ x,
+                       float *__restrict__ y, const float *__restrict__ addend, int addend_mode,
+                       int rows_per_cta) {
+  __shared__ float red[2][32][R * MR];
+  const Layout L(FMT, (uint64_t)n, (uint64_t)k);
+  const int runs = k / RUN;
+  const int u = threadIdx.x;
+  const bool active = u < runs;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  float xr[MR][32];
+  float X[MR];
+  load_x<MR>(x, k, u, active, xr, X);
+  uint32_t lut[4] = {0, 0, 0, 0};
+  if (FMT == IQ4_NL) iq4_table(lut);
   const int r0 = blockIdx.x * rows_per_cta;
   const int r1 = min(n, r0 + rows_per_cta);
   const uint8_t *scale_plane = w + L.qs_bytes;
   int buf = 0;
   for (int r = r0; r < r1; r += R) {
-    uint4 qa[R], qb[R], hd[R];
-    uint32_t dh[R];
-#pragma unroll
-    for (int i = 0; i < R; ++i) {
-      const int row = r + i;
-      qa[i] = qb[i] = hd[i] = make_uint4(0, 0, 0, 0);
-      dh[i] = 0;
-      if (active && row < r1) {
-        const uint8_t *qrow = w + (size_t)row * L.qs_row;
-        const uint8_t *srow = scale_plane + (size_t)row * L.sc_row;
-        if (FMT == Q8_0) {
-          qa[i] = ld_stream_v4(qrow + (size_t)u * 32);
-          qb[i] = ld_stream_v4(qrow + (size_t)u * 32 + 16);
-          dh[i] = ld_nc_u16(srow + (size_t)u * 2);
-        } else {
-          qa[i] = ld_stream_v4(qrow + (size_t)u * 16);
-          if (FMT == Q4_K)
-            hd[i] = __ldg(reinterpret_cast<const uint4 *>(srow + (size_t)(u >> 3) * 16));
-          else
-            dh[i] = ld_nc_u16(srow + (size_t)u * 2);
-        }
-      }
-    }
     float part[R][MR];
 #pragma unroll
     for (int i = 0; i < R; ++i) {
-      if (FMT == Q4_K) {
-        const float d = f16_bits_to_f32(hd[i].x), dmin = f16_bits_to_f32(hd[i].x >> 16);
-        uint32_t sc, mn;
-        scale_min_k4(u & 7, hd[i].y, hd[i].z, hd[i].w, sc, mn);
-        const float s = d * (float)sc, mv = dmin * (float)mn;
+      const int row = r + i;
 #pragma unroll
-        for (int m = 0; m < MR; ++m) {
-          const float t = dot_nib_run(qa[i], xr[m]);
-          part[i][m] = (256.f * s) * t - (128.f * s + mv) * X[m];
+      for (int m = 0; m < MR; ++m) part[i][m] = 0.f;
+      if (active && row < r1) {
+        const uint8_t *qrow = w + (size_t)row * L.qs_row;
+        const uint8_t *srow = scale_plane + (size_t)row * L.sc_row;
+        uint4 qa, qb = make_uint4(0, 0, 0, 0), hd = make_uint4(0, 0, 0, 0);
+        uint32_t dh = 0;
+        if (FMT == Q8_0) {
+          qa = ld_stream_v4(qrow + (size_t)u * 32);
+          qb = ld_stream_v4(qrow + (size_t)u * 32 + 16);
+        } else {
+          qa = ld_stream_v4(qrow + (size_t)u * 16);
         }
-      } else if (FMT == Q4_0) {
-        const float d = f16_bits_to_f32(dh[i]);
+        if (FMT == Q4_K) hd = __ldg(reinterpret_cast<const uint4 *>(srow + (size_t)(u >> 3) * 16));
+        else dh = ld_nc_u16(srow + (size_t)u * 2);
+        float pm[MR];
+        run_partials<FMT, MR>(qa, qb, hd, dh, u & 7, xr, X, lut, pm);
 #pragma unroll
-        for (int m = 0; m < MR; ++m) {
-          const float t = dot_nib_run(qa[i], xr[m]);
-          part[i][m] = d * (256.f * t - 136.f * X[m]);
-        }
-      } else if (FMT == Q8_0) {
-        const float d = f16_bits_to_f32(dh[i]);
-        const uint32_t ub[8] = {qa[i].x ^ 0x80808080u, qa[i].y ^ 0x80808080u,
-                                qa[i].z ^ 0x80808080u, qa[i].w ^ 0x80808080u,
-                                qb[i].x ^ 0x80808080u, qb[i].y ^ 0x80808080u,
-                                qb[i].z ^ 0x80808080u, qb[i].w ^ 0x80808080u};
-#pragma unroll
-        for (int m = 0; m < MR; ++m) part[i][m] = d * dot_byte_words(ub, xr[m]);
-      } else {  // IQ4_NL
-        const float d = f16_bits_to_f32(dh[i]);
-        uint32_t ub[8];
-        const uint32_t words[4] = {qa[i].x, qa[i].y, qa[i].z, qa[i].w};
-#pragma unroll
-        for (int wd = 0; wd < 4; ++wd) iq4_lookup(words[wd], lut, ub[2 * wd], ub[2 * wd + 1]);
-#pragma unroll
-        for (int m = 0; m < MR; ++m) part[i][m] = d * dot_byte_words(ub, xr[m]);
+        for (int m = 0; m < MR; ++m) part[i][m] = pm[m];
       }
     }
-    // reduce every partial over the warp, then over the warps in fixed order
 #pragma unroll
     for (int i = 0; i < R; ++i)
 #pragma unroll
       for (int m = 0; m < MR; ++m) {
-        float v = active ? part[i][m] : 0.f;
+        float v = part[i][m];
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
         if (lane == 0) red[buf][warp][i * MR + m] = v;
@@ -234,9 +410,62 @@ __global__ void __launch_bounds__(MAXT, 1)
   }
 }
 
+// ---- launch --------------------------------------------------------------------------
+
+template <int FMT, int MR, int MAXT>
+static cudaError_t launch_staged(const void *w, int n, int k, const float *x, float *y,
+                                 const float *addend, int addend_mode, int *err, int sms,
+                                 cudaStream_t stream) {
+  const Layout L(FMT, (uint64_t)n, (uint64_t)k);
+  GemvStaged p;
+  p.n = n;
+  p.k = k;
+  p.team_warps = (k / RUN + 31) / 32;
+  p.teams = p.team_warps >= 8 ? 1 : 8 / p.team_warps;
+  p.rows_per_team = 2;
+  const int TR = p.teams * p.rows_per_team;
+  p.qs_stage_bytes = (uint32_t)ceil_div((uint64_t)TR * L.qs_row, 128) * 128;
+  p.stage_bytes = p.qs_stage_bytes + (uint32_t)ceil_div((uint64_t)TR * L.sc_row, 128) * 128;
+  const uint32_t budget = 96 * 1024;
+  int stages = (int)(budget / p.stage_bytes);
+  if (stages > 8) stages = 8;
+  if (stages < 2) stages = 2;
+  p.stages = stages;
+  // two CTAs per SM when they fit (so a dependent launch can overlap), rows split evenly
+  const int threads = 32 * (1 + p.teams * p.team_warps);
+  const int per_sm = threads <= 512 ? 2 : 1;
+  const int units = (int)ceil_div((uint64_t)n, (uint64_t)TR);
+  int grid = sms * per_sm;
+  if (grid > units) grid = units;
+  // rows split evenly; a CTA's last stage may hold fewer than TR rows
+  p.rows_per_cta = (int)ceil_div((uint64_t)n, (uint64_t)grid);
+  grid = (int)ceil_div((uint64_t)n, (uint64_t)p.rows_per_cta);
+  p.addend_mode = addend_mode;
+  p.addend = addend;
+  p.y = y;
+  p.err = err;
+  const size_t smem = (size_t)stages * p.stage_bytes + 2 * 8 * (size_t)stages +
+                      2 * sizeof(float) * (size_t)p.teams * p.team_warps * 4 * MR;
+  auto kern = gemv_staged_kernel<FMT, MR, MAXT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((unsigned)threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<const uint8_t *>(w), x, p);
+}
+
 template <int FMT, int MR, int R, int MAXT>
-static cudaError_t launch_t(const void *w, int n, int k, const float *x, float *y,
-                            const float *addend, int addend_mode, int sms, cudaStream_t stream) {
+static cudaError_t launch_simple(const void *w, int n, int k, const float *x, float *y,
+                                 const float *addend, int addend_mode, int sms,
+                                 cudaStream_t stream) {
   const int runs = k / RUN;
   const int threads = ((runs + 31) / 32) * 32;
   int per_sm = 2048 / threads;
@@ -246,32 +475,43 @@ static cudaError_t launch_t(const void *w, int n, int k, const float *x, float *
   int rows = (int)ceil_div((uint64_t)n, (uint64_t)target);
   if (rows < 1) rows = 1;
   const int grid = (int)ceil_div((uint64_t)n, (uint64_t)rows);
-  gemv_kernel<FMT, MR, R, MAXT><<<grid, threads, 0, stream>>>(
+  gemv_simple_kernel<FMT, MR, R, MAXT><<<grid, threads, 0, stream>>>(
       static_cast<const uint8_t *>(w), n, k, x, y, addend, addend_mode, rows);
   return cudaGetLastError();
 }
 
 template <int FMT, int MR>
 static cudaError_t launch_fmt(const void *w, int n, int k, const float *x, float *y,
-                              const float *addend, int addend_mode, int sms, cudaStream_t stream) {
-  if (k <= 256 * 32) return launch_t<FMT, MR, 4, 256>(w, n, k, x, y, addend, addend_mode, sms, stream);
-  // 1024-thread CTAs have 64 registers per thread: one activation row per launch
-  cudaError_t e = launch_t<FMT, 1, 2, 1024>(w, n, k, x, y, addend, addend_mode, sms, stream);
+                              const float *addend, int addend_mode, int *err, int sms,
+                              cudaStream_t stream) {
+  if (k % 256 == 0 && k / RUN <= 31 * 32) {  // a team of at most 31 warps plus the producer
+    if (k <= 8192)
+      return launch_staged<FMT, MR, 288>(w, n, k, x, y, addend, addend_mode, err, sms, stream);
+    // 1024-thread CTAs have 64 registers per thread: one activation row per launch
+    cudaError_t e = launch_staged<FMT, 1, 1024>(w, n, k, x, y, addend, addend_mode, err, sms, stream);
+    if (MR == 2 && e == cudaSuccess)
+      e = launch_staged<FMT, 1, 1024>(w, n, k, x + k, y + n, addend_mode == 2 ? addend + n : addend,
+                                      addend_mode, err, sms, stream);
+    return e;
+  }
+  if (k <= 256 * 32) return launch_simple<FMT, MR, 4, 256>(w, n, k, x, y, addend, addend_mode, sms, stream);
+  cudaError_t e = launch_simple<FMT, 1, 2, 1024>(w, n, k, x, y, addend, addend_mode, sms, stream);
   if (MR == 2 && e == cudaSuccess)
-    e = launch_t<FMT, 1, 2, 1024>(w, n, k, x + k, y + n,
-                                  addend_mode == 2 ? addend + n : addend, addend_mode, sms, stream);
+    e = launch_simple<FMT, 1, 2, 1024>(w, n, k, x + k, y + n,
+                                       addend_mode == 2 ? addend + n : addend, addend_mode, sms,
+                                       stream);
   return e;
 }
 
 cudaError_t launch_gemv(int fmt, const void *w, uint64_t n, uint64_t k, const float *x,
-                        uint64_t m, float *y, const float *addend, int addend_mode, int sms,
-                        cudaStream_t stream) {
+                        uint64_t m, float *y, const float *addend, int addend_mode, int *err,
+                        int sms, cudaStream_t stream) {
   // m <= 2 per launch; larger m is split into row pairs by the caller.
   const int N = (int)n, K = (int)k;
-#define MGB_GEMV_CASE(F)                                                                      \
-  case F:                                                                                     \
-    return m == 1 ? launch_fmt<F, 1>(w, N, K, x, y, addend, addend_mode, sms, stream)         \
-                  : launch_fmt<F, 2>(w, N, K, x, y, addend, addend_mode, sms, stream);
+#define MGB_GEMV_CASE(F)                                                                       \
+  case F:                                                                                      \
+    return m == 1 ? launch_fmt<F, 1>(w, N, K, x, y, addend, addend_mode, err, sms, stream)     \
+                  : launch_fmt<F, 2>(w, N, K, x, y, addend, addend_mode, err, sms, stream);
   switch (fmt) {
     MGB_GEMV_CASE(Q4_K)
     MGB_GEMV_CASE(Q8_0)
