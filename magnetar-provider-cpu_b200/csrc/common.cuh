@@ -52,21 +52,30 @@ __device__ __forceinline__ float f16_bits_to_f32(uint32_t bits) {
   return __half2float(__ushort_as_half((unsigned short)(bits & 0xffffu)));
 }
 
-// get_scale_min_k4 (src/native/quant.rs:46-57) on the 12 packed scale bytes
-// held as three little-endian words s0 = bytes 0..3, s1 = 4..7, s2 = 8..11.
-__device__ __forceinline__ void scale_min_k4(int j, uint32_t s0, uint32_t s1, uint32_t s2,
-                                             uint32_t &sc, uint32_t &m) {
+// get_scale_min_k4 (src/native/quant.rs:46-57): sub-block j's 6-bit scale and
+// min in a ggml Q4_K super-block's 12 scale bytes `q`.
+__host__ __device__ inline void scale_min_k4_bytes(int j, const uint8_t *q, uint8_t &sc,
+                                                   uint8_t &m) {
   if (j < 4) {
-    sc = (s0 >> (8 * j)) & 63;
-    m = (s1 >> (8 * j)) & 63;
+    sc = q[j] & 63;
+    m = q[j + 4] & 63;
   } else {
-    const int i = j - 4;
-    const uint32_t b8 = (s2 >> (8 * i)) & 0xff;   // q[j + 4]
-    const uint32_t bl = (s0 >> (8 * i)) & 0xff;   // q[j - 4]
-    const uint32_t bh = (s1 >> (8 * i)) & 0xff;   // q[j]
-    sc = (b8 & 0xf) | ((bl >> 6) << 4);
-    m = (b8 >> 4) | ((bh >> 6) << 4);
+    sc = (uint8_t)((q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4));
+    m = (uint8_t)((q[j + 4] >> 4) | ((q[j] >> 6) << 4));
   }
+}
+
+// The device layout's Q4_K header keeps d and dmin (bytes 0..3) and stores the
+// same eight (scale, min) pairs as 16 contiguous 6-bit fields over bytes
+// 4..15: scale j at bits 6j, min j at bits 48 + 6j.  h1, h2, h3 are bytes
+// 4..7, 8..11, 12..15 as little-endian words.  Two shifts per value, the same
+// for every sub-block (no branch on j).
+__device__ __forceinline__ void q4k_scale_min(int j, uint32_t h1, uint32_t h2, uint32_t h3,
+                                              uint32_t &sc, uint32_t &m) {
+  const uint64_t a = ((uint64_t)h2 << 32) | h1;
+  const uint64_t b = ((uint64_t)h3 << 32) | h2;
+  sc = (uint32_t)(a >> (6 * j)) & 63;
+  m = (uint32_t)(b >> (16 + 6 * j)) & 63;
 }
 
 // ---- device error flag -------------------------------------------------------------

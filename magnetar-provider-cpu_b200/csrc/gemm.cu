@@ -6,17 +6,23 @@
 //
 // CTA tile: BM activation rows (1 or 2 accumulators of 128 rows) x BN weight
 // rows (the MMA N, <= 256, a multiple of 16), K in steps of 64 (one 128-byte
-// swizzle atom of bf16).  Warp roles, 320 threads:
-//   warp 0   TMA producer: per K step one or two bf16 activation boxes
-//            (SWIZZLE_128B, straight into the UMMA operand layout) and the
-//            packed W quant and scale boxes (no swizzle), all on full[s].
-//            Owns the TMEM allocation.
-//   warp 1   one thread issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32) per
-//            16-wide K slice and commits each stage to empty[s].
-//   warps 2-9  dequantise the staged packed W into the bf16 B operand
-//            (K-major, SWIZZLE_128B written by hand), fence the async proxy and
-//            arrive on wready[s]; after the last stage they drain TMEM with
-//            tcgen05.ld and write y (+ the optional addend).
+// swizzle atom of bf16).  Two shared-memory rings: the operand ring (A and B
+// tiles, 3-4 stages, released by the MMA) and the packed-W ring (quant and
+// scale boxes, up to 8 stages, released by the dequantising warps), so the
+// packed weights stream from HBM several steps ahead of the tensor core.
+// Warp roles, 352 threads:
+//   warp 0     TMA producer of the bf16 activation boxes (SWIZZLE_128B,
+//              straight into the UMMA operand layout) on a_full[s].  Owns the
+//              TMEM allocation.
+//   warp 1     one thread issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32)
+//              per 16-wide K slice and commits each operand stage to
+//              ab_empty[s].
+//   warp 2     TMA producer of the packed W quant and scale boxes (no
+//              swizzle) on p_full[s].
+//   warps 3-10 dequantise the staged packed W into the bf16 B operand
+//              (K-major, SWIZZLE_128B written by hand), fence the async proxy
+//              and arrive on b_full[s] and p_empty[s]; after the last stage
+//              they drain TMEM with tcgen05.ld and write y (+ the addend).
 // No TMA multicast anywhere: every CTA loads its own tiles from local HBM.
 // Every wait is bounded; on expiry the kernel records ERR_WAIT_TIMEOUT, skips
 // the remaining work, waits (bounded) for its own copies and MMAs, frees TMEM
@@ -33,21 +39,23 @@ namespace mgb {
 namespace {
 
 constexpr int KSTEP = 64;                    // bf16 values per 128-byte row of a stage
-constexpr int DQ_WARPS = 8;                  // warps 2..9: dequantise, then the epilogue
+constexpr int DQ_WARPS = 8;                  // warps 3..10: dequantise, then the epilogue
 constexpr int DQ_THREADS = 32 * DQ_WARPS;
-constexpr int NUM_THREADS = 64 + DQ_THREADS;
+constexpr int NUM_THREADS = 96 + DQ_THREADS;
 
 struct GemmParams {
   int m, n, k;
-  int bn;            // weight rows per CTA (MMA N)
-  int stages;
-  int qbytes;        // packed quant bytes per weight row per K step (32 or 64)
-  uint32_t a_bytes;  // per stage
+  int bn;               // weight rows per CTA (MMA N)
+  int stages;           // operand ring (A and B tiles)
+  int pstages;          // packed-W ring
+  int qbytes;           // packed quant bytes per weight row per K step (32 or 64)
+  uint32_t a_bytes;     // per operand stage
   uint32_t b_bytes;
-  uint32_t wq_bytes;
-  uint32_t ws_bytes;
   uint32_t stage_bytes;
-  uint32_t tx_bytes;  // bytes the TMA boxes of one stage deliver
+  uint32_t wq_bytes;    // per packed stage
+  uint32_t ws_bytes;
+  uint32_t pstage_bytes;
+  uint32_t ptx_bytes;   // bytes the two packed boxes of one step deliver
   int addend_mode;
   const float *addend;
   float *y;
@@ -188,7 +196,7 @@ __device__ __forceinline__ void dequant_run(const uint8_t *wq_row, const uint8_t
     const uint4 h = *reinterpret_cast<const uint4 *>(ws_row);
     const float d = f16_bits_to_f32(h.x), dmin = f16_bits_to_f32(h.x >> 16);
     uint32_t sc, mn;
-    scale_min_k4(sub, h.y, h.z, h.w, sc, mn);
+    q4k_scale_min(sub, h.y, h.z, h.w, sc, mn);
     dq_nib_linear(qs, d * (float)sc, dmin * (float)mn, out);
   } else if (FMT == Q4_0) {
     const uint4 qs = *reinterpret_cast<const uint4 *>(wq_row + j * 16);
@@ -224,14 +232,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   // 1024-byte align the operand area (SWIZZLE_128B atoms).
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  const int S = p.stages;
-  uint8_t *stage0 = smem;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)S * p.stage_bytes);
-  uint64_t *full = bars;              // TMA bytes landed (activation + packed W)
-  uint64_t *wready = bars + S;        // bf16 W operand written (128 arrivals)
-  uint64_t *empty = bars + 2 * S;     // MMA finished reading the stage
-  uint64_t *done = bars + 3 * S;      // all MMAs finished
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * S + 1);
+  const int SA = p.stages, SP = p.pstages;
+  uint8_t *ab0 = smem;                                        // SA x (A tile, B tile)
+  uint8_t *pk0 = smem + (size_t)SA * p.stage_bytes;           // SP x (quant box, scale box)
+  uint64_t *bars = reinterpret_cast<uint64_t *>(pk0 + (size_t)SP * p.pstage_bytes);
+  uint64_t *a_full = bars;                // activation tile landed (TMA bytes)
+  uint64_t *b_full = bars + SA;           // bf16 W operand written (DQ_THREADS arrivals)
+  uint64_t *ab_empty = bars + 2 * SA;     // MMA finished reading the A and B tiles
+  uint64_t *p_full = bars + 3 * SA;       // packed W boxes landed (TMA bytes)
+  uint64_t *p_empty = p_full + SP;        // every dequant warp finished reading them
+  uint64_t *done = p_empty + SP;          // all MMAs finished
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
   int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -241,10 +252,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   constexpr uint32_t TMEM_COLS = SUBS == 2 ? 512 : 256;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&wready[s], DQ_THREADS);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < SA; ++s) {
+      mbar_init(&a_full[s], 1);
+      mbar_init(&b_full[s], DQ_THREADS);
+      mbar_init(&ab_empty[s], 1);
+    }
+    for (int s = 0; s < SP; ++s) {
+      mbar_init(&p_full[s], 1);
+      mbar_init(&p_empty[s], DQ_WARPS);
     }
     mbar_init(done, 1);
     *abort_flag = 0;
@@ -266,45 +281,59 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- activation tiles (TMA, SWIZZLE_128B) ----------------
     if (lane == 0) {
       int issued = 0;
       for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % S;
-        const uint32_t round = kt / S;
-        if (kt >= S && !mbar_wait(&empty[s], (round - 1) & 1, p.err)) {
+        const int s = kt % SA;
+        if (kt >= SA && !mbar_wait(&ab_empty[s], ((kt / SA) - 1) & 1, p.err)) {
           *(volatile int *)abort_flag = 1;
           break;
         }
         if (*(volatile int *)abort_flag) break;
-        uint8_t *st = stage0 + (size_t)s * p.stage_bytes;
-        mbar_arrive_expect_tx(&full[s], p.tx_bytes);
+        uint8_t *st = ab0 + (size_t)s * p.stage_bytes;
+        mbar_arrive_expect_tx(&a_full[s], p.a_bytes);
         for (int sub = 0; sub < SUBS; ++sub)
-          tma_load_2d(st + sub * 16384, &map_a, kt * KSTEP, m0 + sub * 128, &full[s]);
-        tma_load_2d(st + p.a_bytes + p.b_bytes, &map_wq, kt * p.qbytes, n0, &full[s]);
-        tma_load_2d(st + p.a_bytes + p.b_bytes + p.wq_bytes, &map_ws, (kt / 4) * 16, n0, &full[s]);
+          tma_load_2d(st + sub * 16384, &map_a, kt * KSTEP, m0 + sub * 128, &a_full[s]);
         issued = kt + 1;
       }
       // every copy this thread issued has landed before the CTA may exit
-      for (int kt = (issued > S ? issued - S : 0); kt < issued; ++kt)
-        mbar_wait(&full[kt % S], (kt / S) & 1, nullptr);
+      for (int kt = (issued > SA ? issued - SA : 0); kt < issued; ++kt)
+        mbar_wait(&a_full[kt % SA], (kt / SA) & 1, nullptr);
+    }
+  } else if (warp == 2) {
+    // ---------------- packed W boxes, prefetched SP steps ahead ----------------
+    if (lane == 0) {
+      int issued = 0;
+      for (int kt = 0; kt < KT; ++kt) {
+        const int s = kt % SP;
+        if (kt >= SP && !mbar_wait(&p_empty[s], ((kt / SP) - 1) & 1, p.err)) {
+          *(volatile int *)abort_flag = 1;
+          break;
+        }
+        if (*(volatile int *)abort_flag) break;
+        uint8_t *st = pk0 + (size_t)s * p.pstage_bytes;
+        mbar_arrive_expect_tx(&p_full[s], p.ptx_bytes);
+        tma_load_2d(st, &map_wq, kt * p.qbytes, n0, &p_full[s]);
+        tma_load_2d(st + p.wq_bytes, &map_ws, (kt / 4) * 16, n0, &p_full[s]);
+        issued = kt + 1;
+      }
+      for (int kt = (issued > SP ? issued - SP : 0); kt < issued; ++kt)
+        mbar_wait(&p_full[kt % SP], (kt / SP) & 1, nullptr);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc = instr_desc_bf16(128, p.bn);
-      bool ok = true;
-      int committed = 0;
-      for (int kt = 0; kt < KT && ok; ++kt) {
-        const int s = kt % S;
-        const uint32_t ph = (kt / S) & 1;
-        if (!mbar_wait(&full[s], ph, p.err) || !mbar_wait(&wready[s], ph, p.err)) {
-          ok = false;
+      for (int kt = 0; kt < KT; ++kt) {
+        const int s = kt % SA;
+        const uint32_t ph = (kt / SA) & 1;
+        if (!mbar_wait(&a_full[s], ph, p.err) || !mbar_wait(&b_full[s], ph, p.err)) {
           *(volatile int *)abort_flag = 1;
           break;
         }
         tc_fence_after();
-        uint8_t *st = stage0 + (size_t)s * p.stage_bytes;
+        uint8_t *st = ab0 + (size_t)s * p.stage_bytes;
         const uint32_t a_addr = smem_u32(st), b_addr = smem_u32(st + p.a_bytes);
 #pragma unroll
         for (int sub = 0; sub < SUBS; ++sub)
@@ -312,15 +341,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int kk = 0; kk < KSTEP / 16; ++kk)
             mma_bf16(tmem_base + sub * 256, smem_desc_sw128(a_addr + sub * 16384 + kk * 32),
                      smem_desc_sw128(b_addr + kk * 32), idesc, (kt | kk) != 0);
-        mma_commit(&empty[s]);
-        committed = kt + 1;
+        mma_commit(&ab_empty[s]);
       }
       mma_commit(done);  // arrives once every MMA issued above has completed
-      (void)committed;
     }
   } else {
     // ---------------- dequantise W, then the epilogue ----------------
-    const int t = threadIdx.x - 64;  // 0..DQ_THREADS-1
+    const int t = threadIdx.x - 96;  // 0..DQ_THREADS-1
     uint32_t lut[4] = {0, 0, 0, 0};
     if (FMT == IQ4_NL) {
 #pragma unroll
@@ -332,19 +359,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
     const int items = p.bn * 2;  // (weight row, run) pairs per stage
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % S;
-      const uint32_t ph = (kt / S) & 1;
+    bool ok = true;
+    for (int kt = 0; kt < KT && ok; ++kt) {
+      const int s = kt % SA, sp = kt % SP;
       if (*(volatile int *)abort_flag) break;
-      // this stage's B slot is free once the MMA of round (kt / S) - 1 released it
-      if ((kt >= S && !mbar_wait(&empty[s], ((kt / S) - 1) & 1, p.err)) ||
-          !mbar_wait(&full[s], ph, p.err)) {
+      // the B slot is free once the MMA of round (kt / SA) - 1 released it, and
+      // the packed boxes of this step have landed
+      ok = (kt < SA || mbar_wait(&ab_empty[s], ((kt / SA) - 1) & 1, p.err)) &&
+           mbar_wait(&p_full[sp], (kt / SP) & 1, p.err);
+      if (!ok) {
         *(volatile int *)abort_flag = 1;
         break;
       }
-      uint8_t *st = stage0 + (size_t)s * p.stage_bytes;
-      uint8_t *bt = st + p.a_bytes;
-      const uint8_t *wq = st + p.a_bytes + p.b_bytes;
+      uint8_t *bt = ab0 + (size_t)s * p.stage_bytes + p.a_bytes;
+      const uint8_t *wq = pk0 + (size_t)sp * p.pstage_bytes;
       const uint8_t *ws = wq + p.wq_bytes;
       for (int it = t; it < items; it += DQ_THREADS) {
         const int row = it >> 1, j = it & 1;
@@ -358,7 +386,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
       fence_proxy_async_smem();
-      mbar_arrive(&wready[s]);
+      mbar_arrive(&b_full[s]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_empty[sp]);
     }
     // epilogue: TMEM lanes of this warp's quarter -> y rows; the two warps of
     // a quarter take alternate 8-column chunks
@@ -367,7 +397,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // tcgen05.ld is warp-collective: the whole warp drains TMEM or none of it
     if (__all_sync(0xffffffffu, finished && !*(volatile int *)abort_flag)) {
       const int quarter = warp & 3;
-      const int half = (warp - 2) / 4;
+      const int half = (warp - 3) / 4;
       for (int sub = 0; sub < SUBS; ++sub) {
         const int row = m0 + sub * 128 + quarter * 32 + lane;
         for (int c = 8 * half; c < p.bn; c += 16) {
@@ -376,13 +406,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (row < p.m) {
             const int col = n0 + c;
             float *yr = p.y + (size_t)row * p.n;
+            if (col + 8 <= p.n && p.addend_mode == 0 && (p.n & 3) == 0) {
+              reinterpret_cast<float4 *>(yr + col)[0] = make_float4(v[0], v[1], v[2], v[3]);
+              reinterpret_cast<float4 *>(yr + col)[1] = make_float4(v[4], v[5], v[6], v[7]);
+            } else {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              if (col + e < p.n) {
-                float o = v[e];
-                if (p.addend_mode == 1) o = o + p.addend[col + e];
-                else if (p.addend_mode == 2) o = o + p.addend[(size_t)row * p.n + col + e];
-                yr[col + e] = o;
+              for (int e = 0; e < 8; ++e) {
+                if (col + e < p.n) {
+                  float o = v[e];
+                  if (p.addend_mode == 1) o = o + p.addend[col + e];
+                  else if (p.addend_mode == 2) o = o + p.addend[(size_t)row * p.n + col + e];
+                  yr[col + e] = o;
+                }
               }
             }
           }
@@ -429,8 +464,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-bool make_map_2d(CUtensorMap *map, CUtensorMapDataType dtype, int elem_bytes, const void *base,
-                 uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+bool make_map_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t inner,
+                 uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
                  uint32_t box_outer, CUtensorMapSwizzle swizzle) {
   auto fn = encode_fn();
   if (!fn) return false;
@@ -438,14 +473,13 @@ bool make_map_2d(CUtensorMap *map, CUtensorMapDataType dtype, int elem_bytes, co
   cuuint64_t strides[1] = {row_stride_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  (void)elem_bytes;
   return fn(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 struct TileChoice {
-  int subs, bn, stages;
+  int subs, bn;
 };
 
 TileChoice choose_tiles(uint64_t m, uint64_t n, int sms) {
@@ -457,7 +491,6 @@ TileChoice choose_tiles(uint64_t m, uint64_t n, int sms) {
   if (bn < 32) bn = 32;
   if (bn > 256) bn = 256;
   t.bn = (int)bn;
-  t.stages = 0;
   return t;
 }
 
@@ -495,7 +528,7 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
       (reinterpret_cast<uintptr_t>(xb) & 15))
     return cudaErrorInvalidValue;
   const Layout L(fmt, n, k);
-  TileChoice t = choose_tiles(m, n, sms);
+  const TileChoice t = choose_tiles(m, n, sms);
   GemmParams p;
   p.m = (int)m;
   p.n = (int)n;
@@ -503,34 +536,41 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
   p.bn = t.bn;
   p.qbytes = fmt == Q8_0 ? 64 : 32;
   p.a_bytes = 16384u * t.subs;
-  p.b_bytes = (uint32_t)t.bn * 128u;
+  p.b_bytes = (uint32_t)ceil_div((uint64_t)t.bn * 128u, 1024) * 1024;
+  p.stage_bytes = p.a_bytes + p.b_bytes;
   p.wq_bytes = (uint32_t)ceil_div((uint64_t)t.bn * p.qbytes, 1024) * 1024;
   p.ws_bytes = (uint32_t)ceil_div((uint64_t)t.bn * 16, 1024) * 1024;
-  p.stage_bytes = p.a_bytes + (uint32_t)ceil_div(p.b_bytes, 1024) * 1024 + p.wq_bytes + p.ws_bytes;
-  // b_bytes region rounded to 1024 so the packed boxes stay 1024-aligned
-  p.b_bytes = (uint32_t)ceil_div(p.b_bytes, 1024) * 1024;
-  p.tx_bytes = p.a_bytes + (uint32_t)t.bn * (uint32_t)p.qbytes + (uint32_t)t.bn * 16u;
-  const uint32_t budget = 220 * 1024;
-  int stages = (int)((budget - 1024 - 256) / p.stage_bytes);
-  if (stages > 6) stages = 6;
-  if (stages < 2) return cudaErrorInvalidValue;
-  p.stages = stages;
+  p.pstage_bytes = p.wq_bytes + p.ws_bytes;
+  p.ptx_bytes = (uint32_t)t.bn * (uint32_t)p.qbytes + (uint32_t)t.bn * 16u;
+  // operand ring first (3 or 4 stages), the rest of the budget for the packed ring
+  const uint32_t budget = 225 * 1024 - 1024 /*align slack*/ - 512 /*barriers*/;
+  int sa = p.stage_bytes * 4 + p.pstage_bytes * 4 <= budget ? 4 : 3;
+  int sp = (int)((budget - sa * p.stage_bytes) / p.pstage_bytes);
+  if (sp > 8) sp = 8;
+  if (sp < 2) {
+    sa = 2;
+    sp = (int)((budget - sa * p.stage_bytes) / p.pstage_bytes);
+    if (sp > 8) sp = 8;
+  }
+  if (sp < 2) return cudaErrorInvalidValue;
+  p.stages = sa;
+  p.pstages = sp;
   p.addend_mode = addend_mode;
   p.addend = addend;
   p.y = y;
   p.err = err;
 
   CUtensorMap map_a, map_wq, map_ws;
-  if (!make_map_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xb, k, m, k * 2, KSTEP, 128,
+  if (!make_map_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xb, k, m, k * 2, KSTEP, 128,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map_2d(&map_wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, L.qs_row, n, L.qs_row,
+      !make_map_2d(&map_wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, L.qs_row, n, L.qs_row,
                    (uint32_t)p.qbytes, (uint32_t)t.bn, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_map_2d(&map_ws, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1,
+      !make_map_2d(&map_ws, CU_TENSOR_MAP_DATA_TYPE_UINT8,
                    static_cast<const uint8_t *>(w) + L.qs_bytes, L.sc_row, n, L.sc_row, 16,
                    (uint32_t)t.bn, CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
 
-  const size_t smem = (size_t)stages * p.stage_bytes + 1024 /*align slack*/ + 256 /*barriers*/;
+  const size_t smem = (size_t)sa * p.stage_bytes + (size_t)sp * p.pstage_bytes + 1024 + 512;
   dim3 grid((unsigned)ceil_div(n, (uint64_t)t.bn), (unsigned)ceil_div(m, 128ull * t.subs));
   cudaError_t e = cudaSuccess;
 #define MGB_GEMM_LAUNCH(F, SUBS)                                                               \

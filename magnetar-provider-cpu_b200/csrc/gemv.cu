@@ -1,8 +1,7 @@
 // Decode GEMV for packed weights on sm_100a: y[m, n] = x[m, k] * W^T for
-// m <= 2 activation rows, f32 activations, f32 accumulation.
-// Replaces the reference's `columns_q4k_avx2` / `columns_avx2` /
-// `columns_iq4nl_avx2` (src/native/quant.rs:604-744, :1438-1483) with the f32
-// semantics of its scalar path (:559-597).
+// m <= 2 activation rows.  Replaces the reference's `columns_q4k_avx2` /
+// `columns_avx2` / `columns_iq4nl_avx2` (src/native/quant.rs:604-744,
+// :1438-1483) at the accuracy of its f32 path (:559-597).
 //
 // Main kernel (k % 256 == 0), persistent and bulk-copy staged:
 //   warp 0      one thread streams the CTA's rows of both planes of W (the
@@ -11,22 +10,21 @@
 //               ring of shared-memory stages, starting before anything else:
 //               the bytes in flight cost no registers.
 //   warps 1..   consumer teams of ceil(k / 1024) warps; thread u of a team owns
-//               run u of K (32 values) for the whole kernel, its activations
-//               in registers, and reads its 16 (Q8_0: 32) quant bytes of each
-//               staged row from shared memory.  Per row the team reduces its
-//               partial sums with shuffles and a fixed-order pass over its
-//               warps (deterministic), and one thread writes y.
-// Programmatic dependent launch: the producer starts streaming weights
-// immediately (they never depend on an earlier kernel); consumers execute
+//               run u of K (32 values) for the whole kernel and reads its 16
+//               (Q8_0: 32) quant bytes of each staged row from shared memory.
+//               Per row the team reduces its partial sums with shuffles and a
+//               fixed-order pass over its warps (deterministic).
+// Programmatic dependent launch: the producer starts streaming weights at
+// once (they never depend on an earlier kernel); consumers execute
 // griddepcontrol.wait before reading x or writing y.
 //
-// Quant -> f32 without integer-to-float conversions:
-//   4-bit q: prmt places q in bits 16..19 of 0x3F000000, the float
-//            0.5 + q/256.  With t = sum((0.5 + q/256) x) and X = sum(x) over
-//            the run (computed once per thread), sum(q x) = 256 t - 128 X.
-//   8-bit q: prmt places (q + 128) in the low byte of 0x4B000000, the float
-//            2^23 + q + 128; subtracting 2^23 + 128 is exact.
-// Products accumulate with the packed fma.rn.f32x2 (two values per issue).
+// Arithmetic: each thread holds its run of x as 16-bit integers
+// x ~= dx * v, dx = max|x| / 32767 over the run (|error| <= dx / 2, i.e.
+// <= 2^-16 of the run's largest value), split into a signed high byte and an
+// unsigned low byte.  Integer dot products with the quants (dp4a, exact,
+// int32) give sum(q v) = 256 sum(q hi) + sum(q lo); the run then contributes
+// dx * scale * sum(q v) - min * sum(x) in f32, sum(x) taken from the exact f32
+// values.  Relative error ~1e-5, against the 1e-3 tolerance of the GEMV.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -57,55 +55,94 @@ __device__ __forceinline__ void named_barrier(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-// 0.5 + q/256 for the 4-bit value in byte i of `v` (bits 0..3 of that byte).
-__device__ __forceinline__ float nib_f(uint32_t v, int i) {
-  return __uint_as_float(__byte_perm(v, 0x3F000000u, 0x7054u | ((uint32_t)i << 8)));
+// Four-way byte dot products, accumulating into c (dp4a; u = unsigned bytes,
+// s = signed bytes; first operand a, second b).
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
 }
 
-// 2^23 + b for byte i of `v`.
-__device__ __forceinline__ float byte_f(uint32_t v, int i) {
-  return __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7650u | (uint32_t)i));
-}
+// One thread's run of one activation row as 16-bit integers: dx, the exact
+// f32 sum, and the high / low bytes packed four to a word in the order the
+// format's quant words use (pair order for the linear 4-bit formats: word 2w
+// holds values 8w+0,2,4,6 and word 2w+1 values 8w+1,3,5,7; value order
+// otherwise).
+struct XRun {
+  float dx, sum;
+  uint32_t hi[8], lo[8];
+};
 
-// sum over a 32-value run of (0.5 + q/256) * x for 4-bit quants stored as
-// nibble pairs (byte i = values 2i, 2i+1).
-__device__ __forceinline__ float dot_nib_run(const uint4 &qs, const float *xr) {
-  const uint32_t words[4] = {qs.x, qs.y, qs.z, qs.w};
-  float2 acc = make_float2(0.f, 0.f);
+__device__ __forceinline__ void pack_run(const float (&v)[32], bool pair_order, XRun &r) {
+  float amax = 0.f, s = 0.f;
 #pragma unroll
-  for (int wd = 0; wd < 4; ++wd) {
-    const uint32_t lo = words[wd] & 0x0F0F0F0Fu;
-    const uint32_t hi = (words[wd] >> 4) & 0x0F0F0F0Fu;
+  for (int i = 0; i < 32; i += 4) s += (v[i] + v[i + 1]) + (v[i + 2] + v[i + 3]);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 q = make_float2(nib_f(lo, i), nib_f(hi, i));
-      const float2 xv = make_float2(xr[8 * wd + 2 * i], xr[8 * wd + 2 * i + 1]);
-      acc = __ffma2_rn(q, xv, acc);
-    }
-  }
-  return acc.x + acc.y;
-}
-
-// sum over a run of b * x for the +128-biased bytes of 8 words (byte order =
-// value order).
-__device__ __forceinline__ float dot_byte_words(const uint32_t *u, const float *xr) {
-  const float2 bias = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
-  float2 acc = make_float2(0.f, 0.f);
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  r.sum = s;
+  r.dx = amax / 32767.f;
+  const float inv = amax > 0.f ? 32767.f / amax : 0.f;
 #pragma unroll
   for (int wd = 0; wd < 8; ++wd) {
+    uint32_t h = 0, l = 0;
 #pragma unroll
-    for (int i = 0; i < 4; i += 2) {
-      float2 q = make_float2(byte_f(u[wd], i), byte_f(u[wd], i + 1));
-      q = __fadd2_rn(q, bias);
-      const float2 xv = make_float2(xr[4 * wd + i], xr[4 * wd + i + 1]);
-      acc = __ffma2_rn(q, xv, acc);
+    for (int b = 0; b < 4; ++b) {
+      // pair order: word 2w -> values 8w + 2b, word 2w + 1 -> values 8w + 2b + 1
+      const int e = pair_order ? 8 * (wd / 2) + 2 * b + (wd & 1) : 4 * wd + b;
+      int q = __float2int_rn(v[e] * inv);
+      q = max(-32767, min(32767, q));
+      h |= (uint32_t)((q >> 8) & 0xff) << (8 * b);
+      l |= (uint32_t)(q & 0xff) << (8 * b);
     }
+    r.hi[wd] = h;
+    r.lo[wd] = l;
   }
-  return acc.x + acc.y;
+}
+
+// sum(q v) for a run of 4-bit quants in nibble pairs (byte i = values 2i, 2i+1).
+__device__ __forceinline__ int dot_nib(const uint4 &qs, const XRun &x) {
+  const uint32_t words[4] = {qs.x, qs.y, qs.z, qs.w};
+  int sh = 0, sl = 0;
+#pragma unroll
+  for (int wd = 0; wd < 4; ++wd) {
+    const uint32_t ev = words[wd] & 0x0F0F0F0Fu;         // values 8wd + 0, 2, 4, 6
+    const uint32_t od = (words[wd] >> 4) & 0x0F0F0F0Fu;  // values 8wd + 1, 3, 5, 7
+    sh = dp4a_us(ev, x.hi[2 * wd], sh);
+    sh = dp4a_us(od, x.hi[2 * wd + 1], sh);
+    sl = dp4a_uu(ev, x.lo[2 * wd], sl);
+    sl = dp4a_uu(od, x.lo[2 * wd + 1], sl);
+  }
+  return sh * 256 + sl;
+}
+
+// sum(q v) for a run of signed byte quants in value order.
+__device__ __forceinline__ int dot_s8(const uint32_t (&q)[8], const XRun &x) {
+  int sh = 0, sl = 0;
+#pragma unroll
+  for (int wd = 0; wd < 8; ++wd) {
+    sh = dp4a_ss(q[wd], x.hi[wd], sh);
+    sl = dp4a_su(q[wd], x.lo[wd], sl);
+  }
+  return sh * 256 + sl;
 }
 
 // IQ4_NL codebook lookup: the 8 indices of word `v` (nibble order = value
-// order) -> two words of codebook values biased by +128 (u8).
+// order) -> two words of signed codebook bytes.
 __device__ __forceinline__ void iq4_lookup(uint32_t v, const uint32_t t[4], uint32_t &o0,
                                            uint32_t &o1) {
 #pragma unroll
@@ -114,8 +151,7 @@ __device__ __forceinline__ void iq4_lookup(uint32_t v, const uint32_t t[4], uint
     const uint32_t sel = s & 0x7777u;
     const uint32_t low = __byte_perm(t[0], t[1], sel);
     const uint32_t high = __byte_perm(t[2], t[3], sel);
-    const uint32_t pick = 0x3210u | ((s & 0x8888u) >> 1);
-    const uint32_t r = __byte_perm(low, high, pick);
+    const uint32_t r = __byte_perm(low, high, 0x3210u | ((s & 0x8888u) >> 1));
     if (h == 0) o0 = r; else o1 = r;
   }
 }
@@ -125,80 +161,84 @@ __device__ __forceinline__ void iq4_table(uint32_t lut[4]) {
   for (int i = 0; i < 4; ++i) {
     uint32_t v = 0;
 #pragma unroll
-    for (int b = 0; b < 4; ++b) v |= (uint32_t)((iq4nl_value(4 * i + b) + 128) & 0xff) << (8 * b);
+    for (int b = 0; b < 4; ++b) v |= (uint32_t)(iq4nl_value(4 * i + b) & 0xff) << (8 * b);
     lut[i] = v;
   }
 }
 
-// The partial dot products of one run of one row with MR activation rows.
-// qa (and qb for Q8_0) hold the run's quant bytes; hd the Q4_K header of its
-// super-block; dh the f16 scale of the other formats; j the run's index in
-// its super-block.
+// The partial dot products of one run of one weight row with MR activation
+// rows.  qa (and qb for Q8_0) hold the run's quant bytes; hd the Q4_K header
+// of its super-block; dh the f16 scale of the other formats; j the run's index
+// in its super-block.
 template <int FMT, int MR>
 __device__ __forceinline__ void run_partials(const uint4 &qa, const uint4 &qb, const uint4 &hd,
-                                             uint32_t dh, int j, const float (&xr)[MR][32],
-                                             const float (&X)[MR], const uint32_t lut[4],
-                                             float (&part)[MR]) {
+                                             uint32_t dh, int j, const XRun (&x)[MR],
+                                             const uint32_t lut[4], float (&part)[MR]) {
   if (FMT == Q4_K) {
     const float d = f16_bits_to_f32(hd.x), dmin = f16_bits_to_f32(hd.x >> 16);
     uint32_t sc, mn;
-    scale_min_k4(j, hd.y, hd.z, hd.w, sc, mn);
+    q4k_scale_min(j, hd.y, hd.z, hd.w, sc, mn);
     const float s = d * (float)sc, mv = dmin * (float)mn;
 #pragma unroll
-    for (int m = 0; m < MR; ++m) {
-      const float t = dot_nib_run(qa, xr[m]);
-      part[m] = (256.f * s) * t - (128.f * s + mv) * X[m];
-    }
+    for (int m = 0; m < MR; ++m)
+      part[m] = (s * x[m].dx) * (float)dot_nib(qa, x[m]) - mv * x[m].sum;
   } else if (FMT == Q4_0) {
     const float d = f16_bits_to_f32(dh);
 #pragma unroll
-    for (int m = 0; m < MR; ++m) {
-      const float t = dot_nib_run(qa, xr[m]);
-      part[m] = d * (256.f * t - 136.f * X[m]);
-    }
+    for (int m = 0; m < MR; ++m)
+      part[m] = d * (x[m].dx * (float)dot_nib(qa, x[m]) - 8.f * x[m].sum);
   } else if (FMT == Q8_0) {
     const float d = f16_bits_to_f32(dh);
-    const uint32_t ub[8] = {qa.x ^ 0x80808080u, qa.y ^ 0x80808080u, qa.z ^ 0x80808080u,
-                            qa.w ^ 0x80808080u, qb.x ^ 0x80808080u, qb.y ^ 0x80808080u,
-                            qb.z ^ 0x80808080u, qb.w ^ 0x80808080u};
+    const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-    for (int m = 0; m < MR; ++m) part[m] = d * dot_byte_words(ub, xr[m]);
+    for (int m = 0; m < MR; ++m) part[m] = (d * x[m].dx) * (float)dot_s8(q, x[m]);
   } else {  // IQ4_NL
     const float d = f16_bits_to_f32(dh);
-    uint32_t ub[8];
+    uint32_t q[8];
     const uint32_t words[4] = {qa.x, qa.y, qa.z, qa.w};
 #pragma unroll
-    for (int wd = 0; wd < 4; ++wd) iq4_lookup(words[wd], lut, ub[2 * wd], ub[2 * wd + 1]);
+    for (int wd = 0; wd < 4; ++wd) iq4_lookup(words[wd], lut, q[2 * wd], q[2 * wd + 1]);
 #pragma unroll
-    for (int m = 0; m < MR; ++m) part[m] = d * dot_byte_words(ub, xr[m]);
+    for (int m = 0; m < MR; ++m) part[m] = (d * x[m].dx) * (float)dot_s8(q, x[m]);
   }
 }
 
-template <int MR>
+template <int FMT, int MR>
 __device__ __forceinline__ void load_x(const float *__restrict__ x, int k, int u, bool active,
-                                       float (&xr)[MR][32], float (&X)[MR]) {
+                                       XRun (&xr)[MR]) {
+  constexpr bool pair = FMT == Q4_K || FMT == Q4_0;
 #pragma unroll
   for (int m = 0; m < MR; ++m) {
-    X[m] = 0.f;
+    float v[32];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (active) v = __ldg(reinterpret_cast<const float4 *>(x + (size_t)m * k + (size_t)u * 32) + i);
-      xr[m][4 * i] = v.x;
-      xr[m][4 * i + 1] = v.y;
-      xr[m][4 * i + 2] = v.z;
-      xr[m][4 * i + 3] = v.w;
-      X[m] += (v.x + v.y) + (v.z + v.w);
+      float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (active) f = __ldg(reinterpret_cast<const float4 *>(x + (size_t)m * k + (size_t)u * 32) + i);
+      v[4 * i] = f.x;
+      v[4 * i + 1] = f.y;
+      v[4 * i + 2] = f.z;
+      v[4 * i + 3] = f.w;
     }
+    pack_run(v, pair, xr[m]);
   }
+}
+
+// Sums RPT*MR per-lane values over the warp; lane 0 ends with all of them.
+template <int NV>
+__device__ __forceinline__ void warp_sum(float (&v)[NV]) {
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v[i] += __shfl_xor_sync(0xffffffffu, v[i], off);
 }
 
 // ---- main kernel: bulk-copy staged, persistent ----------------------------------------
 
+constexpr int RPT = 4;  // rows per team per stage
+
 struct GemvStaged {
   int n, k;
   int teams, team_warps;  // consumer geometry
-  int rows_per_team;      // rows per team per stage
   int stages;
   int rows_per_cta;
   uint32_t stage_bytes, qs_stage_bytes;
@@ -215,7 +255,7 @@ __global__ void __launch_bounds__(MAXT, 1)
   extern __shared__ __align__(128) uint8_t smem[];
   const Layout L(FMT, (uint64_t)p.n, (uint64_t)p.k);
   const int S = p.stages;
-  const int TR = p.teams * p.rows_per_team;  // rows per stage
+  const int TR = p.teams * RPT;  // rows per stage
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * p.stage_bytes);
   uint64_t *empty = full + S;
   float *red = reinterpret_cast<float *>(empty + S);  // [2][teams][team_warps][RPT*MR]
@@ -264,31 +304,32 @@ __global__ void __launch_bounds__(MAXT, 1)
   const int runs = p.k / RUN;
   const bool active = u < runs;
   const int team_threads = p.team_warps * 32;
-  const int RPT = p.rows_per_team;
 
   grid_dependency_wait();  // x may be the previous kernel's output
-  float xr[MR][32];
-  float X[MR];
-  load_x<MR>(x, p.k, u, active, xr, X);
+  XRun xr[MR];
+  load_x<FMT, MR>(x, p.k, u, active, xr);
   uint32_t lut[4] = {0, 0, 0, 0};
   if (FMT == IQ4_NL) iq4_table(lut);
 
-  constexpr int MAX_RPT = 4;
   // A wait that gives up records the error and the thread stops waiting, but
   // it keeps stepping through every stage so its team's named barriers match.
   bool ok = true;
   for (int g = 0; g < nstages; ++g) {
     const int s = g % S;
-    ok = ok && mbar_wait(&full[s], (g / S) & 1, p.err);
+    // lane 0 polls; once the phase is complete every lane's own try_wait
+    // succeeds at once and acquires the bulk-copied bytes for that lane
+    if (lane == 0) ok = ok && mbar_wait(&full[s], (g / S) & 1, p.err);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (ok) ok = mbar_try_wait(&full[s], (g / S) & 1);
     const uint8_t *st = smem + (size_t)s * p.stage_bytes;
     const int row0 = r0 + g * TR;
-    float part[MAX_RPT][MR];
+    float part[RPT * MR];
 #pragma unroll
-    for (int i = 0; i < MAX_RPT; ++i) {
+    for (int i = 0; i < RPT; ++i) {
 #pragma unroll
-      for (int m = 0; m < MR; ++m) part[i][m] = 0.f;
+      for (int m = 0; m < MR; ++m) part[i * MR + m] = 0.f;
       const int lr = team * RPT + i;  // row within the stage
-      if (ok && i < RPT && active && row0 + lr < r1) {
+      if (ok && active && row0 + lr < r1) {
         const uint8_t *qrow = st + (size_t)lr * L.qs_row;
         const uint8_t *srow = st + p.qs_stage_bytes + (size_t)lr * L.sc_row;
         uint4 qa, qb = make_uint4(0, 0, 0, 0), hd = make_uint4(0, 0, 0, 0);
@@ -302,24 +343,18 @@ __global__ void __launch_bounds__(MAXT, 1)
         if (FMT == Q4_K) hd = *reinterpret_cast<const uint4 *>(srow + (u >> 3) * 16);
         else dh = *reinterpret_cast<const uint16_t *>(srow + u * 2);
         float pm[MR];
-        run_partials<FMT, MR>(qa, qb, hd, dh, u & 7, xr, X, lut, pm);
+        run_partials<FMT, MR>(qa, qb, hd, dh, u & 7, xr, lut, pm);
 #pragma unroll
-        for (int m = 0; m < MR; ++m) part[i][m] = pm[m];
+        for (int m = 0; m < MR; ++m) part[i * MR + m] = pm[m];
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the stage's bytes
-    float *rb = red + ((size_t)(g & 1) * p.teams + team) * p.team_warps * (MAX_RPT * MR);
+    float *rb = red + ((size_t)(g & 1) * p.teams + team) * p.team_warps * (RPT * MR);
+    warp_sum<RPT * MR>(part);
+    if (lane == 0)
 #pragma unroll
-    for (int i = 0; i < MAX_RPT; ++i)
-#pragma unroll
-      for (int m = 0; m < MR; ++m) {
-        if (i >= RPT) continue;
-        float v = part[i][m];
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        if (lane == 0) rb[tw * (MAX_RPT * MR) + i * MR + m] = v;
-      }
+      for (int i = 0; i < RPT * MR; ++i) rb[tw * (RPT * MR) + i] = part[i];
     named_barrier(1 + team, team_threads);
     const int t = tw * 32 + lane;
     if (t < RPT * MR) {
@@ -327,7 +362,7 @@ __global__ void __launch_bounds__(MAXT, 1)
       const int row = row0 + team * RPT + i;
       if (row < r1) {
         float sum = 0.f;
-        for (int wi = 0; wi < p.team_warps; ++wi) sum += rb[wi * (MAX_RPT * MR) + i * MR + m];
+        for (int wi = 0; wi < p.team_warps; ++wi) sum += rb[wi * (RPT * MR) + t];
         if (p.addend_mode == 1) sum = sum + p.addend[row];
         else if (p.addend_mode == 2) sum = sum + p.addend[(size_t)m * p.n + row];
         p.y[(size_t)m * p.n + row] = sum;
@@ -350,9 +385,8 @@ __global__ void __launch_bounds__(MAXT, 1)
   const bool active = u < runs;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
-  float xr[MR][32];
-  float X[MR];
-  load_x<MR>(x, k, u, active, xr, X);
+  XRun xr[MR];
+  load_x<FMT, MR>(x, k, u, active, xr);
   uint32_t lut[4] = {0, 0, 0, 0};
   if (FMT == IQ4_NL) iq4_table(lut);
   const int r0 = blockIdx.x * rows_per_cta;
@@ -360,12 +394,12 @@ __global__ void __launch_bounds__(MAXT, 1)
   const uint8_t *scale_plane = w + L.qs_bytes;
   int buf = 0;
   for (int r = r0; r < r1; r += R) {
-    float part[R][MR];
+    float part[R * MR];
 #pragma unroll
     for (int i = 0; i < R; ++i) {
       const int row = r + i;
 #pragma unroll
-      for (int m = 0; m < MR; ++m) part[i][m] = 0.f;
+      for (int m = 0; m < MR; ++m) part[i * MR + m] = 0.f;
       if (active && row < r1) {
         const uint8_t *qrow = w + (size_t)row * L.qs_row;
         const uint8_t *srow = scale_plane + (size_t)row * L.sc_row;
@@ -380,20 +414,15 @@ __global__ void __launch_bounds__(MAXT, 1)
         if (FMT == Q4_K) hd = __ldg(reinterpret_cast<const uint4 *>(srow + (size_t)(u >> 3) * 16));
         else dh = ld_nc_u16(srow + (size_t)u * 2);
         float pm[MR];
-        run_partials<FMT, MR>(qa, qb, hd, dh, u & 7, xr, X, lut, pm);
+        run_partials<FMT, MR>(qa, qb, hd, dh, u & 7, xr, lut, pm);
 #pragma unroll
-        for (int m = 0; m < MR; ++m) part[i][m] = pm[m];
+        for (int m = 0; m < MR; ++m) part[i * MR + m] = pm[m];
       }
     }
+    warp_sum<R * MR>(part);
+    if (lane == 0)
 #pragma unroll
-    for (int i = 0; i < R; ++i)
-#pragma unroll
-      for (int m = 0; m < MR; ++m) {
-        float v = part[i][m];
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        if (lane == 0) red[buf][warp][i * MR + m] = v;
-      }
+      for (int i = 0; i < R * MR; ++i) red[buf][warp][i] = part[i];
     __syncthreads();
     if (threadIdx.x < R * MR) {
       const int i = threadIdx.x / MR, m = threadIdx.x % MR;
@@ -422,8 +451,7 @@ static cudaError_t launch_staged(const void *w, int n, int k, const float *x, fl
   p.k = k;
   p.team_warps = (k / RUN + 31) / 32;
   p.teams = p.team_warps >= 8 ? 1 : 8 / p.team_warps;
-  p.rows_per_team = 2;
-  const int TR = p.teams * p.rows_per_team;
+  const int TR = p.teams * RPT;
   p.qs_stage_bytes = (uint32_t)ceil_div((uint64_t)TR * L.qs_row, 128) * 128;
   p.stage_bytes = p.qs_stage_bytes + (uint32_t)ceil_div((uint64_t)TR * L.sc_row, 128) * 128;
   const uint32_t budget = 96 * 1024;
@@ -431,13 +459,13 @@ static cudaError_t launch_staged(const void *w, int n, int k, const float *x, fl
   if (stages > 8) stages = 8;
   if (stages < 2) stages = 2;
   p.stages = stages;
-  // two CTAs per SM when they fit (so a dependent launch can overlap), rows split evenly
+  // two CTAs per SM when they fit (so a dependent launch can overlap), rows split evenly;
+  // a CTA's last stage may hold fewer than TR rows
   const int threads = 32 * (1 + p.teams * p.team_warps);
   const int per_sm = threads <= 512 ? 2 : 1;
   const int units = (int)ceil_div((uint64_t)n, (uint64_t)TR);
   int grid = sms * per_sm;
   if (grid > units) grid = units;
-  // rows split evenly; a CTA's last stage may hold fewer than TR rows
   p.rows_per_cta = (int)ceil_div((uint64_t)n, (uint64_t)grid);
   grid = (int)ceil_div((uint64_t)n, (uint64_t)p.rows_per_cta);
   p.addend_mode = addend_mode;
@@ -445,7 +473,7 @@ static cudaError_t launch_staged(const void *w, int n, int k, const float *x, fl
   p.y = y;
   p.err = err;
   const size_t smem = (size_t)stages * p.stage_bytes + 2 * 8 * (size_t)stages +
-                      2 * sizeof(float) * (size_t)p.teams * p.team_warps * 4 * MR;
+                      2 * sizeof(float) * (size_t)p.teams * p.team_warps * RPT * MR;
   auto kern = gemv_staged_kernel<FMT, MR, MAXT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;

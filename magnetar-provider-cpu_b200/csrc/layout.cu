@@ -41,8 +41,26 @@ __global__ void repack_kernel(int fmt, const uint8_t *__restrict__ src, uint64_t
         words[w] = v;
       }
       *reinterpret_cast<uint4 *>(qs + u * 16) = make_uint4(words[0], words[1], words[2], words[3]);
-      if (j == 0)
-        for (int i = 0; i < 16; ++i) sc[b * 16 + i] = blk[i];
+      if (j == 0) {
+        // header: d, dmin as they are; the eight 6-bit (scale, min) pairs of
+        // get_scale_min_k4 rearranged as 16 contiguous 6-bit fields
+        for (int i = 0; i < 4; ++i) sc[b * 16 + i] = blk[i];
+        uint64_t lo = 0, hi = 0;  // bits 0..63 and 64..95 of the 96-bit field array
+        for (int jj = 0; jj < 8; ++jj) {
+          uint8_t s, m;
+          scale_min_k4_bytes(jj, blk + 4, s, m);
+          const int bs = 6 * jj, bm = 48 + 6 * jj;
+          lo |= (uint64_t)s << bs;
+          if (bm < 64) {
+            lo |= (uint64_t)m << bm;
+            if (bm + 6 > 64) hi |= (uint64_t)m >> (64 - bm);
+          } else {
+            hi |= (uint64_t)m << (bm - 64);
+          }
+        }
+        for (int i = 0; i < 8; ++i) sc[b * 16 + 4 + i] = (uint8_t)(lo >> (8 * i));
+        for (int i = 0; i < 4; ++i) sc[b * 16 + 12 + i] = (uint8_t)(hi >> (8 * i));
+      }
     } else if (fmt == Q8_0) {
       const uint8_t *blk = row_src + u * 34;
       for (int i = 0; i < 32; ++i) qs[u * 32 + i] = blk[2 + i];
@@ -86,7 +104,7 @@ __device__ __forceinline__ void decode_run(int fmt, const uint8_t *__restrict__ 
     const uint4 h = *reinterpret_cast<const uint4 *>(sc + (u / 8) * 16);
     const float d = f16_bits_to_f32(h.x), dmin = f16_bits_to_f32(h.x >> 16);
     uint32_t s, m;
-    scale_min_k4((int)(u % 8), h.y, h.z, h.w, s, m);
+    q4k_scale_min((int)(u % 8), h.y, h.z, h.w, s, m);
     scale = __fmul_rn(d, (float)s);
     min = __fmul_rn(dmin, (float)m);
   } else {
