@@ -106,7 +106,9 @@ def test_gemv_parity(torch_cuda, oracle, fmt, m, n, k):
     y = _qmatmul(torch, fmt, wdev, n, k, x)
     ref = oracle.packed_matmul(fmt, w, n, k, x)
     err = oracle.assert_close(y, ref, GEMV_TOL, f"gemv fmt {fmt} m {m} n {n} k {k}")
-    assert err < 1e-5  # f32 accumulation: far inside the tolerance
+    # activations held as 16-bit integers per 32-value run (|error| <= 2^-16 of
+    # the run's largest value), exact integer dots: ~2e-5, far inside 1e-3
+    assert err < 1e-4
 
 
 @pytest.mark.parametrize("fmt", [mgb.Q4_K])
