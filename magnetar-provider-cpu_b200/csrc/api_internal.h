@@ -20,6 +20,7 @@ int *device_error_flag(int device);
 
 mgb_status validate_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, const float *x,
                             uint64_t m, float *y);
+uint64_t qmatmul_scratch_bytes(int32_t format, uint64_t m, uint64_t n, uint64_t k);
 mgb_status run_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, const float *x,
                        uint64_t m, float *y, const float *addend, int addend_mode, void *workspace,
                        uint64_t workspace_bytes, int *err, int kernel_pref, cudaStream_t stream);

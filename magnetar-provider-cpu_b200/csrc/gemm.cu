@@ -6,17 +6,20 @@
 //
 // CTA tile: BM activation rows (1 or 2 accumulators of 128 rows) x BN weight
 // rows (the MMA N, <= 256, a multiple of 16), K in steps of 64 (one 128-byte
-// swizzle atom of bf16).  Two shared-memory rings: the operand ring (A and B
-// tiles, 3-4 stages, released by the MMA) and the packed-W ring (quant and
-// scale boxes, up to 8 stages, released by the dequantising warps), so the
-// packed weights stream from HBM several steps ahead of the tensor core.
-// Warp roles, 352 threads:
+// swizzle atom of bf16).  Three shared-memory rings, each as deep as its
+// producer's latency needs: activation tiles (from L2, 4 stages, released by
+// the MMA), bf16 W tiles (made on chip, 2 stages, released by the MMA) and
+// packed W (quant and scale boxes from HBM, 3+ stages, released by the
+// dequantising warps), so neither operand waits on a memory round trip.
+// Launched as a programmatic dependent: everything but the activation loads
+// (TMEM, barriers, the weight stream, dequantisation) overlaps the previous
+// kernel on the stream.  Warp roles, 352 threads:
 //   warp 0     TMA producer of the bf16 activation boxes (SWIZZLE_128B,
-//              straight into the UMMA operand layout) on a_full[s].  Owns the
-//              TMEM allocation.
+//              straight into the UMMA operand layout) on a_full[s], after
+//              griddepcontrol.wait.  Owns the TMEM allocation.
 //   warp 1     one thread issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32)
-//              per 16-wide K slice and commits each operand stage to
-//              ab_empty[s].
+//              per 16-wide K slice and commits each step to a_empty[s] and
+//              b_empty[s].
 //   warp 2     TMA producer of the packed W quant and scale boxes (no
 //              swizzle) on p_full[s].
 //   warps 3-10 dequantise the staged packed W into the bf16 B operand
@@ -46,12 +49,12 @@ constexpr int NUM_THREADS = 96 + DQ_THREADS;
 struct GemmParams {
   int m, n, k;
   int bn;               // weight rows per CTA (MMA N)
-  int stages;           // operand ring (A and B tiles)
+  int astages;          // activation-tile ring
+  int bstages;          // bf16 W-tile ring
   int pstages;          // packed-W ring
   int qbytes;           // packed quant bytes per weight row per K step (32 or 64)
-  uint32_t a_bytes;     // per operand stage
-  uint32_t b_bytes;
-  uint32_t stage_bytes;
+  uint32_t a_bytes;     // per activation stage
+  uint32_t b_bytes;     // per W-tile stage
   uint32_t wq_bytes;    // per packed stage
   uint32_t ws_bytes;
   uint32_t pstage_bytes;
@@ -224,6 +227,13 @@ __device__ __forceinline__ void dequant_run(const uint8_t *wq_row, const uint8_t
 
 // ---- the kernel ----------------------------------------------------------------------
 
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 template <int FMT, int SUBS>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_wq,
@@ -232,16 +242,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   // 1024-byte align the operand area (SWIZZLE_128B atoms).
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  const int SA = p.stages, SP = p.pstages;
-  uint8_t *ab0 = smem;                                        // SA x (A tile, B tile)
-  uint8_t *pk0 = smem + (size_t)SA * p.stage_bytes;           // SP x (quant box, scale box)
+  const int SA = p.astages, SB = p.bstages, SP = p.pstages;
+  uint8_t *a0 = smem;                                    // SA activation tiles
+  uint8_t *b0 = a0 + (size_t)SA * p.a_bytes;             // SB bf16 W tiles
+  uint8_t *pk0 = b0 + (size_t)SB * p.b_bytes;            // SP packed W (quant box, scale box)
   uint64_t *bars = reinterpret_cast<uint64_t *>(pk0 + (size_t)SP * p.pstage_bytes);
-  uint64_t *a_full = bars;                // activation tile landed (TMA bytes)
-  uint64_t *b_full = bars + SA;           // bf16 W operand written (DQ_THREADS arrivals)
-  uint64_t *ab_empty = bars + 2 * SA;     // MMA finished reading the A and B tiles
-  uint64_t *p_full = bars + 3 * SA;       // packed W boxes landed (TMA bytes)
-  uint64_t *p_empty = p_full + SP;        // every dequant warp finished reading them
-  uint64_t *done = p_empty + SP;          // all MMAs finished
+  uint64_t *a_full = bars;              // activation tile landed (TMA bytes)
+  uint64_t *a_empty = a_full + SA;      // MMA finished reading it
+  uint64_t *b_full = a_empty + SA;      // bf16 W tile written (DQ_THREADS arrivals)
+  uint64_t *b_empty = b_full + SB;      // MMA finished reading it
+  uint64_t *p_full = b_empty + SB;      // packed W boxes landed (TMA bytes)
+  uint64_t *p_empty = p_full + SP;      // every dequant warp finished reading them
+  uint64_t *done = p_empty + SP;        // all MMAs finished
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
   int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
 
@@ -254,8 +266,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < SA; ++s) {
       mbar_init(&a_full[s], 1);
+      mbar_init(&a_empty[s], 1);
+    }
+    for (int s = 0; s < SB; ++s) {
       mbar_init(&b_full[s], DQ_THREADS);
-      mbar_init(&ab_empty[s], 1);
+      mbar_init(&b_empty[s], 1);
     }
     for (int s = 0; s < SP; ++s) {
       mbar_init(&p_full[s], 1);
@@ -283,15 +298,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     // ---------------- activation tiles (TMA, SWIZZLE_128B) ----------------
     if (lane == 0) {
+      grid_launch_dependents();
+      grid_dependency_wait();  // the activations may be the previous kernel's output
       int issued = 0;
       for (int kt = 0; kt < KT; ++kt) {
         const int s = kt % SA;
-        if (kt >= SA && !mbar_wait(&ab_empty[s], ((kt / SA) - 1) & 1, p.err)) {
+        if (kt >= SA && !mbar_wait(&a_empty[s], ((kt / SA) - 1) & 1, p.err)) {
           *(volatile int *)abort_flag = 1;
           break;
         }
         if (*(volatile int *)abort_flag) break;
-        uint8_t *st = ab0 + (size_t)s * p.stage_bytes;
+        uint8_t *st = a0 + (size_t)s * p.a_bytes;
         mbar_arrive_expect_tx(&a_full[s], p.a_bytes);
         for (int sub = 0; sub < SUBS; ++sub)
           tma_load_2d(st + sub * 16384, &map_a, kt * KSTEP, m0 + sub * 128, &a_full[s]);
@@ -303,6 +320,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == 2) {
     // ---------------- packed W boxes, prefetched SP steps ahead ----------------
+    // (weights never depend on an earlier kernel: no grid-dependency wait)
     if (lane == 0) {
       int issued = 0;
       for (int kt = 0; kt < KT; ++kt) {
@@ -326,22 +344,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0) {
       const uint32_t idesc = instr_desc_bf16(128, p.bn);
       for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % SA;
-        const uint32_t ph = (kt / SA) & 1;
-        if (!mbar_wait(&a_full[s], ph, p.err) || !mbar_wait(&b_full[s], ph, p.err)) {
+        const int sa = kt % SA, sb = kt % SB;
+        if (!mbar_wait(&a_full[sa], (kt / SA) & 1, p.err) ||
+            !mbar_wait(&b_full[sb], (kt / SB) & 1, p.err)) {
           *(volatile int *)abort_flag = 1;
           break;
         }
         tc_fence_after();
-        uint8_t *st = ab0 + (size_t)s * p.stage_bytes;
-        const uint32_t a_addr = smem_u32(st), b_addr = smem_u32(st + p.a_bytes);
+        const uint32_t a_addr = smem_u32(a0 + (size_t)sa * p.a_bytes);
+        const uint32_t b_addr = smem_u32(b0 + (size_t)sb * p.b_bytes);
 #pragma unroll
         for (int sub = 0; sub < SUBS; ++sub)
 #pragma unroll
           for (int kk = 0; kk < KSTEP / 16; ++kk)
             mma_bf16(tmem_base + sub * 256, smem_desc_sw128(a_addr + sub * 16384 + kk * 32),
                      smem_desc_sw128(b_addr + kk * 32), idesc, (kt | kk) != 0);
-        mma_commit(&ab_empty[s]);
+        mma_commit(&a_empty[sa]);
+        mma_commit(&b_empty[sb]);
       }
       mma_commit(done);  // arrives once every MMA issued above has completed
     }
@@ -361,17 +380,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int items = p.bn * 2;  // (weight row, run) pairs per stage
     bool ok = true;
     for (int kt = 0; kt < KT && ok; ++kt) {
-      const int s = kt % SA, sp = kt % SP;
+      const int sb = kt % SB, sp = kt % SP;
       if (*(volatile int *)abort_flag) break;
-      // the B slot is free once the MMA of round (kt / SA) - 1 released it, and
+      // the B slot is free once the MMA of round (kt / SB) - 1 released it, and
       // the packed boxes of this step have landed
-      ok = (kt < SA || mbar_wait(&ab_empty[s], ((kt / SA) - 1) & 1, p.err)) &&
+      ok = (kt < SB || mbar_wait(&b_empty[sb], ((kt / SB) - 1) & 1, p.err)) &&
            mbar_wait(&p_full[sp], (kt / SP) & 1, p.err);
       if (!ok) {
         *(volatile int *)abort_flag = 1;
         break;
       }
-      uint8_t *bt = ab0 + (size_t)s * p.stage_bytes + p.a_bytes;
+      uint8_t *bt = b0 + (size_t)sb * p.b_bytes;
       const uint8_t *wq = pk0 + (size_t)sp * p.pstage_bytes;
       const uint8_t *ws = wq + p.wq_bytes;
       for (int it = t; it < items; it += DQ_THREADS) {
@@ -386,7 +405,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
       fence_proxy_async_smem();
-      mbar_arrive(&b_full[s]);
+      mbar_arrive(&b_full[sb]);
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_empty[sp]);
     }
@@ -437,8 +456,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 // ---- host side ---------------------------------------------------------------------------
 
+// f32 -> bf16 activations; lets the dependent GEMM launch at once (its weight
+// stream and dequantisation overlap this pass; its activation loads wait).
 __global__ void f32_to_bf16_kernel(const float *__restrict__ x, __nv_bfloat16 *__restrict__ out,
                                    uint64_t n) {
+  grid_launch_dependents();
+  grid_dependency_wait();
   const uint64_t n4 = n / 4;
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n4;
        i += (uint64_t)gridDim.x * blockDim.x) {
@@ -494,6 +517,22 @@ TileChoice choose_tiles(uint64_t m, uint64_t n, int sms) {
   return t;
 }
 
+template <typename K, typename... Args>
+cudaError_t launch_dependent(K kern, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                             Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 }  // namespace
 
 uint64_t gemm_workspace_bytes(int, uint64_t m, uint64_t, uint64_t k) {
@@ -512,12 +551,12 @@ cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const fl
       (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 15))
     return cudaErrorInvalidValue;
   __nv_bfloat16 *xb = static_cast<__nv_bfloat16 *>(workspace);
-  {
-    const uint64_t n4 = m * k / 4;
-    uint64_t blocks = ceil_div(n4, 256);
-    if (blocks > (uint64_t)sms * 16) blocks = (uint64_t)sms * 16;
-    f32_to_bf16_kernel<<<(unsigned)blocks, 256, 0, stream>>>(x, xb, m * k);
-  }
+  const uint64_t n4 = m * k / 4;
+  uint64_t blocks = ceil_div(n4, 256);
+  if (blocks > (uint64_t)sms * 16) blocks = (uint64_t)sms * 16;
+  cudaError_t e = launch_dependent(f32_to_bf16_kernel, dim3((unsigned)blocks), dim3(256), 0,
+                                   stream, x, xb, m * k);
+  if (e != cudaSuccess) return e;
   return launch_gemm_bf16(fmt, w, n, k, xb, m, y, addend, addend_mode, err, sms, stream);
 }
 
@@ -537,23 +576,19 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
   p.qbytes = fmt == Q8_0 ? 64 : 32;
   p.a_bytes = 16384u * t.subs;
   p.b_bytes = (uint32_t)ceil_div((uint64_t)t.bn * 128u, 1024) * 1024;
-  p.stage_bytes = p.a_bytes + p.b_bytes;
   p.wq_bytes = (uint32_t)ceil_div((uint64_t)t.bn * p.qbytes, 1024) * 1024;
   p.ws_bytes = (uint32_t)ceil_div((uint64_t)t.bn * 16, 1024) * 1024;
   p.pstage_bytes = p.wq_bytes + p.ws_bytes;
   p.ptx_bytes = (uint32_t)t.bn * (uint32_t)p.qbytes + (uint32_t)t.bn * 16u;
-  // operand ring first (3 or 4 stages), the rest of the budget for the packed ring
+  // ring depths sized to their latency: activation tiles come from L2 (4 deep),
+  // the bf16 W tile is produced on chip (2 deep), packed W streams from HBM (3+)
   const uint32_t budget = 225 * 1024 - 1024 /*align slack*/ - 512 /*barriers*/;
-  int sa = p.stage_bytes * 4 + p.pstage_bytes * 4 <= budget ? 4 : 3;
-  int sp = (int)((budget - sa * p.stage_bytes) / p.pstage_bytes);
-  if (sp > 8) sp = 8;
-  if (sp < 2) {
-    sa = 2;
-    sp = (int)((budget - sa * p.stage_bytes) / p.pstage_bytes);
-    if (sp > 8) sp = 8;
-  }
-  if (sp < 2) return cudaErrorInvalidValue;
-  p.stages = sa;
+  int sa = 4, sb = 2, sp = 3;
+  while (sa * p.a_bytes + sb * p.b_bytes + sp * p.pstage_bytes > budget && sa > 2) --sa;
+  if (sa * p.a_bytes + sb * p.b_bytes + sp * p.pstage_bytes > budget) return cudaErrorInvalidValue;
+  while (sp < 8 && sa * p.a_bytes + sb * p.b_bytes + (sp + 1) * p.pstage_bytes <= budget) ++sp;
+  p.astages = sa;
+  p.bstages = sb;
   p.pstages = sp;
   p.addend_mode = addend_mode;
   p.addend = addend;
@@ -570,7 +605,8 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
                    (uint32_t)t.bn, CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
 
-  const size_t smem = (size_t)sa * p.stage_bytes + (size_t)sp * p.pstage_bytes + 1024 + 512;
+  const size_t smem = (size_t)sa * p.a_bytes + (size_t)sb * p.b_bytes +
+                      (size_t)sp * p.pstage_bytes + 1024 + 512;
   dim3 grid((unsigned)ceil_div(n, (uint64_t)t.bn), (unsigned)ceil_div(m, 128ull * t.subs));
   cudaError_t e = cudaSuccess;
 #define MGB_GEMM_LAUNCH(F, SUBS)                                                               \
@@ -578,7 +614,7 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
     auto kern = gemm_kernel<F, SUBS>;                                                          \
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \
     if (e != cudaSuccess) return e;                                                            \
-    kern<<<grid, NUM_THREADS, smem, stream>>>(map_a, map_wq, map_ws, p);                       \
+    e = launch_dependent(kern, grid, dim3(NUM_THREADS), smem, stream, map_a, map_wq, map_ws, p); \
   } while (0)
 #define MGB_GEMM_FMT(F)                          \
   case F:                                        \
@@ -595,7 +631,7 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
   }
 #undef MGB_GEMM_FMT
 #undef MGB_GEMM_LAUNCH
-  return cudaGetLastError();
+  return e;
 }
 
 }  // namespace mgb

@@ -223,6 +223,65 @@ __device__ __forceinline__ void load_x(const float *__restrict__ x, int k, int u
   }
 }
 
+// ---- activation packing: one pass over x, shared by every CTA of the GEMV ------------
+// Scratch layout for m rows of runs = k/32: hi words [m][8][runs], lo words
+// [m][8][runs], dx [m][runs], sum [m][runs] (72 bytes per run; consecutive runs
+// are consecutive words, so a team's loads coalesce).
+
+__host__ __device__ inline uint64_t xpack_bytes(uint64_t m, uint64_t k) {
+  return m * (k / RUN) * 72;
+}
+
+template <bool PAIR>
+__global__ void pack_x_kernel(const float *__restrict__ x, int m, int k,
+                              uint32_t *__restrict__ ws) {
+  grid_launch_dependents();
+  grid_dependency_wait();  // x may be the previous kernel's output
+  const int runs = k / RUN;
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= m * runs) return;
+  const int row = t / runs, u = t % runs;
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 f = __ldg(reinterpret_cast<const float4 *>(x + (size_t)row * k + (size_t)u * 32) + i);
+    v[4 * i] = f.x;
+    v[4 * i + 1] = f.y;
+    v[4 * i + 2] = f.z;
+    v[4 * i + 3] = f.w;
+  }
+  XRun r;
+  pack_run(v, PAIR, r);
+  uint32_t *hi = ws, *lo = ws + (size_t)m * 8 * runs;
+  float *dx = reinterpret_cast<float *>(ws + (size_t)m * 16 * runs), *sum = dx + (size_t)m * runs;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    hi[((size_t)row * 8 + w) * runs + u] = r.hi[w];
+    lo[((size_t)row * 8 + w) * runs + u] = r.lo[w];
+  }
+  dx[(size_t)row * runs + u] = r.dx;
+  sum[(size_t)row * runs + u] = r.sum;
+}
+
+template <int MR>
+__device__ __forceinline__ void load_packed_x(const uint32_t *__restrict__ ws, int k, int u,
+                                              bool active, XRun (&xr)[MR]) {
+  const int runs = k / RUN;
+  const uint32_t *hi = ws, *lo = ws + (size_t)MR * 8 * runs;
+  const float *dx = reinterpret_cast<const float *>(ws + (size_t)MR * 16 * runs);
+  const float *sum = dx + (size_t)MR * runs;
+#pragma unroll
+  for (int m = 0; m < MR; ++m) {
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      xr[m].hi[w] = active ? hi[((size_t)m * 8 + w) * runs + u] : 0u;
+      xr[m].lo[w] = active ? lo[((size_t)m * 8 + w) * runs + u] : 0u;
+    }
+    xr[m].dx = active ? dx[(size_t)m * runs + u] : 0.f;
+    xr[m].sum = active ? sum[(size_t)m * runs + u] : 0.f;
+  }
+}
+
 // Sums RPT*MR per-lane values over the warp; lane 0 ends with all of them.
 template <int NV>
 __device__ __forceinline__ void warp_sum(float (&v)[NV]) {
@@ -250,7 +309,7 @@ struct GemvStaged {
 
 template <int FMT, int MR, int MAXT>
 __global__ void __launch_bounds__(MAXT, 1)
-    gemv_staged_kernel(const uint8_t *__restrict__ w, const float *__restrict__ x,
+    gemv_staged_kernel(const uint8_t *__restrict__ w, const uint32_t *__restrict__ xpack,
                        const GemvStaged p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const Layout L(FMT, (uint64_t)p.n, (uint64_t)p.k);
@@ -305,9 +364,9 @@ __global__ void __launch_bounds__(MAXT, 1)
   const bool active = u < runs;
   const int team_threads = p.team_warps * 32;
 
-  grid_dependency_wait();  // x may be the previous kernel's output
+  grid_dependency_wait();  // the packed activations come from the preceding pass
   XRun xr[MR];
-  load_x<FMT, MR>(x, p.k, u, active, xr);
+  load_packed_x<MR>(xpack, p.k, u, active, xr);
   uint32_t lut[4] = {0, 0, 0, 0};
   if (FMT == IQ4_NL) iq4_table(lut);
 
@@ -441,15 +500,39 @@ __global__ void __launch_bounds__(MAXT, 1)
 
 // ---- launch --------------------------------------------------------------------------
 
+template <typename K, typename... Args>
+static cudaError_t launch_dependent(K kern, dim3 grid, dim3 block, size_t smem,
+                                    cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// pack_x (MR rows of x -> scratch) then the staged GEMV reading the scratch,
+// both programmatic dependents of whatever precedes them on the stream.
 template <int FMT, int MR, int MAXT>
 static cudaError_t launch_staged(const void *w, int n, int k, const float *x, float *y,
-                                 const float *addend, int addend_mode, int *err, int sms,
-                                 cudaStream_t stream) {
+                                 const float *addend, int addend_mode, void *scratch, int *err,
+                                 int sms, cudaStream_t stream) {
   const Layout L(FMT, (uint64_t)n, (uint64_t)k);
+  const int runs = k / RUN;
+  constexpr bool pair = FMT == Q4_K || FMT == Q4_0;
+  uint32_t *xpack = static_cast<uint32_t *>(scratch);
+  cudaError_t e = launch_dependent(pack_x_kernel<pair>, dim3((unsigned)ceil_div((uint64_t)MR * runs, 128)),
+                                   dim3(128), 0, stream, x, MR, k, xpack);
+  if (e != cudaSuccess) return e;
   GemvStaged p;
   p.n = n;
   p.k = k;
-  p.team_warps = (k / RUN + 31) / 32;
+  p.team_warps = (runs + 31) / 32;
   p.teams = p.team_warps >= 8 ? 1 : 8 / p.team_warps;
   const int TR = p.teams * RPT;
   p.qs_stage_bytes = (uint32_t)ceil_div((uint64_t)TR * L.qs_row, 128) * 128;
@@ -475,19 +558,10 @@ static cudaError_t launch_staged(const void *w, int n, int k, const float *x, fl
   const size_t smem = (size_t)stages * p.stage_bytes + 2 * 8 * (size_t)stages +
                       2 * sizeof(float) * (size_t)p.teams * p.team_warps * RPT * MR;
   auto kern = gemv_staged_kernel<FMT, MR, MAXT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)grid);
-  cfg.blockDim = dim3((unsigned)threads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, static_cast<const uint8_t *>(w), x, p);
+  return launch_dependent(kern, dim3((unsigned)grid), dim3((unsigned)threads), smem, stream,
+                          static_cast<const uint8_t *>(w), static_cast<const uint32_t *>(xpack), p);
 }
 
 template <int FMT, int MR, int R, int MAXT>
@@ -508,18 +582,25 @@ static cudaError_t launch_simple(const void *w, int n, int k, const float *x, fl
   return cudaGetLastError();
 }
 
+static bool staged_ok(uint64_t k) { return k % 256 == 0 && k / RUN <= 31 * 32; }
+
 template <int FMT, int MR>
 static cudaError_t launch_fmt(const void *w, int n, int k, const float *x, float *y,
-                              const float *addend, int addend_mode, int *err, int sms,
-                              cudaStream_t stream) {
-  if (k % 256 == 0 && k / RUN <= 31 * 32) {  // a team of at most 31 warps plus the producer
+                              const float *addend, int addend_mode, void *scratch,
+                              uint64_t scratch_bytes, int *err, int sms, cudaStream_t stream) {
+  // the staged kernel (a team of at most 31 warps plus the producer) needs the
+  // packed-activation scratch; without it the self-contained kernel runs
+  if (staged_ok((uint64_t)k) && scratch && scratch_bytes >= xpack_bytes(MR, (uint64_t)k) &&
+      !(reinterpret_cast<uintptr_t>(scratch) & 15)) {
     if (k <= 8192)
-      return launch_staged<FMT, MR, 288>(w, n, k, x, y, addend, addend_mode, err, sms, stream);
+      return launch_staged<FMT, MR, 288>(w, n, k, x, y, addend, addend_mode, scratch, err, sms,
+                                         stream);
     // 1024-thread CTAs have 64 registers per thread: one activation row per launch
-    cudaError_t e = launch_staged<FMT, 1, 1024>(w, n, k, x, y, addend, addend_mode, err, sms, stream);
+    cudaError_t e = launch_staged<FMT, 1, 1024>(w, n, k, x, y, addend, addend_mode, scratch, err,
+                                                sms, stream);
     if (MR == 2 && e == cudaSuccess)
       e = launch_staged<FMT, 1, 1024>(w, n, k, x + k, y + n, addend_mode == 2 ? addend + n : addend,
-                                      addend_mode, err, sms, stream);
+                                      addend_mode, scratch, err, sms, stream);
     return e;
   }
   if (k <= 256 * 32) return launch_simple<FMT, MR, 4, 256>(w, n, k, x, y, addend, addend_mode, sms, stream);
@@ -531,15 +612,21 @@ static cudaError_t launch_fmt(const void *w, int n, int k, const float *x, float
   return e;
 }
 
+uint64_t gemv_scratch_bytes(uint64_t m, uint64_t k) {
+  return staged_ok(k) ? ceil_div(xpack_bytes(m < 2 ? m : 2, k), 256) * 256 : 0;
+}
+
 cudaError_t launch_gemv(int fmt, const void *w, uint64_t n, uint64_t k, const float *x,
-                        uint64_t m, float *y, const float *addend, int addend_mode, int *err,
-                        int sms, cudaStream_t stream) {
+                        uint64_t m, float *y, const float *addend, int addend_mode, void *scratch,
+                        uint64_t scratch_bytes, int *err, int sms, cudaStream_t stream) {
   // m <= 2 per launch; larger m is split into row pairs by the caller.
   const int N = (int)n, K = (int)k;
-#define MGB_GEMV_CASE(F)                                                                       \
-  case F:                                                                                      \
-    return m == 1 ? launch_fmt<F, 1>(w, N, K, x, y, addend, addend_mode, err, sms, stream)     \
-                  : launch_fmt<F, 2>(w, N, K, x, y, addend, addend_mode, err, sms, stream);
+#define MGB_GEMV_CASE(F)                                                                     \
+  case F:                                                                                    \
+    return m == 1 ? launch_fmt<F, 1>(w, N, K, x, y, addend, addend_mode, scratch,            \
+                                     scratch_bytes, err, sms, stream)                        \
+                  : launch_fmt<F, 2>(w, N, K, x, y, addend, addend_mode, scratch,            \
+                                     scratch_bytes, err, sms, stream);
   switch (fmt) {
     MGB_GEMV_CASE(Q4_K)
     MGB_GEMV_CASE(Q8_0)
