@@ -554,7 +554,12 @@ cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const fl
   const uint64_t n4 = m * k / 4;
   uint64_t blocks = ceil_div(n4, 256);
   if (blocks > (uint64_t)sms * 16) blocks = (uint64_t)sms * 16;
-  cudaError_t e = launch_dependent(f32_to_bf16_kernel, dim3((unsigned)blocks), dim3(256), 0,
+  // same shared-memory carveout as the GEMM: no SM reconfiguration between them
+  cudaError_t e = cudaFuncSetAttribute(f32_to_bf16_kernel,
+                                       cudaFuncAttributePreferredSharedMemoryCarveout,
+                                       (int)cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return e;
+  e = launch_dependent(f32_to_bf16_kernel, dim3((unsigned)blocks), dim3(256), 0,
                                    stream, x, xb, m * k);
   if (e != cudaSuccess) return e;
   return launch_gemm_bf16(fmt, w, n, k, xb, m, y, addend, addend_mode, err, sms, stream);

@@ -232,6 +232,9 @@ __host__ __device__ inline uint64_t xpack_bytes(uint64_t m, uint64_t k) {
   return m * (k / RUN) * 72;
 }
 
+// Four threads per run, each packing 8 of its values into 2 high and 2 low
+// words (words 2p, 2p+1 hold values 8p..8p+7 in either order); the run's
+// max |x| and sum come from a 4-lane shuffle.
 template <bool PAIR>
 __global__ void pack_x_kernel(const float *__restrict__ x, int m, int k,
                               uint32_t *__restrict__ ws) {
@@ -239,28 +242,48 @@ __global__ void pack_x_kernel(const float *__restrict__ x, int m, int k,
   grid_dependency_wait();  // x may be the previous kernel's output
   const int runs = k / RUN;
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= m * runs) return;
-  const int row = t / runs, u = t % runs;
-  float v[32];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float4 f = __ldg(reinterpret_cast<const float4 *>(x + (size_t)row * k + (size_t)u * 32) + i);
-    v[4 * i] = f.x;
-    v[4 * i + 1] = f.y;
-    v[4 * i + 2] = f.z;
-    v[4 * i + 3] = f.w;
+  const int p = t & 3, ru = t >> 2;
+  const bool live = ru < m * runs;  // whole 4-lane groups are live or not
+  const int row = live ? ru / runs : 0, u = live ? ru % runs : 0;
+  float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (live) {
+    const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)row * k + (size_t)u * 32 + 8 * p);
+    const float4 a = __ldg(src), b = __ldg(src + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
   }
-  XRun r;
-  pack_run(v, PAIR, r);
+  float amax = 0.f, s = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+  for (int off = 1; off < 4; off <<= 1) {
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    s += __shfl_xor_sync(0xffffffffu, s, off);
+  }
+  if (!live) return;
+  const float inv = amax > 0.f ? 32767.f / amax : 0.f;
+  uint32_t h[2] = {0, 0}, l[2] = {0, 0};
+#pragma unroll
+  for (int wd = 0; wd < 2; ++wd)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int e = PAIR ? 2 * b + wd : 4 * wd + b;
+      int q = __float2int_rn(v[e] * inv);
+      q = max(-32767, min(32767, q));
+      h[wd] |= (uint32_t)((q >> 8) & 0xff) << (8 * b);
+      l[wd] |= (uint32_t)(q & 0xff) << (8 * b);
+    }
   uint32_t *hi = ws, *lo = ws + (size_t)m * 8 * runs;
   float *dx = reinterpret_cast<float *>(ws + (size_t)m * 16 * runs), *sum = dx + (size_t)m * runs;
 #pragma unroll
-  for (int w = 0; w < 8; ++w) {
-    hi[((size_t)row * 8 + w) * runs + u] = r.hi[w];
-    lo[((size_t)row * 8 + w) * runs + u] = r.lo[w];
+  for (int wd = 0; wd < 2; ++wd) {
+    hi[((size_t)row * 8 + 2 * p + wd) * runs + u] = h[wd];
+    lo[((size_t)row * 8 + 2 * p + wd) * runs + u] = l[wd];
   }
-  dx[(size_t)row * runs + u] = r.dx;
-  sum[(size_t)row * runs + u] = r.sum;
+  if (p == 0) {
+    dx[(size_t)row * runs + u] = amax / 32767.f;
+    sum[(size_t)row * runs + u] = s;
+  }
 }
 
 template <int MR>
@@ -282,13 +305,26 @@ __device__ __forceinline__ void load_packed_x(const uint32_t *__restrict__ ws, i
   }
 }
 
-// Sums RPT*MR per-lane values over the warp; lane 0 ends with all of them.
+// Sums NV per-lane values (NV a power of two <= 32) over the warp with a
+// transposing butterfly: each step halves the values a lane keeps and sends
+// the other half to its partner, so NV values cost NV - 1 + log2(32 / NV)
+// shuffles instead of 5 NV.  Returns the total of value lane / (32 / NV).
 template <int NV>
-__device__ __forceinline__ void warp_sum(float (&v)[NV]) {
+__device__ __forceinline__ float warp_sum_transpose(float (&v)[NV], int lane) {
 #pragma unroll
-  for (int i = 0; i < NV; ++i)
+  for (int c = NV, o = 16; c > 1; c >>= 1, o >>= 1) {
+    const bool upper = (lane & o) != 0;
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) v[i] += __shfl_xor_sync(0xffffffffu, v[i], off);
+    for (int j = 0; j < c / 2; ++j) {
+      const float send = upper ? v[j] : v[j + c / 2];
+      const float keep = upper ? v[j + c / 2] : v[j];
+      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  float s = v[0];
+#pragma unroll
+  for (int o = 16 / NV; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  return s;
 }
 
 // ---- main kernel: bulk-copy staged, persistent ----------------------------------------
@@ -299,6 +335,7 @@ struct GemvStaged {
   int n, k;
   int teams, team_warps;  // consumer geometry
   int stages;
+  int chunk;              // stages per reduction pass
   int rows_per_cta;
   uint32_t stage_bytes, qs_stage_bytes;
   int addend_mode;
@@ -317,7 +354,7 @@ __global__ void __launch_bounds__(MAXT, 1)
   const int TR = p.teams * RPT;  // rows per stage
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * p.stage_bytes);
   uint64_t *empty = full + S;
-  float *red = reinterpret_cast<float *>(empty + S);  // [2][teams][team_warps][RPT*MR]
+  float *red = reinterpret_cast<float *>(empty + S);  // [teams][chunk][RPT][team_warps][MR]
   const int consumer_warps = p.teams * p.team_warps;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = blockIdx.x * p.rows_per_cta;
@@ -363,6 +400,7 @@ __global__ void __launch_bounds__(MAXT, 1)
   const int runs = p.k / RUN;
   const bool active = u < runs;
   const int team_threads = p.team_warps * 32;
+  float *red_team = red + (size_t)team * p.chunk * RPT * p.team_warps * MR;
 
   grid_dependency_wait();  // the packed activations come from the preceding pass
   XRun xr[MR];
@@ -409,23 +447,32 @@ __global__ void __launch_bounds__(MAXT, 1)
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the stage's bytes
-    float *rb = red + ((size_t)(g & 1) * p.teams + team) * p.team_warps * (RPT * MR);
-    warp_sum<RPT * MR>(part);
-    if (lane == 0)
-#pragma unroll
-      for (int i = 0; i < RPT * MR; ++i) rb[tw * (RPT * MR) + i] = part[i];
-    named_barrier(1 + team, team_threads);
-    const int t = tw * 32 + lane;
-    if (t < RPT * MR) {
-      const int i = t / MR, m = t % MR;
-      const int row = row0 + team * RPT + i;
-      if (row < r1) {
-        float sum = 0.f;
-        for (int wi = 0; wi < p.team_warps; ++wi) sum += rb[wi * (RPT * MR) + t];
-        if (p.addend_mode == 1) sum = sum + p.addend[row];
-        else if (p.addend_mode == 2) sum = sum + p.addend[(size_t)m * p.n + row];
-        p.y[(size_t)m * p.n + row] = sum;
+    // warp totals of this stage's rows -> red[stage in chunk][row][warp][m]
+    constexpr int NV = RPT * MR;
+    const int c = g % p.chunk;
+    const float tot = warp_sum_transpose<NV>(part, lane);
+    if ((lane & (32 / NV - 1)) == 0) {
+      const int v = lane / (32 / NV);
+      red_team[((c * RPT + v / MR) * p.team_warps + tw) * MR + v % MR] = tot;
+    }
+    // every `chunk` stages (and after the last) the team sums its warps in a
+    // fixed order and writes y
+    if (c == p.chunk - 1 || g == nstages - 1) {
+      named_barrier(1 + team, team_threads);
+      const int g0 = g - c;
+      for (int t = tw * 32 + lane; t < (c + 1) * NV; t += team_threads) {
+        const int cc = t / NV, i = (t % NV) / MR, m = t % MR;
+        const int row = r0 + (g0 + cc) * TR + team * RPT + i;
+        if (row < r1) {
+          float sum = 0.f;
+          for (int wi = 0; wi < p.team_warps; ++wi)
+            sum += red_team[((cc * RPT + i) * p.team_warps + wi) * MR + m];
+          if (p.addend_mode == 1) sum = sum + p.addend[row];
+          else if (p.addend_mode == 2) sum = sum + p.addend[(size_t)m * p.n + row];
+          p.y[(size_t)m * p.n + row] = sum;
+        }
       }
+      named_barrier(1 + team, team_threads);
     }
   }
 }
@@ -478,10 +525,11 @@ __global__ void __launch_bounds__(MAXT, 1)
         for (int m = 0; m < MR; ++m) part[i * MR + m] = pm[m];
       }
     }
-    warp_sum<R * MR>(part);
-    if (lane == 0)
-#pragma unroll
-      for (int i = 0; i < R * MR; ++i) red[buf][warp][i] = part[i];
+    {
+      constexpr int NV = R * MR;
+      const float tot = warp_sum_transpose<NV>(part, lane);
+      if ((lane & (32 / NV - 1)) == 0) red[buf][warp][lane / (32 / NV)] = tot;
+    }
     __syncthreads();
     if (threadIdx.x < R * MR) {
       const int i = threadIdx.x / MR, m = threadIdx.x % MR;
@@ -526,7 +574,13 @@ static cudaError_t launch_staged(const void *w, int n, int k, const float *x, fl
   const int runs = k / RUN;
   constexpr bool pair = FMT == Q4_K || FMT == Q4_0;
   uint32_t *xpack = static_cast<uint32_t *>(scratch);
-  cudaError_t e = launch_dependent(pack_x_kernel<pair>, dim3((unsigned)ceil_div((uint64_t)MR * runs, 128)),
+  // the small pass keeps the big kernels' shared-memory carveout: no SM
+  // reconfiguration between the two
+  cudaError_t e = cudaFuncSetAttribute(pack_x_kernel<pair>,
+                                       cudaFuncAttributePreferredSharedMemoryCarveout,
+                                       (int)cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return e;
+  e = launch_dependent(pack_x_kernel<pair>, dim3((unsigned)ceil_div((uint64_t)MR * runs * 4, 128)),
                                    dim3(128), 0, stream, x, MR, k, xpack);
   if (e != cudaSuccess) return e;
   GemvStaged p;
@@ -551,12 +605,18 @@ static cudaError_t launch_staged(const void *w, int n, int k, const float *x, fl
   if (grid > units) grid = units;
   p.rows_per_cta = (int)ceil_div((uint64_t)n, (uint64_t)grid);
   grid = (int)ceil_div((uint64_t)n, (uint64_t)p.rows_per_cta);
+  // reduction buffer: as many stages as fit in 16 KB (usually all of a CTA's)
+  const int nst = (int)ceil_div((uint64_t)p.rows_per_cta, (uint64_t)TR);
+  const size_t red_stage = sizeof(float) * (size_t)p.teams * RPT * p.team_warps * MR;
+  int chunk = (int)(16384 / red_stage);
+  if (chunk > nst) chunk = nst;
+  if (chunk < 1) chunk = 1;
+  p.chunk = chunk;
   p.addend_mode = addend_mode;
   p.addend = addend;
   p.y = y;
   p.err = err;
-  const size_t smem = (size_t)stages * p.stage_bytes + 2 * 8 * (size_t)stages +
-                      2 * sizeof(float) * (size_t)p.teams * p.team_warps * RPT * MR;
+  const size_t smem = (size_t)stages * p.stage_bytes + 2 * 8 * (size_t)stages + red_stage * chunk;
   auto kern = gemv_staged_kernel<FMT, MR, MAXT>;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
