@@ -101,19 +101,19 @@ mgb_status run_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, co
   for (uint64_t r = 0; r < m; r += 2) {
     const uint64_t rows = m - r < 2 ? m - r : 2;
     const float *add = addend_mode == 2 ? addend + r * n : addend;
-    e = launch_gemv(format, w, n, k, x + r * k, rows, y + r * n, add, addend_mode, workspace,
-                    workspace_bytes, err, sms, stream);
+    e = launch_gemv(format, w, n, k, x + r * k, rows, y + r * n, add, addend_mode, err, sms,
+                    stream);
     if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
   }
   return MGB_OK;
 }
 
-// Scratch the dispatch above uses for m rows: the GEMM's bf16 activations, or
-// the GEMV's packed activations.
+// Scratch the dispatch above uses for m rows: the GEMM's bf16 activations
+// (the GEMV needs none).
 uint64_t qmatmul_scratch_bytes(int32_t format, uint64_t m, uint64_t n, uint64_t k) {
   if (!format_supported(format)) return 0;
   if (m > 2 && gemm_supported(format, m, n, k)) return gemm_workspace_bytes(format, m, n, k);
-  return gemv_scratch_bytes(m, k);
+  return 0;
 }
 
 mgb_status validate_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, const float *x,

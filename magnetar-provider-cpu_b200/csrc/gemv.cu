@@ -223,85 +223,88 @@ __device__ __forceinline__ void load_x(const float *__restrict__ x, int k, int u
   }
 }
 
-// ---- activation packing: one pass over x, shared by every CTA of the GEMV ------------
-// Scratch layout for m rows of runs = k/32: hi words [m][8][runs], lo words
-// [m][8][runs], dx [m][runs], sum [m][runs] (72 bytes per run; consecutive runs
-// are consecutive words, so a team's loads coalesce).
+// ---- activation packing, once per CTA into shared memory ------------------------------
+// Layout for m rows of runs = k/32: hi words [m][8][runs], lo words [m][8][runs],
+// dx [m][runs], sum [m][runs] (72 bytes per run; consecutive runs are
+// consecutive words, so a team's reads are conflict-free).
 
 __host__ __device__ inline uint64_t xpack_bytes(uint64_t m, uint64_t k) {
   return m * (k / RUN) * 72;
 }
 
-// Four threads per run, each packing 8 of its values into 2 high and 2 low
-// words (words 2p, 2p+1 hold values 8p..8p+7 in either order); the run's
-// max |x| and sum come from a 4-lane shuffle.
+// The consumer threads (ct of nthreads, a multiple of 32) pack the m rows of x:
+// four lanes per run, each packing 8 of its values into 2 high and 2 low words
+// (words 2p, 2p+1 hold values 8p..8p+7 in either order); the run's max |x|
+// and sum come from a 4-lane shuffle.
 template <bool PAIR>
-__global__ void pack_x_kernel(const float *__restrict__ x, int m, int k,
-                              uint32_t *__restrict__ ws) {
-  grid_launch_dependents();
-  grid_dependency_wait();  // x may be the previous kernel's output
+__device__ __forceinline__ void pack_x_to_smem(const float *__restrict__ x, int m, int k, int ct,
+                                               int nthreads, uint32_t *xs) {
   const int runs = k / RUN;
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  const int p = t & 3, ru = t >> 2;
-  const bool live = ru < m * runs;  // whole 4-lane groups are live or not
-  const int row = live ? ru / runs : 0, u = live ? ru % runs : 0;
-  float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  if (live) {
-    const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)row * k + (size_t)u * 32 + 8 * p);
-    const float4 a = __ldg(src), b = __ldg(src + 1);
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-  }
-  float amax = 0.f, s = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-#pragma unroll
-  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-#pragma unroll
-  for (int off = 1; off < 4; off <<= 1) {
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-    s += __shfl_xor_sync(0xffffffffu, s, off);
-  }
-  if (!live) return;
-  const float inv = amax > 0.f ? 32767.f / amax : 0.f;
-  uint32_t h[2] = {0, 0}, l[2] = {0, 0};
-#pragma unroll
-  for (int wd = 0; wd < 2; ++wd)
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const int e = PAIR ? 2 * b + wd : 4 * wd + b;
-      int q = __float2int_rn(v[e] * inv);
-      q = max(-32767, min(32767, q));
-      h[wd] |= (uint32_t)((q >> 8) & 0xff) << (8 * b);
-      l[wd] |= (uint32_t)(q & 0xff) << (8 * b);
+  const int total = m * runs * 4;
+  uint32_t *hi = xs, *lo = xs + (size_t)m * 8 * runs;
+  float *dx = reinterpret_cast<float *>(xs + (size_t)m * 16 * runs), *sum = dx + (size_t)m * runs;
+  for (int base = 0; base < total; base += nthreads) {
+    const int t = base + ct;
+    const int p = t & 3, ru = t >> 2;
+    const bool live = t < total;  // whole 4-lane groups are live or not
+    const int row = live ? ru / runs : 0, u = live ? ru % runs : 0;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (live) {
+      const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)row * k + (size_t)u * 32 + 8 * p);
+      const float4 a = __ldg(src), b = __ldg(src + 1);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
     }
-  uint32_t *hi = ws, *lo = ws + (size_t)m * 8 * runs;
-  float *dx = reinterpret_cast<float *>(ws + (size_t)m * 16 * runs), *sum = dx + (size_t)m * runs;
+    float amax = 0.f, s = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
 #pragma unroll
-  for (int wd = 0; wd < 2; ++wd) {
-    hi[((size_t)row * 8 + 2 * p + wd) * runs + u] = h[wd];
-    lo[((size_t)row * 8 + 2 * p + wd) * runs + u] = l[wd];
-  }
-  if (p == 0) {
-    dx[(size_t)row * runs + u] = amax / 32767.f;
-    sum[(size_t)row * runs + u] = s;
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+      s += __shfl_xor_sync(0xffffffffu, s, off);
+    }
+    if (!live) continue;
+    const float inv = amax > 0.f ? 32767.f / amax : 0.f;
+    uint32_t h[2] = {0, 0}, l[2] = {0, 0};
+#pragma unroll
+    for (int wd = 0; wd < 2; ++wd)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int e = PAIR ? 2 * b + wd : 4 * wd + b;
+        int q = __float2int_rn(v[e] * inv);
+        q = max(-32767, min(32767, q));
+        h[wd] |= (uint32_t)((q >> 8) & 0xff) << (8 * b);
+        l[wd] |= (uint32_t)(q & 0xff) << (8 * b);
+      }
+#pragma unroll
+    for (int wd = 0; wd < 2; ++wd) {
+      hi[((size_t)row * 8 + 2 * p + wd) * runs + u] = h[wd];
+      lo[((size_t)row * 8 + 2 * p + wd) * runs + u] = l[wd];
+    }
+    if (p == 0) {
+      dx[(size_t)row * runs + u] = amax / 32767.f;
+      sum[(size_t)row * runs + u] = s;
+    }
   }
 }
 
 template <int MR>
-__device__ __forceinline__ void load_packed_x(const uint32_t *__restrict__ ws, int k, int u,
-                                              bool active, XRun (&xr)[MR]) {
+__device__ __forceinline__ void load_packed_x(const uint32_t *xs, int k, int u, bool active,
+                                              XRun (&xr)[MR]) {
   const int runs = k / RUN;
-  const uint32_t *hi = ws, *lo = ws + (size_t)MR * 8 * runs;
-  const float *dx = reinterpret_cast<const float *>(ws + (size_t)MR * 16 * runs);
+  const uint32_t *hi = xs, *lo = xs + (size_t)MR * 8 * runs;
+  const float *dx = reinterpret_cast<const float *>(xs + (size_t)MR * 16 * runs);
   const float *sum = dx + (size_t)MR * runs;
+  const int uu = active ? u : 0;
 #pragma unroll
   for (int m = 0; m < MR; ++m) {
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
-      xr[m].hi[w] = active ? hi[((size_t)m * 8 + w) * runs + u] : 0u;
-      xr[m].lo[w] = active ? lo[((size_t)m * 8 + w) * runs + u] : 0u;
+      xr[m].hi[w] = active ? hi[((size_t)m * 8 + w) * runs + uu] : 0u;
+      xr[m].lo[w] = active ? lo[((size_t)m * 8 + w) * runs + uu] : 0u;
     }
-    xr[m].dx = active ? dx[(size_t)m * runs + u] : 0.f;
-    xr[m].sum = active ? sum[(size_t)m * runs + u] : 0.f;
+    xr[m].dx = active ? dx[(size_t)m * runs + uu] : 0.f;
+    xr[m].sum = active ? sum[(size_t)m * runs + uu] : 0.f;
   }
 }
 
@@ -346,7 +349,7 @@ struct GemvStaged {
 
 template <int FMT, int MR, int MAXT>
 __global__ void __launch_bounds__(MAXT, 1)
-    gemv_staged_kernel(const uint8_t *__restrict__ w, const uint32_t *__restrict__ xpack,
+    gemv_staged_kernel(const uint8_t *__restrict__ w, const float *__restrict__ x,
                        const GemvStaged p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const Layout L(FMT, (uint64_t)p.n, (uint64_t)p.k);
@@ -354,7 +357,8 @@ __global__ void __launch_bounds__(MAXT, 1)
   const int TR = p.teams * RPT;  // rows per stage
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * p.stage_bytes);
   uint64_t *empty = full + S;
-  float *red = reinterpret_cast<float *>(empty + S);  // [teams][chunk][RPT][team_warps][MR]
+  uint32_t *xs = reinterpret_cast<uint32_t *>(empty + S);  // packed activations (xpack_bytes)
+  float *red = reinterpret_cast<float *>(xs + xpack_bytes(MR, p.k) / 4);  // [teams][chunk][RPT][team_warps][MR]
   const int consumer_warps = p.teams * p.team_warps;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = blockIdx.x * p.rows_per_cta;
@@ -402,11 +406,16 @@ __global__ void __launch_bounds__(MAXT, 1)
   const int team_threads = p.team_warps * 32;
   float *red_team = red + (size_t)team * p.chunk * RPT * p.team_warps * MR;
 
-  grid_dependency_wait();  // the packed activations come from the preceding pass
+  // x may be the previous kernel's output; the weight stream above never waits
+  grid_dependency_wait();
+  constexpr bool pair = FMT == Q4_K || FMT == Q4_0;
+  pack_x_to_smem<pair>(x, MR, p.k, threadIdx.x - 32, consumer_warps * 32, xs);
+  named_barrier(15, consumer_warps * 32);
   XRun xr[MR];
-  load_packed_x<MR>(xpack, p.k, u, active, xr);
+  load_packed_x<MR>(xs, p.k, u, active, xr);
   uint32_t lut[4] = {0, 0, 0, 0};
   if (FMT == IQ4_NL) iq4_table(lut);
+  const int uu = active ? u : 0;  // idle lanes read a valid run; their result is dropped
 
   // A wait that gives up records the error and the thread stops waiting, but
   // it keeps stepping through every stage so its team's named barriers match.
@@ -420,30 +429,30 @@ __global__ void __launch_bounds__(MAXT, 1)
     if (ok) ok = mbar_try_wait(&full[s], (g / S) & 1);
     const uint8_t *st = smem + (size_t)s * p.stage_bytes;
     const int row0 = r0 + g * TR;
+    // branch-free over the team's RPT rows (rows past the end of a partial
+    // stage read stale stage bytes and are dropped), so their loads and
+    // integer dot products interleave
     float part[RPT * MR];
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
-#pragma unroll
-      for (int m = 0; m < MR; ++m) part[i * MR + m] = 0.f;
       const int lr = team * RPT + i;  // row within the stage
-      if (ok && active && row0 + lr < r1) {
-        const uint8_t *qrow = st + (size_t)lr * L.qs_row;
-        const uint8_t *srow = st + p.qs_stage_bytes + (size_t)lr * L.sc_row;
-        uint4 qa, qb = make_uint4(0, 0, 0, 0), hd = make_uint4(0, 0, 0, 0);
-        uint32_t dh = 0;
-        if (FMT == Q8_0) {
-          qa = *reinterpret_cast<const uint4 *>(qrow + u * 32);
-          qb = *reinterpret_cast<const uint4 *>(qrow + u * 32 + 16);
-        } else {
-          qa = *reinterpret_cast<const uint4 *>(qrow + u * 16);
-        }
-        if (FMT == Q4_K) hd = *reinterpret_cast<const uint4 *>(srow + (u >> 3) * 16);
-        else dh = *reinterpret_cast<const uint16_t *>(srow + u * 2);
-        float pm[MR];
-        run_partials<FMT, MR>(qa, qb, hd, dh, u & 7, xr, lut, pm);
-#pragma unroll
-        for (int m = 0; m < MR; ++m) part[i * MR + m] = pm[m];
+      const uint8_t *qrow = st + (size_t)lr * L.qs_row;
+      const uint8_t *srow = st + p.qs_stage_bytes + (size_t)lr * L.sc_row;
+      uint4 qa, qb = make_uint4(0, 0, 0, 0), hd = make_uint4(0, 0, 0, 0);
+      uint32_t dh = 0;
+      if (FMT == Q8_0) {
+        qa = *reinterpret_cast<const uint4 *>(qrow + uu * 32);
+        qb = *reinterpret_cast<const uint4 *>(qrow + uu * 32 + 16);
+      } else {
+        qa = *reinterpret_cast<const uint4 *>(qrow + uu * 16);
       }
+      if (FMT == Q4_K) hd = *reinterpret_cast<const uint4 *>(srow + (uu >> 3) * 16);
+      else dh = *reinterpret_cast<const uint16_t *>(srow + uu * 2);
+      float pm[MR];
+      run_partials<FMT, MR>(qa, qb, hd, dh, uu & 7, xr, lut, pm);
+      const bool keep = ok && active && row0 + lr < r1;
+#pragma unroll
+      for (int m = 0; m < MR; ++m) part[i * MR + m] = keep ? pm[m] : 0.f;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the stage's bytes
@@ -564,25 +573,14 @@ static cudaError_t launch_dependent(K kern, dim3 grid, dim3 block, size_t smem,
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-// pack_x (MR rows of x -> scratch) then the staged GEMV reading the scratch,
-// both programmatic dependents of whatever precedes them on the stream.
+// The staged GEMV: a programmatic dependent of whatever precedes it on the
+// stream (its weight stream starts at once; it waits before reading x).
 template <int FMT, int MR, int MAXT>
 static cudaError_t launch_staged(const void *w, int n, int k, const float *x, float *y,
-                                 const float *addend, int addend_mode, void *scratch, int *err,
-                                 int sms, cudaStream_t stream) {
+                                 const float *addend, int addend_mode, int *err, int sms,
+                                 cudaStream_t stream) {
   const Layout L(FMT, (uint64_t)n, (uint64_t)k);
   const int runs = k / RUN;
-  constexpr bool pair = FMT == Q4_K || FMT == Q4_0;
-  uint32_t *xpack = static_cast<uint32_t *>(scratch);
-  // the small pass keeps the big kernels' shared-memory carveout: no SM
-  // reconfiguration between the two
-  cudaError_t e = cudaFuncSetAttribute(pack_x_kernel<pair>,
-                                       cudaFuncAttributePreferredSharedMemoryCarveout,
-                                       (int)cudaSharedmemCarveoutMaxShared);
-  if (e != cudaSuccess) return e;
-  e = launch_dependent(pack_x_kernel<pair>, dim3((unsigned)ceil_div((uint64_t)MR * runs * 4, 128)),
-                                   dim3(128), 0, stream, x, MR, k, xpack);
-  if (e != cudaSuccess) return e;
   GemvStaged p;
   p.n = n;
   p.k = k;
@@ -616,12 +614,13 @@ static cudaError_t launch_staged(const void *w, int n, int k, const float *x, fl
   p.addend = addend;
   p.y = y;
   p.err = err;
-  const size_t smem = (size_t)stages * p.stage_bytes + 2 * 8 * (size_t)stages + red_stage * chunk;
+  const size_t smem = (size_t)stages * p.stage_bytes + 2 * 8 * (size_t)stages +
+                      xpack_bytes(MR, (uint64_t)k) + red_stage * chunk;
   auto kern = gemv_staged_kernel<FMT, MR, MAXT>;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   return launch_dependent(kern, dim3((unsigned)grid), dim3((unsigned)threads), smem, stream,
-                          static_cast<const uint8_t *>(w), static_cast<const uint32_t *>(xpack), p);
+                          static_cast<const uint8_t *>(w), x, p);
 }
 
 template <int FMT, int MR, int R, int MAXT>
@@ -646,21 +645,16 @@ static bool staged_ok(uint64_t k) { return k % 256 == 0 && k / RUN <= 31 * 32; }
 
 template <int FMT, int MR>
 static cudaError_t launch_fmt(const void *w, int n, int k, const float *x, float *y,
-                              const float *addend, int addend_mode, void *scratch,
-                              uint64_t scratch_bytes, int *err, int sms, cudaStream_t stream) {
-  // the staged kernel (a team of at most 31 warps plus the producer) needs the
-  // packed-activation scratch; without it the self-contained kernel runs
-  if (staged_ok((uint64_t)k) && scratch && scratch_bytes >= xpack_bytes(MR, (uint64_t)k) &&
-      !(reinterpret_cast<uintptr_t>(scratch) & 15)) {
+                              const float *addend, int addend_mode, int *err, int sms,
+                              cudaStream_t stream) {
+  if (staged_ok((uint64_t)k)) {  // a team of at most 31 warps plus the producer
     if (k <= 8192)
-      return launch_staged<FMT, MR, 288>(w, n, k, x, y, addend, addend_mode, scratch, err, sms,
-                                         stream);
+      return launch_staged<FMT, MR, 288>(w, n, k, x, y, addend, addend_mode, err, sms, stream);
     // 1024-thread CTAs have 64 registers per thread: one activation row per launch
-    cudaError_t e = launch_staged<FMT, 1, 1024>(w, n, k, x, y, addend, addend_mode, scratch, err,
-                                                sms, stream);
+    cudaError_t e = launch_staged<FMT, 1, 1024>(w, n, k, x, y, addend, addend_mode, err, sms, stream);
     if (MR == 2 && e == cudaSuccess)
       e = launch_staged<FMT, 1, 1024>(w, n, k, x + k, y + n, addend_mode == 2 ? addend + n : addend,
-                                      addend_mode, scratch, err, sms, stream);
+                                      addend_mode, err, sms, stream);
     return e;
   }
   if (k <= 256 * 32) return launch_simple<FMT, MR, 4, 256>(w, n, k, x, y, addend, addend_mode, sms, stream);
@@ -672,21 +666,15 @@ static cudaError_t launch_fmt(const void *w, int n, int k, const float *x, float
   return e;
 }
 
-uint64_t gemv_scratch_bytes(uint64_t m, uint64_t k) {
-  return staged_ok(k) ? ceil_div(xpack_bytes(m < 2 ? m : 2, k), 256) * 256 : 0;
-}
-
 cudaError_t launch_gemv(int fmt, const void *w, uint64_t n, uint64_t k, const float *x,
-                        uint64_t m, float *y, const float *addend, int addend_mode, void *scratch,
-                        uint64_t scratch_bytes, int *err, int sms, cudaStream_t stream) {
+                        uint64_t m, float *y, const float *addend, int addend_mode, int *err,
+                        int sms, cudaStream_t stream) {
   // m <= 2 per launch; larger m is split into row pairs by the caller.
   const int N = (int)n, K = (int)k;
-#define MGB_GEMV_CASE(F)                                                                     \
-  case F:                                                                                    \
-    return m == 1 ? launch_fmt<F, 1>(w, N, K, x, y, addend, addend_mode, scratch,            \
-                                     scratch_bytes, err, sms, stream)                        \
-                  : launch_fmt<F, 2>(w, N, K, x, y, addend, addend_mode, scratch,            \
-                                     scratch_bytes, err, sms, stream);
+#define MGB_GEMV_CASE(F)                                                                      \
+  case F:                                                                                     \
+    return m == 1 ? launch_fmt<F, 1>(w, N, K, x, y, addend, addend_mode, err, sms, stream)    \
+                  : launch_fmt<F, 2>(w, N, K, x, y, addend, addend_mode, err, sms, stream);
   switch (fmt) {
     MGB_GEMV_CASE(Q4_K)
     MGB_GEMV_CASE(Q8_0)

@@ -17,12 +17,10 @@ cudaError_t launch_input_major(int fmt, const void *w, uint64_t k_rows, uint64_t
 // gemv.cu: m <= 2.  addend_mode 0 none, 1 row broadcast addend[n], 2 addend[m, n].
 // Launched with programmatic stream serialization (it may start while the
 // previous kernel on the stream drains; it waits for it before reading x).
-// The staged kernel packs the activations into `scratch` first
-// (gemv_scratch_bytes); with no scratch the self-contained kernel runs.
-uint64_t gemv_scratch_bytes(uint64_t m, uint64_t k);
+// No scratch: each CTA packs its activations into shared memory.
 cudaError_t launch_gemv(int fmt, const void *w, uint64_t n, uint64_t k, const float *x,
-                        uint64_t m, float *y, const float *addend, int addend_mode, void *scratch,
-                        uint64_t scratch_bytes, int *err, int sms, cudaStream_t stream);
+                        uint64_t m, float *y, const float *addend, int addend_mode, int *err,
+                        int sms, cudaStream_t stream);
 
 // gemm.cu: tensor-core path (bf16 operands, f32 accumulation) for m > 2.
 uint64_t gemm_workspace_bytes(int fmt, uint64_t m, uint64_t n, uint64_t k);

@@ -282,13 +282,11 @@ mgb_status run_matmul(mgb_provider *p, const std::string &kernel, const mgb_kern
                   (unsigned long long)k, (unsigned long long)w.stored_cols);
     s = ensure_buf(p, product, m * n * 4);
     if (s != MGB_OK) return s;
-    // scratch for the GEMM's bf16 activations or the GEMV's packed activations
+    // scratch for the GEMM's bf16 activations
     uint64_t ws = qmatmul_scratch_bytes(w.format, m, n, k);
-    if (gemm_supported(w.format, m, n, k)) {
-      const uint64_t g = gemm_workspace_bytes(w.format, m, n, k);
-      if (kernel_pref == MGB_KERNEL_GEMM && g > ws) ws = g;
-    }
-    if (kernel_pref == MGB_KERNEL_GEMV) ws = gemv_scratch_bytes(m, k);
+    if (gemm_supported(w.format, m, n, k) && kernel_pref == MGB_KERNEL_GEMM)
+      ws = gemm_workspace_bytes(w.format, m, n, k);
+    if (kernel_pref == MGB_KERNEL_GEMV) ws = 0;
     if (ws) {
       s = ensure_workspace(p, ws);
       if (s != MGB_OK) return s;

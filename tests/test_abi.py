@@ -39,10 +39,10 @@ def test_status_names_and_packed_sizes():
     assert mgb.packed_bytes(mgb.Q8_0, 14336, 4096) == 62_390_272
     assert mgb.packed_bytes(mgb.IQ4_NL, 14336, 4096) == 33_030_144
     assert mgb.packed_bytes(mgb.Q6_K, 1, 256) == 0  # declined format
-    # decode: packed activations, 72 bytes per 32-value run; prefill: bf16 activations
-    assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 1, 4096, 4096) == 4096 // 32 * 72
-    assert mgb.qmatmul_workspace_bytes(mgb.Q8_0, 2, 14336, 4096) == 2 * 4096 // 32 * 72
-    assert mgb.qmatmul_workspace_bytes(mgb.Q8_0, 2, 5, 96) == 0  # ragged k: no scratch
+    # decode GEMV: no scratch; prefill GEMM: the bf16 activations
+    assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 1, 4096, 4096) == 0
+    assert mgb.qmatmul_workspace_bytes(mgb.Q8_0, 2, 14336, 4096) == 0
+    assert mgb.qmatmul_workspace_bytes(mgb.Q8_0, 3, 5, 96) == 0  # ragged k: GEMV pairs
     assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 512, 14336, 4096) == 512 * 4096 * 2
 
 
