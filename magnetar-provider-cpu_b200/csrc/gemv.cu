@@ -589,17 +589,19 @@ static cudaError_t launch_staged(const void *w, int n, int k, const float *x, fl
   const int TR = p.teams * RPT;
   p.qs_stage_bytes = (uint32_t)ceil_div((uint64_t)TR * L.qs_row, 128) * 128;
   p.stage_bytes = p.qs_stage_bytes + (uint32_t)ceil_div((uint64_t)TR * L.sc_row, 128) * 128;
-  const uint32_t budget = 96 * 1024;
+  // One CTA per SM, at most ~110 KB of shared memory: the next GEMV on the
+  // stream (a programmatic dependent) then fits beside it and streams its
+  // weights while this one finishes.  Rows split evenly; a CTA's last stage
+  // may hold fewer than TR rows.
+  const uint64_t fixed = xpack_bytes(MR, (uint64_t)k) + 2048;
+  const uint64_t budget = 110 * 1024 > fixed ? 110 * 1024 - fixed : 0;
   int stages = (int)(budget / p.stage_bytes);
   if (stages > 8) stages = 8;
   if (stages < 2) stages = 2;
   p.stages = stages;
-  // two CTAs per SM when they fit (so a dependent launch can overlap), rows split evenly;
-  // a CTA's last stage may hold fewer than TR rows
   const int threads = 32 * (1 + p.teams * p.team_warps);
-  const int per_sm = threads <= 512 ? 2 : 1;
   const int units = (int)ceil_div((uint64_t)n, (uint64_t)TR);
-  int grid = sms * per_sm;
+  int grid = sms;
   if (grid > units) grid = units;
   p.rows_per_cta = (int)ceil_div((uint64_t)n, (uint64_t)grid);
   grid = (int)ceil_div((uint64_t)n, (uint64_t)p.rows_per_cta);
