@@ -589,9 +589,8 @@ static cudaError_t launch_staged(const void *w, int n, int k, const float *x, fl
   const int TR = p.teams * RPT;
   p.qs_stage_bytes = (uint32_t)ceil_div((uint64_t)TR * L.qs_row, 128) * 128;
   p.stage_bytes = p.qs_stage_bytes + (uint32_t)ceil_div((uint64_t)TR * L.sc_row, 128) * 128;
-  // One CTA per SM, at most ~110 KB of shared memory: the next GEMV on the
-  // stream (a programmatic dependent) then fits beside it and streams its
-  // weights while this one finishes.  Rows split evenly; a CTA's last stage
+  // Two CTAs per SM when they fit (more consumer warps to hide latency), each
+  // within ~110 KB of shared memory.  Rows split evenly; a CTA's last stage
   // may hold fewer than TR rows.
   const uint64_t fixed = xpack_bytes(MR, (uint64_t)k) + 2048;
   const uint64_t budget = 110 * 1024 > fixed ? 110 * 1024 - fixed : 0;
@@ -600,8 +599,9 @@ static cudaError_t launch_staged(const void *w, int n, int k, const float *x, fl
   if (stages < 2) stages = 2;
   p.stages = stages;
   const int threads = 32 * (1 + p.teams * p.team_warps);
+  const int per_sm = threads <= 512 ? 2 : 1;
   const int units = (int)ceil_div((uint64_t)n, (uint64_t)TR);
-  int grid = sms;
+  int grid = sms * per_sm;
   if (grid > units) grid = units;
   p.rows_per_cta = (int)ceil_div((uint64_t)n, (uint64_t)grid);
   grid = (int)ceil_div((uint64_t)n, (uint64_t)p.rows_per_cta);
