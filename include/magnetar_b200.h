@@ -265,6 +265,31 @@ uint64_t mgb_qmatmul_workspace_bytes(int32_t format, uint64_t m, uint64_t n, uin
 mgb_status mgb_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, const float *x,
                        uint64_t m, float *y, const float *addend, uint64_t addend_len,
                        void *workspace, uint64_t workspace_bytes, void *stream);
+/* mgb_qmatmul for callers that must not allocate device memory.  No
+ * counterpart in the reference (its CPU kernels allocate host buffers freely).
+ * Who needs it: a runtime that reserves the whole GPU for its own arena up
+ * front (a cudaMalloc would fail or bypass its accounting), or a latency-
+ * critical path that must stay out of the driver's allocator (cudaFree
+ * synchronises the device).  Same arguments and results as mgb_qmatmul
+ * without the workspace: the tensor-core path stages its bf16 activations in a
+ * fixed array inside this library's device image, MGB_STATIC_SCRATCH_BYTES
+ * (8 MiB) on every GPU that loads the library, held until the process exits.
+ * Limits and rules:
+ *  - m * k must be <= MGB_STATIC_SCRATCH_BYTES / 2 whenever m > 2 and
+ *    k % 256 == 0 (the tensor-core path); larger shapes are rejected with
+ *    MGB_INVALID_ARGUMENT and a message naming the limit;
+ *  - the array is shared by every call on a device and keeps the last call's
+ *    bytes: calls that may overlap on the GPU (different streams without
+ *    ordering between them) race on it and corrupt each other's results;
+ *  - the first call on a device resolves the array's device address (once,
+ *    with that device current); make that first call before any stream
+ *    capture;
+ *  - nothing is allocated, and no device error word is attached: a bounded
+ *    device wait that expires leaves y unspecified without a status. */
+#define MGB_STATIC_SCRATCH_BYTES (8u << 20)
+mgb_status mgb_qmatmul_static_scratch(int32_t format, const void *w, uint64_t n, uint64_t k,
+                                      const float *x, uint64_t m, float *y, const float *addend,
+                                      uint64_t addend_len, void *stream);
 /* The tensor-core GEMM alone for activations already in bf16: y[m, n] =
  * xb[m, k] (bf16, 16-byte aligned) * W^T, f32 accumulation, no scratch.
  * Needs k % 256 == 0.  For callers whose producer emits bf16 (no counterpart

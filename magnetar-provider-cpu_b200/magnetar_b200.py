@@ -118,6 +118,8 @@ _SIGNATURES = {
     "mgb_repack": ([_i32, _vp, _u64, _u64, _vp, _vp], _i32),
     "mgb_qmatmul_workspace_bytes": ([_i32, _u64, _u64, _u64], _u64),
     "mgb_qmatmul": ([_i32, _vp, _u64, _u64, _vp, _u64, _vp, _vp, _u64, _vp, _u64, _vp], _i32),
+    "mgb_qmatmul_static_scratch": ([_i32, _vp, _u64, _u64, _vp, _u64, _vp, _vp, _u64, _vp],
+                                   _i32),
     "mgb_qmatmul_bf16": ([_i32, _vp, _u64, _u64, _vp, _u64, _vp, _vp, _u64, _vp], _i32),
     "mgb_dequantize": ([_i32, _vp, _u64, _u64, _vp, _vp], _i32),
     "mgb_qmatmul_input_major": ([_i32, _vp, _u64, _u64, _vp, _u64, _vp, _vp], _i32),
