@@ -141,6 +141,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
   return false;
 }
 
+// mbar_wait for waits that are not on a critical path (or that share the SM
+// with another kernel's busy warps): after a few polls the thread sleeps
+// between polls (32 ns doubling to `max_ns`), leaving the issue slots to
+// warps with work.  Same iteration bound (at most ~WAIT_BOUND * max_ns).
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t *bar, uint32_t parity, int *err,
+                                                  uint32_t max_ns = 256) {
+  uint32_t ns = 32;
+  for (uint32_t i = 0; i < WAIT_BOUND; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i >= 4) {
+      __nanosleep(ns);
+      if (ns < max_ns) ns <<= 1;
+    }
+    if (err && (i & 1023) == 1023 && *(volatile int *)err != 0) return false;
+  }
+  record_error(err, ERR_WAIT_TIMEOUT);
+  return false;
+}
+
 // 1-D bulk copy global -> shared, completing `bytes` on `bar`.  Both addresses
 // 16-byte aligned, bytes a multiple of 16 (no multicast).
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,

@@ -88,29 +88,38 @@ struct XRun {
   uint32_t hi[8], lo[8];
 };
 
+// Quantises one run: q = round(v / dx) with dx = max|v| / 32767, so |q| <=
+// 32767.  The rounding adds 1.5 * 2^23 in one fused multiply-add, which leaves
+// 0x4B400000 + q in the float's bits: byte 0 is q's low byte and byte 1 its
+// high byte (two's complement, |q| < 2^22), so byte permutes build the words.
 __device__ __forceinline__ void pack_run(const float (&v)[32], bool pair_order, XRun &r) {
-  float amax = 0.f, s = 0.f;
+  float s = 0.f;
 #pragma unroll
   for (int i = 0; i < 32; i += 4) s += (v[i] + v[i + 1]) + (v[i + 2] + v[i + 3]);
+  float mx[16];  // max |v| as a tree (depth 5, not a chain of 32)
 #pragma unroll
-  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  for (int i = 0; i < 16; ++i) mx[i] = fmaxf(fabsf(v[2 * i]), fabsf(v[2 * i + 1]));
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+    for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
+  const float amax = mx[0];
   r.sum = s;
   r.dx = amax / 32767.f;
   const float inv = amax > 0.f ? 32767.f / amax : 0.f;
+  uint32_t b[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) b[i] = __float_as_uint(fmaf(v[i], inv, 12582912.f));
 #pragma unroll
   for (int wd = 0; wd < 8; ++wd) {
-    uint32_t h = 0, l = 0;
+    // pair order: word 2w -> values 8w + 2j, word 2w + 1 -> values 8w + 2j + 1
+    int e[4];
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      // pair order: word 2w -> values 8w + 2b, word 2w + 1 -> values 8w + 2b + 1
-      const int e = pair_order ? 8 * (wd / 2) + 2 * b + (wd & 1) : 4 * wd + b;
-      int q = __float2int_rn(v[e] * inv);
-      q = max(-32767, min(32767, q));
-      h |= (uint32_t)((q >> 8) & 0xff) << (8 * b);
-      l |= (uint32_t)(q & 0xff) << (8 * b);
-    }
-    r.hi[wd] = h;
-    r.lo[wd] = l;
+    for (int j = 0; j < 4; ++j) e[j] = pair_order ? 8 * (wd / 2) + 2 * j + (wd & 1) : 4 * wd + j;
+    const uint32_t l01 = __byte_perm(b[e[0]], b[e[1]], 0x0040u), l23 = __byte_perm(b[e[2]], b[e[3]], 0x0040u);
+    const uint32_t h01 = __byte_perm(b[e[0]], b[e[1]], 0x0051u), h23 = __byte_perm(b[e[2]], b[e[3]], 0x0051u);
+    r.lo[wd] = __byte_perm(l01, l23, 0x5410u);
+    r.hi[wd] = __byte_perm(h01, h23, 0x5410u);
   }
 }
 
@@ -203,6 +212,133 @@ __device__ __forceinline__ void run_partials(const uint4 &qa, const uint4 &qb, c
   }
 }
 
+// A run's two f32 factors, decoded once from the scale plane: the multiplier
+// of its integer dot product and the multiplier of its activation sum, so that
+// the run contributes (s * dx) * dot - m * sum.  Q4_K: s = d * scale_j,
+// m = dmin * min_j; Q4_0: s = d, m = 8 d (q - 8); Q8_0, IQ4_NL: s = d, m = 0.
+template <int FMT>
+__device__ __forceinline__ float2 decode_run_scale(const uint8_t *srow, int uu) {
+  if (FMT == Q4_K) {
+    const uint4 hd = *reinterpret_cast<const uint4 *>(srow + (uu >> 3) * 16);
+    const float d = f16_bits_to_f32(hd.x), dmin = f16_bits_to_f32(hd.x >> 16);
+    uint32_t sc, mn;
+    q4k_scale_min(uu & 7, hd.y, hd.z, hd.w, sc, mn);
+    return make_float2(d * (float)sc, dmin * (float)mn);
+  } else {
+    const float d = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(srow + uu * 2));
+    return make_float2(d, FMT == Q4_0 ? 8.f * d : 0.f);
+  }
+}
+
+// Partial dot products of one run of one weight row (its quant bytes at qrow,
+// its decoded factors sm) with MR activation rows.
+template <int FMT, int MR>
+__device__ __forceinline__ void run_partials_decoded(const uint8_t *qrow, int uu, float2 sm,
+                                                     const XRun (&x)[MR], const uint32_t lut[4],
+                                                     float (&part)[MR]) {
+  if (FMT == Q8_0) {
+    const uint4 qa = *reinterpret_cast<const uint4 *>(qrow + uu * 32);
+    const uint4 qb = *reinterpret_cast<const uint4 *>(qrow + uu * 32 + 16);
+    const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+    for (int m = 0; m < MR; ++m) part[m] = (sm.x * x[m].dx) * (float)dot_s8(q, x[m]);
+  } else if (FMT == IQ4_NL) {
+    const uint4 qa = *reinterpret_cast<const uint4 *>(qrow + uu * 16);
+    uint32_t q[8];
+    const uint32_t words[4] = {qa.x, qa.y, qa.z, qa.w};
+#pragma unroll
+    for (int wd = 0; wd < 4; ++wd) iq4_lookup(words[wd], lut, q[2 * wd], q[2 * wd + 1]);
+#pragma unroll
+    for (int m = 0; m < MR; ++m) part[m] = (sm.x * x[m].dx) * (float)dot_s8(q, x[m]);
+  } else {  // Q4_K, Q4_0: nibble pairs
+    const uint4 qa = *reinterpret_cast<const uint4 *>(qrow + uu * 16);
+#pragma unroll
+    for (int m = 0; m < MR; ++m)
+      part[m] = (sm.x * x[m].dx) * (float)dot_nib(qa, x[m]) - sm.y * x[m].sum;
+  }
+}
+
+// Partial dot products of one run (uu) of RPT weight rows with MR activation
+// rows.  The rows' quant words and decoded factors are loaded first; the
+// integer dot products then run word by word across all rows, so 2 * RPT * MR
+// independent dp4a chains interleave instead of two per row.  Row i's quants
+// start at q + i * q_stride, its factors at dec[i * dec_stride].
+template <int FMT, int MR, int RPT>
+__device__ __forceinline__ void rows_partials(const uint8_t *q, size_t q_stride, const float2 *dec,
+                                              size_t dec_stride, int uu, const XRun (&x)[MR],
+                                              const uint32_t lut[4], float (&part)[RPT * MR]) {
+  int sh[RPT][MR], sl[RPT][MR];
+  float2 sm[RPT];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) {
+    sm[i] = dec[(size_t)i * dec_stride];
+#pragma unroll
+    for (int m = 0; m < MR; ++m) sh[i][m] = sl[i][m] = 0;
+  }
+  if (FMT == Q8_0) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {  // 16 bytes of each row's run at a time
+      uint4 qa[RPT];
+#pragma unroll
+      for (int i = 0; i < RPT; ++i)
+        qa[i] = *reinterpret_cast<const uint4 *>(q + (size_t)i * q_stride + uu * 32 + 16 * h);
+#pragma unroll
+      for (int wd = 0; wd < 4; ++wd)
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) {
+          const uint32_t v = wd == 0 ? qa[i].x : wd == 1 ? qa[i].y : wd == 2 ? qa[i].z : qa[i].w;
+#pragma unroll
+          for (int m = 0; m < MR; ++m) {
+            sh[i][m] = dp4a_ss(v, x[m].hi[4 * h + wd], sh[i][m]);
+            sl[i][m] = dp4a_su(v, x[m].lo[4 * h + wd], sl[i][m]);
+          }
+        }
+    }
+  } else {
+    uint4 qa[RPT];
+#pragma unroll
+    for (int i = 0; i < RPT; ++i)
+      qa[i] = *reinterpret_cast<const uint4 *>(q + (size_t)i * q_stride + uu * 16);
+#pragma unroll
+    for (int wd = 0; wd < 4; ++wd)
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) {
+        const uint32_t v = wd == 0 ? qa[i].x : wd == 1 ? qa[i].y : wd == 2 ? qa[i].z : qa[i].w;
+        if (FMT == IQ4_NL) {
+          uint32_t c0, c1;  // codebook bytes of values 8wd + 0..3 and 8wd + 4..7
+          iq4_lookup(v, lut, c0, c1);
+#pragma unroll
+          for (int m = 0; m < MR; ++m) {
+            sh[i][m] = dp4a_ss(c0, x[m].hi[2 * wd], sh[i][m]);
+            sh[i][m] = dp4a_ss(c1, x[m].hi[2 * wd + 1], sh[i][m]);
+            sl[i][m] = dp4a_su(c0, x[m].lo[2 * wd], sl[i][m]);
+            sl[i][m] = dp4a_su(c1, x[m].lo[2 * wd + 1], sl[i][m]);
+          }
+        } else {  // Q4_K, Q4_0: nibble pairs
+          const uint32_t ev = v & 0x0F0F0F0Fu;         // values 8wd + 0, 2, 4, 6
+          const uint32_t od = (v >> 4) & 0x0F0F0F0Fu;  // values 8wd + 1, 3, 5, 7
+#pragma unroll
+          for (int m = 0; m < MR; ++m) {
+            sh[i][m] = dp4a_us(ev, x[m].hi[2 * wd], sh[i][m]);
+            sh[i][m] = dp4a_us(od, x[m].hi[2 * wd + 1], sh[i][m]);
+            sl[i][m] = dp4a_uu(ev, x[m].lo[2 * wd], sl[i][m]);
+            sl[i][m] = dp4a_uu(od, x[m].lo[2 * wd + 1], sl[i][m]);
+          }
+        }
+      }
+  }
+#pragma unroll
+  for (int i = 0; i < RPT; ++i)
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      const float dot = (float)(sh[i][m] * 256 + sl[i][m]);
+      if (FMT == Q4_K || FMT == Q4_0)
+        part[i * MR + m] = (sm[i].x * x[m].dx) * dot - sm[i].y * x[m].sum;
+      else
+        part[i * MR + m] = (sm[i].x * x[m].dx) * dot;
+    }
+}
+
 template <int FMT, int MR>
 __device__ __forceinline__ void load_x(const float *__restrict__ x, int k, int u, bool active,
                                        XRun (&xr)[MR]) {
@@ -235,7 +371,10 @@ __host__ __device__ inline uint64_t xpack_bytes(uint64_t m, uint64_t k) {
 // The consumer threads (ct of nthreads, a multiple of 32) pack the m rows of x:
 // four lanes per run, each packing 8 of its values into 2 high and 2 low words
 // (words 2p, 2p+1 hold values 8p..8p+7 in either order); the run's max |x|
-// and sum come from a 4-lane shuffle.
+// and sum come from a 4-lane shuffle.  Each pass covers two tasks per thread
+// and issues the loads of both before packing either, so a pass costs one
+// memory round trip (one pass for k <= 4096 at one activation row).  x is
+// global memory or the kernel's shared-memory copy of it.
 template <bool PAIR>
 __device__ __forceinline__ void pack_x_to_smem(const float *__restrict__ x, int m, int k, int ct,
                                                int nthreads, uint32_t *xs) {
@@ -243,47 +382,61 @@ __device__ __forceinline__ void pack_x_to_smem(const float *__restrict__ x, int 
   const int total = m * runs * 4;
   uint32_t *hi = xs, *lo = xs + (size_t)m * 8 * runs;
   float *dx = reinterpret_cast<float *>(xs + (size_t)m * 16 * runs), *sum = dx + (size_t)m * runs;
-  for (int base = 0; base < total; base += nthreads) {
-    const int t = base + ct;
-    const int p = t & 3, ru = t >> 2;
-    const bool live = t < total;  // whole 4-lane groups are live or not
-    const int row = live ? ru / runs : 0, u = live ? ru % runs : 0;
-    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (live) {
-      const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)row * k + (size_t)u * 32 + 8 * p);
-      const float4 a = __ldg(src), b = __ldg(src + 1);
-      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-    }
-    float amax = 0.f, s = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+  for (int base = 0; base < total; base += 2 * nthreads) {
+    float v[2][8];
+    bool live[2];
+    int row[2], u[2];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-#pragma unroll
-    for (int off = 1; off < 4; off <<= 1) {
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-      s += __shfl_xor_sync(0xffffffffu, s, off);
-    }
-    if (!live) continue;
-    const float inv = amax > 0.f ? 32767.f / amax : 0.f;
-    uint32_t h[2] = {0, 0}, l[2] = {0, 0};
-#pragma unroll
-    for (int wd = 0; wd < 2; ++wd)
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const int e = PAIR ? 2 * b + wd : 4 * wd + b;
-        int q = __float2int_rn(v[e] * inv);
-        q = max(-32767, min(32767, q));
-        h[wd] |= (uint32_t)((q >> 8) & 0xff) << (8 * b);
-        l[wd] |= (uint32_t)(q & 0xff) << (8 * b);
+    for (int h = 0; h < 2; ++h) {
+      const int t = base + h * nthreads + ct;
+      const int ru = t >> 2;
+      live[h] = t < total;  // whole 4-lane groups are live or not
+      row[h] = live[h] ? ru / runs : 0;
+      u[h] = live[h] ? ru % runs : 0;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+      if (live[h]) {
+        const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)row[h] * k +
+                                                             (size_t)u[h] * 32 + 8 * (t & 3));
+        a = src[0];
+        b = src[1];
       }
-#pragma unroll
-    for (int wd = 0; wd < 2; ++wd) {
-      hi[((size_t)row * 8 + 2 * p + wd) * runs + u] = h[wd];
-      lo[((size_t)row * 8 + 2 * p + wd) * runs + u] = l[wd];
+      v[h][0] = a.x; v[h][1] = a.y; v[h][2] = a.z; v[h][3] = a.w;
+      v[h][4] = b.x; v[h][5] = b.y; v[h][6] = b.z; v[h][7] = b.w;
     }
-    if (p == 0) {
-      dx[(size_t)row * runs + u] = amax / 32767.f;
-      sum[(size_t)row * runs + u] = s;
+    const int p = ct & 3;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float amax = 0.f;
+      float s = ((v[h][0] + v[h][1]) + (v[h][2] + v[h][3])) + ((v[h][4] + v[h][5]) + (v[h][6] + v[h][7]));
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[h][i]));
+#pragma unroll
+      for (int off = 1; off < 4; off <<= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        s += __shfl_xor_sync(0xffffffffu, s, off);
+      }
+      if (!live[h]) continue;
+      const float inv = amax > 0.f ? 32767.f / amax : 0.f;
+      uint32_t hw[2] = {0, 0}, lw[2] = {0, 0};
+#pragma unroll
+      for (int wd = 0; wd < 2; ++wd)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const int e = PAIR ? 2 * b + wd : 4 * wd + b;
+          int q = __float2int_rn(v[h][e] * inv);
+          q = max(-32767, min(32767, q));
+          hw[wd] |= (uint32_t)((q >> 8) & 0xff) << (8 * b);
+          lw[wd] |= (uint32_t)(q & 0xff) << (8 * b);
+        }
+#pragma unroll
+      for (int wd = 0; wd < 2; ++wd) {
+        hi[((size_t)row[h] * 8 + 2 * p + wd) * runs + u[h]] = hw[wd];
+        lo[((size_t)row[h] * 8 + 2 * p + wd) * runs + u[h]] = lw[wd];
+      }
+      if (p == 0) {
+        dx[(size_t)row[h] * runs + u[h]] = amax / 32767.f;
+        sum[(size_t)row[h] * runs + u[h]] = s;
+      }
     }
   }
 }
@@ -332,33 +485,39 @@ __device__ __forceinline__ float warp_sum_transpose(float (&v)[NV], int lane) {
 
 // ---- main kernel: bulk-copy staged, persistent ----------------------------------------
 
-constexpr int RPT = 4;  // rows per team per stage
+// Rows per team per stage: 8 for one activation row (16 independent integer
+// dot chains per thread), 4 for two.
+template <int MR>
+__host__ __device__ constexpr int rows_per_team() { return MR == 1 ? 8 : 4; }
 
 struct GemvStaged {
   int n, k;
   int teams, team_warps;  // consumer geometry
-  int stages;
+  int stages;             // ring slots (never more than a CTA's stages of work)
   int chunk;              // stages per reduction pass
   int rows_per_cta;
   uint32_t stage_bytes, qs_stage_bytes;
+  uint32_t dec_stage_bytes;  // decoded run factors of one stage: rows * runs * 8
   int addend_mode;
   const float *addend;
   float *y;
   int *err;
 };
 
-template <int FMT, int MR, int MAXT>
-__global__ void __launch_bounds__(MAXT, 1)
+template <int FMT, int MR, int MAXT, int MINB>
+__global__ void __launch_bounds__(MAXT, MINB)
     gemv_staged_kernel(const uint8_t *__restrict__ w, const float *__restrict__ x,
                        const GemvStaged p) {
+  constexpr int RPT = rows_per_team<MR>();
   extern __shared__ __align__(128) uint8_t smem[];
   const Layout L(FMT, (uint64_t)p.n, (uint64_t)p.k);
   const int S = p.stages;
   const int TR = p.teams * RPT;  // rows per stage
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * p.stage_bytes);
+  const int runs = p.k / RUN;
+  float2 *dec = reinterpret_cast<float2 *>(smem + (size_t)S * p.stage_bytes);  // [S][TR][runs]
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * (p.stage_bytes + p.dec_stage_bytes));
   uint64_t *empty = full + S;
-  uint32_t *xs = reinterpret_cast<uint32_t *>(empty + S);  // packed activations (xpack_bytes)
-  float *red = reinterpret_cast<float *>(xs + xpack_bytes(MR, p.k) / 4);  // [teams][chunk][RPT][team_warps][MR]
+  float *red = reinterpret_cast<float *>(empty + S);  // [teams][chunk][RPT][team_warps][MR]
   const int consumer_warps = p.teams * p.team_warps;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = blockIdx.x * p.rows_per_cta;
@@ -380,7 +539,7 @@ __global__ void __launch_bounds__(MAXT, 1)
       int issued = 0;
       for (int g = 0; g < nstages; ++g) {
         const int s = g % S;
-        if (g >= S && !mbar_wait(&empty[s], ((g / S) - 1) & 1, p.err)) break;
+        if (g >= S && !mbar_wait_backoff(&empty[s], ((g / S) - 1) & 1, p.err, 64)) break;
         const int row = r0 + g * TR;
         const int rows = min(TR, r1 - row);
         uint8_t *st = smem + (size_t)s * p.stage_bytes;
@@ -392,7 +551,7 @@ __global__ void __launch_bounds__(MAXT, 1)
       }
       // every copy issued has landed before the CTA may exit
       for (int g = (issued > S ? issued - S : 0); g < issued; ++g)
-        mbar_wait(&full[g % S], (g / S) & 1, nullptr);
+        mbar_wait_backoff(&full[g % S], (g / S) & 1, nullptr);
     }
     return;
   }
@@ -401,58 +560,76 @@ __global__ void __launch_bounds__(MAXT, 1)
   const int cw = warp - 1;
   const int team = cw / p.team_warps, tw = cw % p.team_warps;
   const int u = tw * 32 + lane;  // this thread's run of K
-  const int runs = p.k / RUN;
   const bool active = u < runs;
+  const int uu = active ? u : 0;  // idle lanes read a valid run; their result is dropped
   const int team_threads = p.team_warps * 32;
   float *red_team = red + (size_t)team * p.chunk * RPT * p.team_warps * MR;
-
-  // x may be the previous kernel's output; the weight stream above never waits
-  grid_dependency_wait();
-  constexpr bool pair = FMT == Q4_K || FMT == Q4_0;
-  pack_x_to_smem<pair>(x, MR, p.k, threadIdx.x - 32, consumer_warps * 32, xs);
-  named_barrier(15, consumer_warps * 32);
-  XRun xr[MR];
-  load_packed_x<MR>(xs, p.k, u, active, xr);
-  uint32_t lut[4] = {0, 0, 0, 0};
-  if (FMT == IQ4_NL) iq4_table(lut);
-  const int uu = active ? u : 0;  // idle lanes read a valid run; their result is dropped
 
   // A wait that gives up records the error and the thread stops waiting, but
   // it keeps stepping through every stage so its team's named barriers match.
   bool ok = true;
+  auto wait_stage = [&](int g, uint32_t max_ns) {
+    // lane 0 polls (sleeping between polls: a co-resident kernel may be
+    // computing); once the phase is complete every lane's own try_wait
+    // succeeds at once and acquires the bulk-copied bytes for that lane
+    if (lane == 0) ok = ok && mbar_wait_backoff(&full[g % S], (g / S) & 1, p.err, max_ns);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (ok) ok = mbar_try_wait(&full[g % S], (g / S) & 1);
+  };
+  // Each thread decodes the factors of its own run of its team's rows of
+  // stage g into its own slots (no other thread reads them: no barrier).
+  auto decode_stage = [&](int g) {
+    const int s = g % S;
+    const uint8_t *sc = smem + (size_t)s * p.stage_bytes + p.qs_stage_bytes;
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+      const int lr = team * RPT + i;
+      if (active) dec[((size_t)s * TR + lr) * runs + u] = decode_run_scale<FMT>(sc + (size_t)lr * L.sc_row, u);
+    }
+  };
+
+  // Before the activations can be read: decode the run factors of the stages
+  // already in flight (they land while the previous kernel drains).
+  const int pre = min(S, nstages);
+  for (int g = 0; g < pre; ++g) {
+    wait_stage(g, 256);
+    decode_stage(g);
+  }
+
+  // x may be the previous kernel's output; the weight stream above never
+  // waits.  One warp waits for the previous grid (its completion, its memory
+  // made visible to this grid); the others block on a hardware barrier
+  // meanwhile, so no warp of this CTA spins while the previous kernel still
+  // computes on the SM.  The barrier orders every thread's x loads and y
+  // stores after that wait.  Each thread then loads and quantises its own run
+  // of x.
+  if (cw == 0) grid_dependency_wait();
+  named_barrier(14, consumer_warps * 32);
+  XRun xr[MR];
+  load_x<FMT, MR>(x, p.k, u, active, xr);
+  uint32_t lut[4] = {0, 0, 0, 0};
+  if (FMT == IQ4_NL) iq4_table(lut);
+
   for (int g = 0; g < nstages; ++g) {
     const int s = g % S;
-    // lane 0 polls; once the phase is complete every lane's own try_wait
-    // succeeds at once and acquires the bulk-copied bytes for that lane
-    if (lane == 0) ok = ok && mbar_wait(&full[s], (g / S) & 1, p.err);
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    if (ok) ok = mbar_try_wait(&full[s], (g / S) & 1);
+    if (g >= pre) {
+      wait_stage(g, 64);
+      decode_stage(g);
+    }
     const uint8_t *st = smem + (size_t)s * p.stage_bytes;
     const int row0 = r0 + g * TR;
     // branch-free over the team's RPT rows (rows past the end of a partial
     // stage read stale stage bytes and are dropped), so their loads and
     // integer dot products interleave
     float part[RPT * MR];
+    rows_partials<FMT, MR, RPT>(st + (size_t)team * RPT * L.qs_row, L.qs_row,
+                                dec + ((size_t)s * TR + team * RPT) * runs + uu, runs, uu, xr, lut,
+                                part);
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
-      const int lr = team * RPT + i;  // row within the stage
-      const uint8_t *qrow = st + (size_t)lr * L.qs_row;
-      const uint8_t *srow = st + p.qs_stage_bytes + (size_t)lr * L.sc_row;
-      uint4 qa, qb = make_uint4(0, 0, 0, 0), hd = make_uint4(0, 0, 0, 0);
-      uint32_t dh = 0;
-      if (FMT == Q8_0) {
-        qa = *reinterpret_cast<const uint4 *>(qrow + uu * 32);
-        qb = *reinterpret_cast<const uint4 *>(qrow + uu * 32 + 16);
-      } else {
-        qa = *reinterpret_cast<const uint4 *>(qrow + uu * 16);
-      }
-      if (FMT == Q4_K) hd = *reinterpret_cast<const uint4 *>(srow + (uu >> 3) * 16);
-      else dh = *reinterpret_cast<const uint16_t *>(srow + uu * 2);
-      float pm[MR];
-      run_partials<FMT, MR>(qa, qb, hd, dh, uu & 7, xr, lut, pm);
-      const bool keep = ok && active && row0 + lr < r1;
+      const bool keep = ok && active && row0 + team * RPT + i < r1;
 #pragma unroll
-      for (int m = 0; m < MR; ++m) part[i * MR + m] = keep ? pm[m] : 0.f;
+      for (int m = 0; m < MR; ++m) part[i * MR + m] = keep ? part[i * MR + m] : 0.f;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the stage's bytes
@@ -476,8 +653,8 @@ __global__ void __launch_bounds__(MAXT, 1)
           float sum = 0.f;
           for (int wi = 0; wi < p.team_warps; ++wi)
             sum += red_team[((cc * RPT + i) * p.team_warps + wi) * MR + m];
-          if (p.addend_mode == 1) sum = sum + p.addend[row];
-          else if (p.addend_mode == 2) sum = sum + p.addend[(size_t)m * p.n + row];
+          if (p.addend_mode == 1) sum = sum + __ldcg(p.addend + row);
+          else if (p.addend_mode == 2) sum = sum + __ldcg(p.addend + (size_t)m * p.n + row);
           p.y[(size_t)m * p.n + row] = sum;
         }
       }
@@ -575,13 +752,20 @@ static cudaError_t launch_dependent(K kern, dim3 grid, dim3 block, size_t smem,
 
 // The staged GEMV: a programmatic dependent of whatever precedes it on the
 // stream (its weight stream starts at once; it waits before reading x).
-template <int FMT, int MR, int MAXT>
-static cudaError_t launch_staged(const void *w, int n, int k, const float *x, float *y,
-                                 const float *addend, int addend_mode, int *err, int sms,
-                                 cudaStream_t stream) {
+constexpr size_t MAX_SMEM = 227 * 1024;
+// Shared memory of one CTA when two kernels' CTAs are to share an SM (the next
+// GEMV on the stream streams its weights while this one computes).
+constexpr size_t CORESIDENT_SMEM = 112 * 1024;
+
+// Geometry and shared-memory size of a staged launch.  One CTA per SM with 8
+// consumer warps (k <= 8192) or one team of up to 31 warps (larger k); rows
+// split evenly; a CTA's last stage may hold fewer than TR rows; the ring
+// never has more slots than a CTA has stages.
+template <int FMT, int MR>
+static size_t staged_config(int n, int k, int sms, GemvStaged &p, int &grid, int &threads) {
+  constexpr int RPT = rows_per_team<MR>();
   const Layout L(FMT, (uint64_t)n, (uint64_t)k);
   const int runs = k / RUN;
-  GemvStaged p;
   p.n = n;
   p.k = k;
   p.team_warps = (runs + 31) / 32;
@@ -589,36 +773,52 @@ static cudaError_t launch_staged(const void *w, int n, int k, const float *x, fl
   const int TR = p.teams * RPT;
   p.qs_stage_bytes = (uint32_t)ceil_div((uint64_t)TR * L.qs_row, 128) * 128;
   p.stage_bytes = p.qs_stage_bytes + (uint32_t)ceil_div((uint64_t)TR * L.sc_row, 128) * 128;
-  // Two CTAs per SM when they fit (more consumer warps to hide latency), each
-  // within ~110 KB of shared memory.  Rows split evenly; a CTA's last stage
-  // may hold fewer than TR rows.
-  const uint64_t fixed = xpack_bytes(MR, (uint64_t)k) + 2048;
-  const uint64_t budget = 110 * 1024 > fixed ? 110 * 1024 - fixed : 0;
-  int stages = (int)(budget / p.stage_bytes);
-  if (stages > 8) stages = 8;
-  if (stages < 2) stages = 2;
-  p.stages = stages;
-  const int threads = 32 * (1 + p.teams * p.team_warps);
-  const int per_sm = threads <= 512 ? 2 : 1;
+  p.dec_stage_bytes = (uint32_t)(TR * runs * 8);
+  threads = 32 * (1 + p.teams * p.team_warps);
   const int units = (int)ceil_div((uint64_t)n, (uint64_t)TR);
-  int grid = sms * per_sm;
+  grid = sms;
   if (grid > units) grid = units;
   p.rows_per_cta = (int)ceil_div((uint64_t)n, (uint64_t)grid);
   grid = (int)ceil_div((uint64_t)n, (uint64_t)p.rows_per_cta);
-  // reduction buffer: as many stages as fit in 16 KB (usually all of a CTA's)
   const int nst = (int)ceil_div((uint64_t)p.rows_per_cta, (uint64_t)TR);
+  // reduction buffer: as many stages as fit in 16 KB (usually all of a CTA's)
   const size_t red_stage = sizeof(float) * (size_t)p.teams * RPT * p.team_warps * MR;
   int chunk = (int)(16384 / red_stage);
   if (chunk > nst) chunk = nst;
   if (chunk < 1) chunk = 1;
   p.chunk = chunk;
+  const size_t fixed = red_stage * chunk;
+  const size_t per_stage = (size_t)p.stage_bytes + p.dec_stage_bytes + 16;
+  const size_t budget = CORESIDENT_SMEM > fixed ? CORESIDENT_SMEM - fixed : 0;
+  int stages = (int)(budget / per_stage);
+  if (stages > 8) stages = 8;
+  if (stages > nst) stages = nst;
+  if (stages < 1) stages = 1;
+  p.stages = stages;
+  return (size_t)stages * per_stage + fixed;
+}
+
+template <int FMT, int MR>
+static bool staged_fits(int n, int k, int sms) {
+  GemvStaged p;
+  int grid, threads;
+  return staged_config<FMT, MR>(n, k, sms, p, grid, threads) <= MAX_SMEM;
+}
+
+// The staged GEMV: a programmatic dependent of whatever precedes it on the
+// stream (its weight stream starts at once; it waits before reading x).
+template <int FMT, int MR, int MAXT, int MINB>
+static cudaError_t launch_staged(const void *w, int n, int k, const float *x, float *y,
+                                 const float *addend, int addend_mode, int *err, int sms,
+                                 cudaStream_t stream) {
+  GemvStaged p;
+  int grid, threads;
+  const size_t smem = staged_config<FMT, MR>(n, k, sms, p, grid, threads);
   p.addend_mode = addend_mode;
   p.addend = addend;
   p.y = y;
   p.err = err;
-  const size_t smem = (size_t)stages * p.stage_bytes + 2 * 8 * (size_t)stages +
-                      xpack_bytes(MR, (uint64_t)k) + red_stage * chunk;
-  auto kern = gemv_staged_kernel<FMT, MR, MAXT>;
+  auto kern = gemv_staged_kernel<FMT, MR, MAXT, MINB>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   return launch_dependent(kern, dim3((unsigned)grid), dim3((unsigned)threads), smem, stream,
@@ -650,14 +850,17 @@ static cudaError_t launch_fmt(const void *w, int n, int k, const float *x, float
                               const float *addend, int addend_mode, int *err, int sms,
                               cudaStream_t stream) {
   if (staged_ok((uint64_t)k)) {  // a team of at most 31 warps plus the producer
-    if (k <= 8192)
-      return launch_staged<FMT, MR, 288>(w, n, k, x, y, addend, addend_mode, err, sms, stream);
-    // 1024-thread CTAs have 64 registers per thread: one activation row per launch
-    cudaError_t e = launch_staged<FMT, 1, 1024>(w, n, k, x, y, addend, addend_mode, err, sms, stream);
-    if (MR == 2 && e == cudaSuccess)
-      e = launch_staged<FMT, 1, 1024>(w, n, k, x + k, y + n, addend_mode == 2 ? addend + n : addend,
-                                      addend_mode, err, sms, stream);
-    return e;
+    // 288 threads with at most 112 registers each: two kernels' CTAs fit on an SM
+    if (k <= 8192 && staged_fits<FMT, MR>(n, k, sms))
+      return launch_staged<FMT, MR, 288, 2>(w, n, k, x, y, addend, addend_mode, err, sms, stream);
+    if (k > 8192 && staged_fits<FMT, 1>(n, k, sms)) {
+      // 1024-thread CTAs have 64 registers per thread: one activation row per launch
+      cudaError_t e = launch_staged<FMT, 1, 1024, 1>(w, n, k, x, y, addend, addend_mode, err, sms, stream);
+      if (MR == 2 && e == cudaSuccess)
+        e = launch_staged<FMT, 1, 1024, 1>(w, n, k, x + k, y + n, addend_mode == 2 ? addend + n : addend,
+                                           addend_mode, err, sms, stream);
+      return e;
+    }
   }
   if (k <= 256 * 32) return launch_simple<FMT, MR, 4, 256>(w, n, k, x, y, addend, addend_mode, sms, stream);
   cudaError_t e = launch_simple<FMT, 1, 2, 1024>(w, n, k, x, y, addend, addend_mode, sms, stream);
