@@ -485,10 +485,14 @@ __device__ __forceinline__ float warp_sum_transpose(float (&v)[NV], int lane) {
 
 // ---- main kernel: bulk-copy staged, persistent ----------------------------------------
 
-// Rows per team per stage: 8 for one activation row (16 independent integer
-// dot chains per thread), 4 for two.
-template <int MR>
-__host__ __device__ constexpr int rows_per_team() { return MR == 1 ? 8 : 4; }
+// Rows per team per stage: 8 for one activation row of a 4-bit format in a
+// 288-thread CTA (16 independent integer dot chains per thread), otherwise 4
+// (two activation rows; Q8_0's twice larger rows, which would leave room for
+// one ring slot; or the 64 registers of a 1024-thread CTA).
+template <int FMT, int MR, int MAXT>
+__host__ __device__ constexpr int rows_per_team() {
+  return MR == 1 && FMT != Q8_0 && MAXT <= 288 ? 8 : 4;
+}
 
 struct GemvStaged {
   int n, k;
@@ -508,7 +512,7 @@ template <int FMT, int MR, int MAXT, int MINB>
 __global__ void __launch_bounds__(MAXT, MINB)
     gemv_staged_kernel(const uint8_t *__restrict__ w, const float *__restrict__ x,
                        const GemvStaged p) {
-  constexpr int RPT = rows_per_team<MR>();
+  constexpr int RPT = rows_per_team<FMT, MR, MAXT>();
   extern __shared__ __align__(128) uint8_t smem[];
   const Layout L(FMT, (uint64_t)p.n, (uint64_t)p.k);
   const int S = p.stages;
@@ -761,9 +765,9 @@ constexpr size_t CORESIDENT_SMEM = 112 * 1024;
 // consumer warps (k <= 8192) or one team of up to 31 warps (larger k); rows
 // split evenly; a CTA's last stage may hold fewer than TR rows; the ring
 // never has more slots than a CTA has stages.
-template <int FMT, int MR>
+template <int FMT, int MR, int MAXT>
 static size_t staged_config(int n, int k, int sms, GemvStaged &p, int &grid, int &threads) {
-  constexpr int RPT = rows_per_team<MR>();
+  constexpr int RPT = rows_per_team<FMT, MR, MAXT>();
   const Layout L(FMT, (uint64_t)n, (uint64_t)k);
   const int runs = k / RUN;
   p.n = n;
@@ -798,11 +802,11 @@ static size_t staged_config(int n, int k, int sms, GemvStaged &p, int &grid, int
   return (size_t)stages * per_stage + fixed;
 }
 
-template <int FMT, int MR>
+template <int FMT, int MR, int MAXT>
 static bool staged_fits(int n, int k, int sms) {
   GemvStaged p;
   int grid, threads;
-  return staged_config<FMT, MR>(n, k, sms, p, grid, threads) <= MAX_SMEM;
+  return staged_config<FMT, MR, MAXT>(n, k, sms, p, grid, threads) <= MAX_SMEM;
 }
 
 // The staged GEMV: a programmatic dependent of whatever precedes it on the
@@ -813,7 +817,7 @@ static cudaError_t launch_staged(const void *w, int n, int k, const float *x, fl
                                  cudaStream_t stream) {
   GemvStaged p;
   int grid, threads;
-  const size_t smem = staged_config<FMT, MR>(n, k, sms, p, grid, threads);
+  const size_t smem = staged_config<FMT, MR, MAXT>(n, k, sms, p, grid, threads);
   p.addend_mode = addend_mode;
   p.addend = addend;
   p.y = y;
@@ -851,9 +855,9 @@ static cudaError_t launch_fmt(const void *w, int n, int k, const float *x, float
                               cudaStream_t stream) {
   if (staged_ok((uint64_t)k)) {  // a team of at most 31 warps plus the producer
     // 288 threads with at most 112 registers each: two kernels' CTAs fit on an SM
-    if (k <= 8192 && staged_fits<FMT, MR>(n, k, sms))
+    if (k <= 8192 && staged_fits<FMT, MR, 288>(n, k, sms))
       return launch_staged<FMT, MR, 288, 2>(w, n, k, x, y, addend, addend_mode, err, sms, stream);
-    if (k > 8192 && staged_fits<FMT, 1>(n, k, sms)) {
+    if (k > 8192 && staged_fits<FMT, 1, 1024>(n, k, sms)) {
       // 1024-thread CTAs have 64 registers per thread: one activation row per launch
       cudaError_t e = launch_staged<FMT, 1, 1024, 1>(w, n, k, x, y, addend, addend_mode, err, sms, stream);
       if (MR == 2 && e == cudaSuccess)
