@@ -191,6 +191,7 @@ def run_b200(args) -> None:
 
     import magnetar_b200 as mgb
     import synthetic
+    import tp
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -204,16 +205,15 @@ def run_b200(args) -> None:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
-    if N % world:
-        raise SystemExit(f"N={N} does not split over {world} ranks")
-    n_loc = N // world
+    lo, hi = tp.shard_bounds(N, world, rank)
+    n_loc = hi - lo
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
     fmt = mgb.Q4_K
 
     # weights: this rank's stored rows, in the device layout, rotated over R copies
     full = synthetic.packed_weights(fmt, N, K)
-    w_loc = synthetic.row_slice(fmt, full, K, np.arange(rank * n_loc, (rank + 1) * n_loc))
+    w_loc = np.array(tp.shard_packed(fmt, full, N, K, world, rank))
     del full
     w_bytes = mgb.packed_bytes(fmt, n_loc, K)
     set_bytes = w_bytes + M * K * 4 + M * n_loc * 4
@@ -230,16 +230,13 @@ def run_b200(args) -> None:
     Y = [torch.empty((M, n_loc), dtype=torch.float32, device=dev) for _ in range(R)]
     ws_bytes = mgb.qmatmul_workspace_bytes(fmt, M, n_loc, K)
     WS = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-    gathered = torch.empty((world, M, n_loc), dtype=torch.float32, device=dev) if world > 1 else None
-    Y_full = torch.empty((M, N), dtype=torch.float32, device=dev) if world > 1 else None
 
     def step(i: int) -> None:
         s = i % R
         mgb.qmatmul(fmt, W[s].data_ptr(), n_loc, K, X[s].data_ptr(), M, Y[s].data_ptr(),
                     workspace_ptr=WS.data_ptr(), workspace_bytes=ws_bytes, stream=sp)
         if world > 1:
-            dist.all_gather_into_tensor(gathered.view(-1), Y[s].view(-1))
-            Y_full.view(M, world, n_loc).copy_(gathered.transpose(0, 1))
+            tp.gather_columns(Y[s])  # [M, N] on every rank
 
     def timed(fn, steps: int, warmup: int) -> float:
         for i in range(warmup):

@@ -161,7 +161,7 @@ __device__ __forceinline__ bool mbar_wait_backoff(uint64_t *bar, uint32_t parity
 }
 
 // 1-D bulk copy global -> shared, completing `bytes` on `bar`.  Both addresses
-// 16-byte aligned, bytes a multiple of 16 (no multicast).
+// 16-byte aligned, bytes a multiple of 16 (this CTA's shared memory only).
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
                                          uint64_t *bar) {
   asm volatile(

@@ -26,7 +26,7 @@
 //              (K-major, SWIZZLE_128B written by hand), fence the async proxy
 //              and arrive on b_full[s] and p_empty[s]; after the last stage
 //              they drain TMEM with tcgen05.ld and write y (+ the addend).
-// No TMA multicast anywhere: every CTA loads its own tiles from local HBM.
+// Every CTA loads its own tiles from this GPU's HBM (no cluster-shared loads).
 // Every wait is bounded; on expiry the kernel records ERR_WAIT_TIMEOUT, skips
 // the remaining work, waits (bounded) for its own copies and MMAs, frees TMEM
 // and returns.
