@@ -6,26 +6,26 @@
 //
 // CTA tile: BM activation rows (1 or 2 accumulators of 128 rows) x BN weight
 // rows (the MMA N, <= 256, a multiple of 16), K in steps of 64 (one 128-byte
-// swizzle atom of bf16).  Three shared-memory rings, each as deep as its
-// producer's latency needs: activation tiles (from L2, 4 stages, released by
-// the MMA), bf16 W tiles (made on chip, 2 stages, released by the MMA) and
-// packed W (quant and scale boxes from HBM, 3+ stages, released by the
-// dequantising warps), so neither operand waits on a memory round trip.
-// Launched as a programmatic dependent: everything but the activation loads
-// (TMEM, barriers, the weight stream, dequantisation) overlaps the previous
-// kernel on the stream.  Warp roles, 352 threads:
+// swizzle atom of bf16).  Two shared-memory rings: operand stages (the
+// activation tile and the bf16 W tile of a K step, 3 deep), each with one
+// `full` barrier (the activation TMA bytes + one arrival per dequantising
+// warp) and one `empty` barrier (the MMAs' commit), so the MMA issuer waits
+// and commits once per step; and packed-W stages (quant and scale boxes from
+// HBM, 3+ deep, released by the dequantising warps).  Launched as a
+// programmatic dependent: everything but the activation loads (TMEM, barriers,
+// the weight stream, dequantisation) overlaps the previous kernel on the
+// stream.  Warp roles, 352 threads:
 //   warp 0     TMA producer of the bf16 activation boxes (SWIZZLE_128B,
-//              straight into the UMMA operand layout) on a_full[s], after
+//              straight into the UMMA operand layout) on full[s], after
 //              griddepcontrol.wait.  Owns the TMEM allocation.
 //   warp 1     one thread issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32)
-//              per 16-wide K slice and commits each step to a_empty[s] and
-//              b_empty[s].
+//              per 16-wide K slice and commits each step to empty[s].
 //   warp 2     TMA producer of the packed W quant and scale boxes (no
 //              swizzle) on p_full[s].
 //   warps 3-10 dequantise the staged packed W into the bf16 B operand
 //              (K-major, SWIZZLE_128B written by hand), fence the async proxy
-//              and arrive on b_full[s] and p_empty[s]; after the last stage
-//              they drain TMEM with tcgen05.ld and write y (+ the addend).
+//              and arrive on full[s] and p_empty[s]; after the last stage they
+//              drain TMEM with tcgen05.ld and write y (+ the addend).
 // Every CTA loads its own tiles from this GPU's HBM (no cluster-shared loads).
 // Every wait is bounded; on expiry the kernel records ERR_WAIT_TIMEOUT, skips
 // the remaining work, waits (bounded) for its own copies and MMAs, frees TMEM
@@ -242,16 +242,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   // 1024-byte align the operand area (SWIZZLE_128B atoms).
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  const int SA = p.astages, SB = p.bstages, SP = p.pstages;
-  uint8_t *a0 = smem;                                    // SA activation tiles
-  uint8_t *b0 = a0 + (size_t)SA * p.a_bytes;             // SB bf16 W tiles
-  uint8_t *pk0 = b0 + (size_t)SB * p.b_bytes;            // SP packed W (quant box, scale box)
+  const int S = p.astages, SP = p.pstages;
+  uint8_t *a0 = smem;                                    // S activation tiles
+  uint8_t *b0 = a0 + (size_t)S * p.a_bytes;              // S bf16 W tiles
+  uint8_t *pk0 = b0 + (size_t)S * p.b_bytes;             // SP packed W (quant box, scale box)
   uint64_t *bars = reinterpret_cast<uint64_t *>(pk0 + (size_t)SP * p.pstage_bytes);
-  uint64_t *a_full = bars;              // activation tile landed (TMA bytes)
-  uint64_t *a_empty = a_full + SA;      // MMA finished reading it
-  uint64_t *b_full = a_empty + SA;      // bf16 W tile written (DQ_THREADS arrivals)
-  uint64_t *b_empty = b_full + SB;      // MMA finished reading it
-  uint64_t *p_full = b_empty + SB;      // packed W boxes landed (TMA bytes)
+  // A stage is its activation tile and its bf16 W tile: one barrier says both
+  // are ready (the TMA bytes + one arrival per dequantising warp), one says
+  // the MMAs finished reading both.  The MMA issuer waits and commits once per
+  // K step: its own instruction stream is what keeps the tensor pipe fed.
+  uint64_t *full = bars;
+  uint64_t *empty = full + S;
+  uint64_t *p_full = empty + S;         // packed W boxes landed (TMA bytes)
   uint64_t *p_empty = p_full + SP;      // every dequant warp finished reading them
   uint64_t *done = p_empty + SP;        // all MMAs finished
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
@@ -264,13 +266,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   constexpr uint32_t TMEM_COLS = SUBS == 2 ? 512 : 256;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < SA; ++s) {
-      mbar_init(&a_full[s], 1);
-      mbar_init(&a_empty[s], 1);
-    }
-    for (int s = 0; s < SB; ++s) {
-      mbar_init(&b_full[s], DQ_THREADS);
-      mbar_init(&b_empty[s], 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1 + DQ_WARPS);
+      mbar_init(&empty[s], 1);
     }
     for (int s = 0; s < SP; ++s) {
       mbar_init(&p_full[s], 1);
@@ -300,23 +298,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0) {
       grid_launch_dependents();
       grid_dependency_wait();  // the activations may be the previous kernel's output
-      int issued = 0;
       for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % SA;
-        if (kt >= SA && !mbar_wait(&a_empty[s], ((kt / SA) - 1) & 1, p.err)) {
+        const int s = kt % S;
+        if (kt >= S && !mbar_wait(&empty[s], ((kt / S) - 1) & 1, p.err)) {
           *(volatile int *)abort_flag = 1;
           break;
         }
         if (*(volatile int *)abort_flag) break;
         uint8_t *st = a0 + (size_t)s * p.a_bytes;
-        mbar_arrive_expect_tx(&a_full[s], p.a_bytes);
+        mbar_arrive_expect_tx(&full[s], p.a_bytes);
         for (int sub = 0; sub < SUBS; ++sub)
-          tma_load_2d(st + sub * 16384, &map_a, kt * KSTEP, m0 + sub * 128, &a_full[s]);
-        issued = kt + 1;
+          tma_load_2d(st + sub * 16384, &map_a, kt * KSTEP, m0 + sub * 128, &full[s]);
       }
-      // every copy this thread issued has landed before the CTA may exit
-      for (int kt = (issued > SA ? issued - SA : 0); kt < issued; ++kt)
-        mbar_wait(&a_full[kt % SA], (kt / SA) & 1, nullptr);
+      // (every activation copy has landed before the MMAs that read it, and
+      // the epilogue waits for those)
     }
   } else if (warp == 2) {
     // ---------------- packed W boxes, prefetched SP steps ahead ----------------
@@ -344,23 +339,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0) {
       const uint32_t idesc = instr_desc_bf16(128, p.bn);
       for (int kt = 0; kt < KT; ++kt) {
-        const int sa = kt % SA, sb = kt % SB;
-        if (!mbar_wait(&a_full[sa], (kt / SA) & 1, p.err) ||
-            !mbar_wait(&b_full[sb], (kt / SB) & 1, p.err)) {
+        const int s = kt % S;
+        if (!mbar_wait(&full[s], (kt / S) & 1, p.err)) {
           *(volatile int *)abort_flag = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(a0 + (size_t)sa * p.a_bytes);
-        const uint32_t b_addr = smem_u32(b0 + (size_t)sb * p.b_bytes);
+        const uint32_t a_addr = smem_u32(a0 + (size_t)s * p.a_bytes);
+        const uint32_t b_addr = smem_u32(b0 + (size_t)s * p.b_bytes);
 #pragma unroll
         for (int sub = 0; sub < SUBS; ++sub)
 #pragma unroll
           for (int kk = 0; kk < KSTEP / 16; ++kk)
             mma_bf16(tmem_base + sub * 256, smem_desc_sw128(a_addr + sub * 16384 + kk * 32),
                      smem_desc_sw128(b_addr + kk * 32), idesc, (kt | kk) != 0);
-        mma_commit(&a_empty[sa]);
-        mma_commit(&b_empty[sb]);
+        mma_commit(&empty[s]);
       }
       mma_commit(done);  // arrives once every MMA issued above has completed
     }
@@ -380,11 +373,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int items = p.bn * 2;  // (weight row, run) pairs per stage
     bool ok = true;
     for (int kt = 0; kt < KT && ok; ++kt) {
-      const int sb = kt % SB, sp = kt % SP;
+      const int sb = kt % S, sp = kt % SP;
       if (*(volatile int *)abort_flag) break;
-      // the B slot is free once the MMA of round (kt / SB) - 1 released it, and
+      // the stage is free once the MMAs of round (kt / S) - 1 released it, and
       // the packed boxes of this step have landed
-      ok = (kt < SB || mbar_wait(&b_empty[sb], ((kt / SB) - 1) & 1, p.err)) &&
+      ok = (kt < S || mbar_wait(&empty[sb], ((kt / S) - 1) & 1, p.err)) &&
            mbar_wait(&p_full[sp], (kt / SP) & 1, p.err);
       if (!ok) {
         *(volatile int *)abort_flag = 1;
@@ -404,10 +397,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           *reinterpret_cast<uint4 *>(dst_row + ((chunk ^ (row & 7)) << 4)) = out[c];
         }
       }
+      // each thread's writes reach the async proxy; the warp syncs and one
+      // lane arrives for it
       fence_proxy_async_smem();
-      mbar_arrive(&b_full[sb]);
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_empty[sp]);
+      if (lane == 0) {
+        mbar_arrive(&full[sb]);
+        mbar_arrive(&p_empty[sp]);
+      }
     }
     // epilogue: TMEM lanes of this warp's quarter -> y rows; the two warps of
     // a quarter take alternate 8-column chunks
@@ -571,6 +568,7 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
   if (!gemm_supported(fmt, m, n, k) || (reinterpret_cast<uintptr_t>(w) & 15) ||
       (reinterpret_cast<uintptr_t>(xb) & 15))
     return cudaErrorInvalidValue;
+  // more than 128 activation rows: CTA pairs sharing each MMA (cta_group::2)
   const Layout L(fmt, n, k);
   const TileChoice t = choose_tiles(m, n, sms);
   GemmParams p;
@@ -585,15 +583,16 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
   p.ws_bytes = (uint32_t)ceil_div((uint64_t)t.bn * 16, 1024) * 1024;
   p.pstage_bytes = p.wq_bytes + p.ws_bytes;
   p.ptx_bytes = (uint32_t)t.bn * (uint32_t)p.qbytes + (uint32_t)t.bn * 16u;
-  // ring depths sized to their latency: activation tiles come from L2 (4 deep),
-  // the bf16 W tile is produced on chip (2 deep), packed W streams from HBM (3+)
+  // operand stages (activation tile + bf16 W tile, 3 deep) and packed-W stages
+  // (streamed from HBM, 3+ deep)
   const uint32_t budget = 225 * 1024 - 1024 /*align slack*/ - 512 /*barriers*/;
-  int sa = 4, sb = 2, sp = 3;
-  while (sa * p.a_bytes + sb * p.b_bytes + sp * p.pstage_bytes > budget && sa > 2) --sa;
-  if (sa * p.a_bytes + sb * p.b_bytes + sp * p.pstage_bytes > budget) return cudaErrorInvalidValue;
-  while (sp < 8 && sa * p.a_bytes + sb * p.b_bytes + (sp + 1) * p.pstage_bytes <= budget) ++sp;
+  const uint32_t ab = p.a_bytes + p.b_bytes;
+  int sa = 3, sp = 3;
+  while (sa * ab + sp * p.pstage_bytes > budget && sa > 2) --sa;
+  if (sa * ab + sp * p.pstage_bytes > budget) return cudaErrorInvalidValue;
+  while (sp < 8 && sa * ab + (sp + 1) * p.pstage_bytes <= budget) ++sp;
   p.astages = sa;
-  p.bstages = sb;
+  p.bstages = sa;
   p.pstages = sp;
   p.addend_mode = addend_mode;
   p.addend = addend;
@@ -610,8 +609,7 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
                    (uint32_t)t.bn, CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
 
-  const size_t smem = (size_t)sa * p.a_bytes + (size_t)sb * p.b_bytes +
-                      (size_t)sp * p.pstage_bytes + 1024 + 512;
+  const size_t smem = (size_t)sa * ab + (size_t)sp * p.pstage_bytes + 1024 + 512;
   dim3 grid((unsigned)ceil_div(n, (uint64_t)t.bn), (unsigned)ceil_div(m, 128ull * t.subs));
   cudaError_t e = cudaSuccess;
 #define MGB_GEMM_LAUNCH(F, SUBS)                                                               \
