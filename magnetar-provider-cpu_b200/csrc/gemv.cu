@@ -200,7 +200,7 @@ __device__ __forceinline__ void run_partials(const uint4 &qa, const uint4 &qb, c
     const float d = f16_bits_to_f32(dh);
     const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-    for (int m = 0; m < MR; ++m) part[m] = (d * x[m].dx) * (float)dot_s8(q, x[m]);
+    for (int m = 0; m < MR; ++m) part[m] = (d * x[m].dx) * (float)dot_s8(q, x[m]) + 0.f * x[m].sum;
   } else {  // IQ4_NL
     const float d = f16_bits_to_f32(dh);
     uint32_t q[8];
@@ -208,7 +208,7 @@ __device__ __forceinline__ void run_partials(const uint4 &qa, const uint4 &qb, c
 #pragma unroll
     for (int wd = 0; wd < 4; ++wd) iq4_lookup(words[wd], lut, q[2 * wd], q[2 * wd + 1]);
 #pragma unroll
-    for (int m = 0; m < MR; ++m) part[m] = (d * x[m].dx) * (float)dot_s8(q, x[m]);
+    for (int m = 0; m < MR; ++m) part[m] = (d * x[m].dx) * (float)dot_s8(q, x[m]) + 0.f * x[m].sum;
   }
 }
 
@@ -227,34 +227,6 @@ __device__ __forceinline__ float2 decode_run_scale(const uint8_t *srow, int uu) 
   } else {
     const float d = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(srow + uu * 2));
     return make_float2(d, FMT == Q4_0 ? 8.f * d : 0.f);
-  }
-}
-
-// Partial dot products of one run of one weight row (its quant bytes at qrow,
-// its decoded factors sm) with MR activation rows.
-template <int FMT, int MR>
-__device__ __forceinline__ void run_partials_decoded(const uint8_t *qrow, int uu, float2 sm,
-                                                     const XRun (&x)[MR], const uint32_t lut[4],
-                                                     float (&part)[MR]) {
-  if (FMT == Q8_0) {
-    const uint4 qa = *reinterpret_cast<const uint4 *>(qrow + uu * 32);
-    const uint4 qb = *reinterpret_cast<const uint4 *>(qrow + uu * 32 + 16);
-    const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-#pragma unroll
-    for (int m = 0; m < MR; ++m) part[m] = (sm.x * x[m].dx) * (float)dot_s8(q, x[m]);
-  } else if (FMT == IQ4_NL) {
-    const uint4 qa = *reinterpret_cast<const uint4 *>(qrow + uu * 16);
-    uint32_t q[8];
-    const uint32_t words[4] = {qa.x, qa.y, qa.z, qa.w};
-#pragma unroll
-    for (int wd = 0; wd < 4; ++wd) iq4_lookup(words[wd], lut, q[2 * wd], q[2 * wd + 1]);
-#pragma unroll
-    for (int m = 0; m < MR; ++m) part[m] = (sm.x * x[m].dx) * (float)dot_s8(q, x[m]);
-  } else {  // Q4_K, Q4_0: nibble pairs
-    const uint4 qa = *reinterpret_cast<const uint4 *>(qrow + uu * 16);
-#pragma unroll
-    for (int m = 0; m < MR; ++m)
-      part[m] = (sm.x * x[m].dx) * (float)dot_nib(qa, x[m]) - sm.y * x[m].sum;
   }
 }
 
@@ -335,7 +307,7 @@ __device__ __forceinline__ void rows_partials(const uint8_t *q, size_t q_stride,
       if (FMT == Q4_K || FMT == Q4_0)
         part[i * MR + m] = (sm[i].x * x[m].dx) * dot - sm[i].y * x[m].sum;
       else
-        part[i * MR + m] = (sm[i].x * x[m].dx) * dot;
+        part[i * MR + m] = (sm[i].x * x[m].dx) * dot + 0.f * x[m].sum;  // NaN / Inf in x reach y
     }
 }
 
@@ -356,108 +328,6 @@ __device__ __forceinline__ void load_x(const float *__restrict__ x, int k, int u
       v[4 * i + 3] = f.w;
     }
     pack_run(v, pair, xr[m]);
-  }
-}
-
-// ---- activation packing, once per CTA into shared memory ------------------------------
-// Layout for m rows of runs = k/32: hi words [m][8][runs], lo words [m][8][runs],
-// dx [m][runs], sum [m][runs] (72 bytes per run; consecutive runs are
-// consecutive words, so a team's reads are conflict-free).
-
-__host__ __device__ inline uint64_t xpack_bytes(uint64_t m, uint64_t k) {
-  return m * (k / RUN) * 72;
-}
-
-// The consumer threads (ct of nthreads, a multiple of 32) pack the m rows of x:
-// four lanes per run, each packing 8 of its values into 2 high and 2 low words
-// (words 2p, 2p+1 hold values 8p..8p+7 in either order); the run's max |x|
-// and sum come from a 4-lane shuffle.  Each pass covers two tasks per thread
-// and issues the loads of both before packing either, so a pass costs one
-// memory round trip (one pass for k <= 4096 at one activation row).  x is
-// global memory or the kernel's shared-memory copy of it.
-template <bool PAIR>
-__device__ __forceinline__ void pack_x_to_smem(const float *__restrict__ x, int m, int k, int ct,
-                                               int nthreads, uint32_t *xs) {
-  const int runs = k / RUN;
-  const int total = m * runs * 4;
-  uint32_t *hi = xs, *lo = xs + (size_t)m * 8 * runs;
-  float *dx = reinterpret_cast<float *>(xs + (size_t)m * 16 * runs), *sum = dx + (size_t)m * runs;
-  for (int base = 0; base < total; base += 2 * nthreads) {
-    float v[2][8];
-    bool live[2];
-    int row[2], u[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int t = base + h * nthreads + ct;
-      const int ru = t >> 2;
-      live[h] = t < total;  // whole 4-lane groups are live or not
-      row[h] = live[h] ? ru / runs : 0;
-      u[h] = live[h] ? ru % runs : 0;
-      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
-      if (live[h]) {
-        const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)row[h] * k +
-                                                             (size_t)u[h] * 32 + 8 * (t & 3));
-        a = src[0];
-        b = src[1];
-      }
-      v[h][0] = a.x; v[h][1] = a.y; v[h][2] = a.z; v[h][3] = a.w;
-      v[h][4] = b.x; v[h][5] = b.y; v[h][6] = b.z; v[h][7] = b.w;
-    }
-    const int p = ct & 3;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      float amax = 0.f;
-      float s = ((v[h][0] + v[h][1]) + (v[h][2] + v[h][3])) + ((v[h][4] + v[h][5]) + (v[h][6] + v[h][7]));
-#pragma unroll
-      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[h][i]));
-#pragma unroll
-      for (int off = 1; off < 4; off <<= 1) {
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-        s += __shfl_xor_sync(0xffffffffu, s, off);
-      }
-      if (!live[h]) continue;
-      const float inv = amax > 0.f ? 32767.f / amax : 0.f;
-      uint32_t hw[2] = {0, 0}, lw[2] = {0, 0};
-#pragma unroll
-      for (int wd = 0; wd < 2; ++wd)
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          const int e = PAIR ? 2 * b + wd : 4 * wd + b;
-          int q = __float2int_rn(v[h][e] * inv);
-          q = max(-32767, min(32767, q));
-          hw[wd] |= (uint32_t)((q >> 8) & 0xff) << (8 * b);
-          lw[wd] |= (uint32_t)(q & 0xff) << (8 * b);
-        }
-#pragma unroll
-      for (int wd = 0; wd < 2; ++wd) {
-        hi[((size_t)row[h] * 8 + 2 * p + wd) * runs + u[h]] = hw[wd];
-        lo[((size_t)row[h] * 8 + 2 * p + wd) * runs + u[h]] = lw[wd];
-      }
-      if (p == 0) {
-        dx[(size_t)row[h] * runs + u[h]] = amax / 32767.f;
-        sum[(size_t)row[h] * runs + u[h]] = s;
-      }
-    }
-  }
-}
-
-template <int MR>
-__device__ __forceinline__ void load_packed_x(const uint32_t *xs, int k, int u, bool active,
-                                              XRun (&xr)[MR]) {
-  const int runs = k / RUN;
-  const uint32_t *hi = xs, *lo = xs + (size_t)MR * 8 * runs;
-  const float *dx = reinterpret_cast<const float *>(xs + (size_t)MR * 16 * runs);
-  const float *sum = dx + (size_t)MR * runs;
-  const int uu = active ? u : 0;
-#pragma unroll
-  for (int m = 0; m < MR; ++m) {
-#pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      xr[m].hi[w] = active ? hi[((size_t)m * 8 + w) * runs + uu] : 0u;
-      xr[m].lo[w] = active ? lo[((size_t)m * 8 + w) * runs + uu] : 0u;
-    }
-    xr[m].dx = active ? dx[(size_t)m * runs + uu] : 0.f;
-    xr[m].sum = active ? sum[(size_t)m * runs + uu] : 0.f;
   }
 }
 

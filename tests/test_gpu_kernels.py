@@ -200,3 +200,20 @@ def test_input_major_parity(torch_cuda, oracle, fmt):
         torch.cuda.synchronize()
         ref = oracle.packed_axpy(fmt, w, rows, cols, x)
         assert np.array_equal(yd.cpu().numpy(), ref)  # same order, same roundings
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("m", [1, 2, 5])
+def test_nan_activation_reaches_its_row_only(torch_cuda, oracle, fmt, m):
+    """A NaN activation makes its whole output row NaN and leaves the other rows
+    finite, as the reference's f32 matmul does (x * w is NaN for every w)."""
+    n, k = 96, 512
+    w = synthetic.packed_weights(fmt, n, k, seed=21)
+    wdev = _device_layout(torch_cuda, fmt, w, n, k)
+    x = synthetic.activations(m, k, seed=22)
+    x[0, 37] = np.nan
+    y = _qmatmul(torch_cuda, fmt, wdev, n, k, x)
+    ref = oracle.packed_matmul(fmt, w, n, k, x)
+    assert np.isnan(ref[0]).all()
+    assert np.isnan(y[0]).all(), f"{np.isnan(y[0]).sum()} of {n} NaN in row 0"
+    assert np.isfinite(y[1:]).all()
