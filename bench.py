@@ -22,7 +22,12 @@ over one batch.  Metric: TFLOP/s (2*M*N*K per step), whole job.
   persistent pool), restated in C (oracle/cpu_baseline.c), on a sample of
   the same workload, on every host core.
 N > 1 (torchrun): tensor parallel along N (each rank holds 14336/N weight
-rows), outputs all-gathered over NCCL; strong scaling, max over ranks.
+rows); the kernels store every output column into every rank's y over NVLink
+(CUDA IPC mappings) and a stream-ordered wait completes the step
+(`tp.FusedShardedPackedMatmul`); strong scaling, max over ranks.  The NCCL
+all-gather variant (`tp.gather_columns`) is timed beside it as
+`tp_baseline_nccl`.  e2e at N > 1: pinned x -> device, the fused call, the
+full y -> pinned host, on every rank.
 """
 
 from __future__ import annotations
@@ -231,12 +236,24 @@ def run_b200(args) -> None:
     ws_bytes = mgb.qmatmul_workspace_bytes(fmt, M, n_loc, K)
     WS = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
 
+    op = None
+    if world > 1:
+        op = tp.FusedShardedPackedMatmul(fmt, w_loc, N, K, world, rank, max_m=M, device=dev)
+
     def step(i: int) -> None:
+        s = i % R
+        if op is not None:  # fused all-gather: [M, N] on every rank
+            op.weight = W[s]
+            op(X[s])
+            return
+        mgb.qmatmul(fmt, W[s].data_ptr(), n_loc, K, X[s].data_ptr(), M, Y[s].data_ptr(),
+                    workspace_ptr=WS.data_ptr(), workspace_bytes=ws_bytes, stream=sp)
+
+    def step_nccl(i: int) -> None:
         s = i % R
         mgb.qmatmul(fmt, W[s].data_ptr(), n_loc, K, X[s].data_ptr(), M, Y[s].data_ptr(),
                     workspace_ptr=WS.data_ptr(), workspace_bytes=ws_bytes, stream=sp)
-        if world > 1:
-            tp.gather_columns(Y[s])  # [M, N] on every rank
+        tp.gather_columns(Y[s])  # [M, N] on every rank
 
     def timed(fn, steps: int, warmup: int) -> float:
         for i in range(warmup):
@@ -264,6 +281,12 @@ def run_b200(args) -> None:
     ms_step = total_ms / args.steps
     flops = 2.0 * M * N * K
     value = flops / (ms_step * 1e-3) / 1e12
+    nccl = None
+    if world > 1:
+        nccl_ms = timed(step_nccl, args.steps, args.warmup) / args.steps
+        nccl = {"ms_per_step": nccl_ms, "value": flops / (nccl_ms * 1e-3) / 1e12,
+                "unit": "TFLOP/s", "step": "mgb_qmatmul into [M, N/G] + NCCL "
+                                           "all_gather_into_tensor + interleave"}
 
     # roofline: the GEMM kernel alone on bf16 activations
     XB = [x.to(torch.bfloat16) for x in X]
@@ -284,19 +307,31 @@ def run_b200(args) -> None:
                 "traffic": traffic, "ms_per_launch": gemm_ms,
                 "flops_per_launch": 2.0 * M * n_loc * K}
 
-    # e2e through the Provider's C ABI with pinned host buffers
-    prov = mgb.B200Provider(device=local)
-    assert prov.write_packed_weight_tensor("w", fmt, n_loc, K, True, w_loc) == "Stored"
+    # e2e with pinned host buffers: through the Provider's C ABI on one GPU,
+    # through the fused tensor-parallel call on several
     xh = torch.from_numpy(x_host).pin_memory()
-    yh = torch.empty((M, n_loc), dtype=torch.float32).pin_memory()
+    prov = None
+    if op is None:
+        prov = mgb.B200Provider(device=local)
+        assert prov.write_packed_weight_tensor("w", fmt, n_loc, K, True, w_loc) == "Stored"
+        yh = torch.empty((M, n_loc), dtype=torch.float32).pin_memory()
 
-    def e2e_step(_i: int) -> None:
-        prov.write_tensor_ptr("x", (M, K), xh.data_ptr())
-        h = prov.submit_kernel("matmul", ["x", "w"], "y")
-        r = prov.complete_kernel(h)
-        if not r.ok:
-            raise RuntimeError(r.reason)
-        prov.read_tensor_into("y", yh.data_ptr(), M * n_loc)
+        def e2e_step(_i: int) -> None:
+            prov.write_tensor_ptr("x", (M, K), xh.data_ptr())
+            h = prov.submit_kernel("matmul", ["x", "w"], "y")
+            r = prov.complete_kernel(h)
+            if not r.ok:
+                raise RuntimeError(r.reason)
+            prov.read_tensor_into("y", yh.data_ptr(), M * n_loc)
+    else:
+        op.weight = W[0]
+        yh = torch.empty((M, N), dtype=torch.float32).pin_memory()
+        xd = torch.empty((M, K), dtype=torch.float32, device=dev)
+
+        def e2e_step(_i: int) -> None:
+            xd.copy_(xh, non_blocking=True)
+            yh.copy_(op(xd), non_blocking=True)
+            stream.synchronize()
 
     e2e_steps = max(3, min(args.steps, 50))
     for i in range(max(3, args.warmup)):
@@ -311,12 +346,18 @@ def run_b200(args) -> None:
         t = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    prov.close()
+    if prov is not None:
+        prov.close()
+        path = ("mgb_write_tensor (pinned) -> mgb_submit_kernel(matmul) -> mgb_complete_kernel -> "
+                "mgb_read_tensor (pinned); wall clock")
+        d2h = M * N * 4
+    else:
+        path = ("pinned x -> device, tp.FusedShardedPackedMatmul (mgb_qmatmul_tp + mgb_tp_wait), "
+                "full y [M, N] -> pinned host on every rank; wall clock")
+        d2h = M * N * 4 * world
     e2e = {"value": flops / e2e_s / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": M * K * 4 * world,
-           "d2h_bytes_per_step": M * N * 4, "ms_per_step": e2e_s * 1e3, "steps": e2e_steps,
-           "path": "mgb_write_tensor (pinned) -> mgb_submit_kernel(matmul) -> "
-                   "mgb_complete_kernel -> mgb_read_tensor (pinned); wall clock",
-           "timing": "wall clock per rank, max over ranks"}
+           "d2h_bytes_per_step": d2h, "ms_per_step": e2e_s * 1e3, "steps": e2e_steps,
+           "path": path, "timing": "wall clock per rank, max over ranks"}
 
     # second half of the metric: config 0 decode GEMV weight GB/s (rank 0's GPU)
     gemv = None
@@ -387,10 +428,15 @@ def run_b200(args) -> None:
                            "l2": f"{R} rotating input sets of {set_bytes / 1e6:.0f} MB "
                                  f"({R * set_bytes / 1e6:.0f} MB > 3x 126 MB L2)",
                            "step": "mgb_qmatmul: f32->bf16 activation pass + tcgen05 GEMM"
-                                   + (" + NCCL all-gather of output columns" if world > 1 else "")},
+                                   + (" storing every column into every rank's y over NVLink "
+                                      "+ stream-ordered wait for all ranks (mgb_qmatmul_tp, "
+                                      "mgb_tp_wait)" if world > 1 else "")},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-                "gpu_launches": 2 * args.steps, "clocks": clocks, "gemv": gemv}
+                "gpu_launches": (3 if world > 1 else 2) * args.steps, "clocks": clocks,
+                "gemv": gemv, "tp_baseline_nccl": nccl}
         print(json.dumps(line), flush=True)
+    if op is not None:
+        op.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

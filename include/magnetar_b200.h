@@ -322,6 +322,66 @@ mgb_status mgb_take_device_error(int32_t device, int32_t *code);
 mgb_status mgb_quantize_rows(const float *x, uint64_t len, int8_t *values, float *scales,
                              int32_t *sums, void *stream);
 
+/* ---- tensor parallelism over output columns (one process per GPU) ------------------ */
+
+/* Rank g of G holds stored rows [g n/G, (g+1) n/G) of a packed weight, the
+ * unit the reference's CPU pool splits a packed matmul on (`packed_matmul`,
+ * src/native/mod.rs:135-150).  `mgb_qmatmul_tp` computes this rank's columns
+ * and writes each one straight into every rank's full y over NVLink (the
+ * all-gather fused into the kernel's output stores; peers' buffers are mapped
+ * with CUDA IPC).  No counterpart in the reference, which runs on one host. */
+#define MGB_MAX_TP 8
+/* Bytes of a rank's synchronisation words: done[MGB_MAX_TP] (u32 at offset 0,
+ * word r written by rank r) and the call's CTA counter (u32 at offset 128). */
+#define MGB_TP_SYNC_BYTES 256u
+#define MGB_TP_COUNTER_OFFSET 128u
+
+/* Where one rank's tensor-parallel call writes.  All pointers are valid on the
+ * calling GPU (this rank's own buffers or IPC mappings of the peers').  Output
+ * element (row, col) of the call goes to y[r] + row * ldy + col0 + col for
+ * every r < world.  When every CTA has stored, the call stores `epoch` with
+ * release semantics (system scope) into done[r][rank] for every r;
+ * `cta_counter` is this rank's counter word, zero before its first call (each
+ * call leaves it zero). */
+typedef struct mgb_tp_out {
+    float *y[MGB_MAX_TP];
+    uint32_t *done[MGB_MAX_TP];
+    uint32_t *cta_counter;
+    uint64_t ldy;
+    uint64_t col0;
+    uint32_t epoch;
+    int32_t world;
+    int32_t rank;
+} mgb_tp_out;
+
+/* cudaMalloc'd, zero-filled device memory on the current device, whole
+ * allocations so a CUDA IPC handle maps exactly them. */
+mgb_status mgb_device_alloc(uint64_t bytes, void **out);
+mgb_status mgb_device_free(void *ptr);
+/* The 64-byte CUDA IPC handle of an mgb_device_alloc allocation, and its
+ * mapping in another process (peer access enabled on demand). */
+#define MGB_IPC_HANDLE_BYTES 64
+mgb_status mgb_ipc_handle(void *ptr, uint8_t *handle_out);
+mgb_status mgb_ipc_open(const uint8_t *handle, void **out);
+mgb_status mgb_ipc_close(void *mapped);
+/* This rank's shard product x[m, k] * W_shard^T (n = the shard's stored rows)
+ * written into every rank's y as `out` says, then the completion published.
+ * Same kernels, workspace and addend rules as mgb_qmatmul (the addend is this
+ * rank's [n] or [m, n] slice).  The caller must not overwrite a peer's y while
+ * the peer still reads it: alternate between two y buffers per rank (a call
+ * starts writing only after the previous work on its stream, which includes
+ * the wait for the previous call's peers, has finished). */
+mgb_status mgb_qmatmul_tp(int32_t format, const void *w, uint64_t n, uint64_t k, const float *x,
+                          uint64_t m, const mgb_tp_out *out, const float *addend,
+                          uint64_t addend_len, void *workspace, uint64_t workspace_bytes,
+                          void *stream);
+/* Stream-ordered wait until done[r] has reached `epoch` for every r < world
+ * (`done` = this rank's synchronisation words).  Work queued after it on
+ * `stream` sees every rank's columns.  A wait longer than timeout_ms (0: 2000)
+ * gives up and records device error 1 (see mgb_take_device_error). */
+mgb_status mgb_tp_wait(const uint32_t *done, int32_t world, uint32_t epoch, uint32_t timeout_ms,
+                       void *stream);
+
 #ifdef __cplusplus
 }
 #endif

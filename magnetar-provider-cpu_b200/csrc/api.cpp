@@ -76,8 +76,9 @@ int *device_error_flag(int device) {
 // Picks the kernel for m activation rows: GEMV (f32, m <= 2 per launch) or the
 // tensor-core GEMM.  kernel_pref: MGB_KERNEL_AUTO / GEMV / GEMM.
 mgb_status run_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, const float *x,
-                       uint64_t m, float *y, const float *addend, int addend_mode, void *workspace,
-                       uint64_t workspace_bytes, int *err, int kernel_pref, cudaStream_t stream) {
+                       uint64_t m, const OutSpec &out, const float *addend, int addend_mode,
+                       void *workspace, uint64_t workspace_bytes, int *err, int kernel_pref,
+                       cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   const int sms = device_sms(dev);
@@ -92,17 +93,18 @@ mgb_status run_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, co
                 (unsigned long long)gemm_workspace_bytes(format, m, n, k));
   cudaError_t e;
   if (use_gemm) {
-    e = launch_gemm(format, w, n, k, x, m, y, addend, addend_mode, workspace, workspace_bytes, err,
-                    sms, stream);
+    e = launch_gemm(format, w, n, k, x, m, out, addend, addend_mode, workspace, workspace_bytes,
+                    err, sms, stream);
     if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
     return MGB_OK;
   }
   if (k / 32 > 1024) return fail(MGB_UNSUPPORTED, "GEMV supports k <= 32768 (got %llu)", (unsigned long long)k);
+  // row pairs; a tensor-parallel call completes with its last launch
   for (uint64_t r = 0; r < m; r += 2) {
     const uint64_t rows = m - r < 2 ? m - r : 2;
     const float *add = addend_mode == 2 ? addend + r * n : addend;
-    e = launch_gemv(format, w, n, k, x + r * k, rows, y + r * n, add, addend_mode, err, sms,
-                    stream);
+    const OutSpec sub = r + rows < m ? without_completion(rows_from(out, r)) : rows_from(out, r);
+    e = launch_gemv(format, w, n, k, x + r * k, rows, sub, add, addend_mode, err, sms, stream);
     if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
   }
   return MGB_OK;
@@ -197,8 +199,9 @@ mgb_status mgb_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, co
   }
   int dev = 0;
   cudaGetDevice(&dev);
-  return run_qmatmul(format, w, n, k, x, m, y, addend, mode, workspace, workspace_bytes,
-                     device_error_flag(dev), MGB_KERNEL_AUTO, static_cast<cudaStream_t>(stream));
+  return run_qmatmul(format, w, n, k, x, m, plain_out(y, n), addend, mode, workspace,
+                     workspace_bytes, device_error_flag(dev), MGB_KERNEL_AUTO,
+                     static_cast<cudaStream_t>(stream));
 }
 
 mgb_status mgb_qmatmul_bf16(int32_t format, const void *w, uint64_t n, uint64_t k, const void *xb,
@@ -222,8 +225,9 @@ mgb_status mgb_qmatmul_bf16(int32_t format, const void *w, uint64_t n, uint64_t 
   }
   int dev = 0;
   cudaGetDevice(&dev);
-  cudaError_t e = launch_gemm_bf16(format, w, n, k, xb, m, y, addend, mode, device_error_flag(dev),
-                                   device_sms(dev), static_cast<cudaStream_t>(stream));
+  cudaError_t e = launch_gemm_bf16(format, w, n, k, xb, m, plain_out(y, n), addend, mode,
+                                   device_error_flag(dev), device_sms(dev),
+                                   static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? MGB_OK : cuda_fail(e, "GEMM launch");
 }
 

@@ -9,6 +9,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "outspec.h"
+
 namespace mgb {
 
 // Format codes: the reference's `FORMATS` order (src/native/quant.rs:71-87).
@@ -172,5 +174,35 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 }
 
 __host__ __device__ inline uint64_t ceil_div(uint64_t a, uint64_t b) { return (a + b - 1) / b; }
+
+// ---- output fan-out and completion of a tensor-parallel call ----------------------
+
+// Output element (m, col) of this call, written to every rank's y.
+__device__ __forceinline__ void out_store(const OutSpec &o, int m, uint64_t col, float v) {
+  const uint64_t off = (uint64_t)m * o.ldy + o.col0 + col;
+  for (int r = 0; r < o.world; ++r) o.y_ranks[r][off] = v;
+}
+
+// Every thread that stored output calls this before the CTA barrier that
+// precedes out_complete: its stores (to peer GPUs too) become visible
+// system-wide.  A plain call (one rank) needs no fence.
+__device__ __forceinline__ void out_fence(const OutSpec &o) {
+  if (o.world > 1 || o.cta_counter) __threadfence_system();
+}
+
+// One thread per CTA, after a barrier that follows every out_fence of the CTA
+// and after this thread's griddepcontrol.wait (the previous call on the stream
+// has finished with the counter).  The CTA that counts last publishes the call.
+__device__ __forceinline__ void out_complete(const OutSpec &o, uint32_t total_ctas) {
+  if (!o.cta_counter) return;
+  __threadfence_system();
+  const uint32_t before = atomicAdd(o.cta_counter, 1u);
+  if (before != total_ctas - 1) return;
+  *o.cta_counter = 0;  // every CTA of this call has counted: ready for the next call
+  __threadfence_system();
+  for (int r = 0; r < o.world; ++r)
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(o.done_ranks[r] + o.rank), "r"(o.epoch)
+                 : "memory");
+}
 
 }  // namespace mgb

@@ -61,7 +61,8 @@ struct GemmParams {
   uint32_t ptx_bytes;   // bytes the two packed boxes of one step deliver
   int addend_mode;
   const float *addend;
-  float *y;
+  OutSpec out;          // y of this rank, or of every rank (fused all-gather)
+  int vec_out;          // every output row start is 16-byte aligned: float4 stores
   int *err;
 };
 
@@ -421,10 +422,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tmem_ld8(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * 256 + c), v);
           if (row < p.m) {
             const int col = n0 + c;
-            float *yr = p.y + (size_t)row * p.n;
-            if (col + 8 <= p.n && p.addend_mode == 0 && (p.n & 3) == 0) {
-              reinterpret_cast<float4 *>(yr + col)[0] = make_float4(v[0], v[1], v[2], v[3]);
-              reinterpret_cast<float4 *>(yr + col)[1] = make_float4(v[4], v[5], v[6], v[7]);
+            // this call's column col lands at col0 + col of every output rank's y
+            if (col + 8 <= p.n && p.addend_mode == 0 && p.vec_out) {
+              for (int r = 0; r < p.out.world; ++r) {
+                float4 *yr = reinterpret_cast<float4 *>(p.out.y_ranks[r] + (size_t)row * p.out.ldy +
+                                                        p.out.col0 + col);
+                yr[0] = make_float4(v[0], v[1], v[2], v[3]);
+                yr[1] = make_float4(v[4], v[5], v[6], v[7]);
+              }
             } else {
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
@@ -432,7 +437,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                   float o = v[e];
                   if (p.addend_mode == 1) o = o + p.addend[col + e];
                   else if (p.addend_mode == 2) o = o + p.addend[(size_t)row * p.n + col + e];
-                  yr[col + e] = o;
+                  for (int r = 0; r < p.out.world; ++r)
+                    p.out.y_ranks[r][(size_t)row * p.out.ldy + p.out.col0 + col + e] = o;
                 }
               }
             }
@@ -441,8 +447,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
   }
+  out_fence(p.out);
   tc_fence_before();
   __syncthreads();
+  // (thread 0 is the activation producer: it has waited for the previous grid)
+  if (threadIdx.x == 0) out_complete(p.out, gridDim.x * gridDim.y);
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
@@ -542,7 +551,7 @@ bool gemm_supported(int fmt, uint64_t m, uint64_t n, uint64_t k) {
 }
 
 cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const float *x, uint64_t m,
-                        float *y, const float *addend, int addend_mode, void *workspace,
+                        const OutSpec &out, const float *addend, int addend_mode, void *workspace,
                         uint64_t workspace_bytes, int *err, int sms, cudaStream_t stream) {
   if (!gemm_supported(fmt, m, n, k) || workspace_bytes < gemm_workspace_bytes(fmt, m, n, k) ||
       (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 15))
@@ -559,11 +568,11 @@ cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const fl
   e = launch_dependent(f32_to_bf16_kernel, dim3((unsigned)blocks), dim3(256), 0,
                                    stream, x, xb, m * k);
   if (e != cudaSuccess) return e;
-  return launch_gemm_bf16(fmt, w, n, k, xb, m, y, addend, addend_mode, err, sms, stream);
+  return launch_gemm_bf16(fmt, w, n, k, xb, m, out, addend, addend_mode, err, sms, stream);
 }
 
 cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, const void *xb,
-                             uint64_t m, float *y, const float *addend, int addend_mode, int *err,
+                             uint64_t m, const OutSpec &out, const float *addend, int addend_mode, int *err,
                              int sms, cudaStream_t stream) {
   if (!gemm_supported(fmt, m, n, k) || (reinterpret_cast<uintptr_t>(w) & 15) ||
       (reinterpret_cast<uintptr_t>(xb) & 15))
@@ -596,7 +605,10 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
   p.pstages = sp;
   p.addend_mode = addend_mode;
   p.addend = addend;
-  p.y = y;
+  p.out = out;
+  p.vec_out = ((out.ldy | out.col0) & 3) == 0;
+  for (int r = 0; r < out.world; ++r)
+    if (reinterpret_cast<uintptr_t>(out.y_ranks[r]) & 15) p.vec_out = 0;
   p.err = err;
 
   CUtensorMap map_a, map_wq, map_ws;

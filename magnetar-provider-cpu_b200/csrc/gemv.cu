@@ -374,7 +374,7 @@ struct GemvStaged {
   uint32_t dec_stage_bytes;  // decoded run factors of one stage: rows * runs * 8
   int addend_mode;
   const float *addend;
-  float *y;
+  OutSpec out;
   int *err;
 };
 
@@ -529,11 +529,20 @@ __global__ void __launch_bounds__(MAXT, MINB)
             sum += red_team[((cc * RPT + i) * p.team_warps + wi) * MR + m];
           if (p.addend_mode == 1) sum = sum + __ldcg(p.addend + row);
           else if (p.addend_mode == 2) sum = sum + __ldcg(p.addend + (size_t)m * p.n + row);
-          p.y[(size_t)m * p.n + row] = sum;
+          out_store(p.out, m, row, sum);
         }
       }
       named_barrier(1 + team, team_threads);
     }
+  }
+  // a tensor-parallel call: every consumer's stores are fenced, then one
+  // thread (past the grid dependency wait) counts the CTA
+  if (p.out.cta_counter) {
+    out_fence(p.out);
+    named_barrier(13, consumer_warps * 32);
+    if (threadIdx.x == 32) out_complete(p.out, gridDim.x);
+  } else {
+    out_fence(p.out);
   }
 }
 
@@ -542,7 +551,7 @@ __global__ void __launch_bounds__(MAXT, MINB)
 template <int FMT, int MR, int R, int MAXT>
 __global__ void __launch_bounds__(MAXT, 1)
     gemv_simple_kernel(const uint8_t *__restrict__ w, int n, int k, const float *__restrict__ x,
-                       float *__restrict__ y, const float *__restrict__ addend, int addend_mode,
+                       const OutSpec out, const float *__restrict__ addend, int addend_mode,
                        int rows_per_cta) {
   __shared__ float red[2][32][R * MR];
   const Layout L(FMT, (uint64_t)n, (uint64_t)k);
@@ -599,11 +608,14 @@ __global__ void __launch_bounds__(MAXT, 1)
         for (int wi = 0; wi < nwarps; ++wi) s += red[buf][wi][threadIdx.x];
         if (addend_mode == 1) s = s + addend[row];
         else if (addend_mode == 2) s = s + addend[(size_t)m * n + row];
-        y[(size_t)m * n + row] = s;
+        out_store(out, m, row, s);
       }
     }
     buf ^= 1;
   }
+  out_fence(out);
+  __syncthreads();
+  if (threadIdx.x == 0) out_complete(out, gridDim.x);
 }
 
 // ---- launch --------------------------------------------------------------------------
@@ -682,7 +694,7 @@ static bool staged_fits(int n, int k, int sms) {
 // The staged GEMV: a programmatic dependent of whatever precedes it on the
 // stream (its weight stream starts at once; it waits before reading x).
 template <int FMT, int MR, int MAXT, int MINB>
-static cudaError_t launch_staged(const void *w, int n, int k, const float *x, float *y,
+static cudaError_t launch_staged(const void *w, int n, int k, const float *x, const OutSpec &out,
                                  const float *addend, int addend_mode, int *err, int sms,
                                  cudaStream_t stream) {
   GemvStaged p;
@@ -690,7 +702,7 @@ static cudaError_t launch_staged(const void *w, int n, int k, const float *x, fl
   const size_t smem = staged_config<FMT, MR, MAXT>(n, k, sms, p, grid, threads);
   p.addend_mode = addend_mode;
   p.addend = addend;
-  p.y = y;
+  p.out = out;
   p.err = err;
   auto kern = gemv_staged_kernel<FMT, MR, MAXT, MINB>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -700,7 +712,7 @@ static cudaError_t launch_staged(const void *w, int n, int k, const float *x, fl
 }
 
 template <int FMT, int MR, int R, int MAXT>
-static cudaError_t launch_simple(const void *w, int n, int k, const float *x, float *y,
+static cudaError_t launch_simple(const void *w, int n, int k, const float *x, const OutSpec &out,
                                  const float *addend, int addend_mode, int sms,
                                  cudaStream_t stream) {
   const int runs = k / RUN;
@@ -713,47 +725,54 @@ static cudaError_t launch_simple(const void *w, int n, int k, const float *x, fl
   if (rows < 1) rows = 1;
   const int grid = (int)ceil_div((uint64_t)n, (uint64_t)rows);
   gemv_simple_kernel<FMT, MR, R, MAXT><<<grid, threads, 0, stream>>>(
-      static_cast<const uint8_t *>(w), n, k, x, y, addend, addend_mode, rows);
+      static_cast<const uint8_t *>(w), n, k, x, out, addend, addend_mode, rows);
   return cudaGetLastError();
 }
 
 static bool staged_ok(uint64_t k) { return k % 256 == 0 && k / RUN <= 31 * 32; }
 
 template <int FMT, int MR>
-static cudaError_t launch_fmt(const void *w, int n, int k, const float *x, float *y,
+static cudaError_t launch_fmt(const void *w, int n, int k, const float *x, const OutSpec &out,
                               const float *addend, int addend_mode, int *err, int sms,
                               cudaStream_t stream) {
+  // Two activation rows in two launches: the first writes output row 0 and
+  // leaves the call's completion to the second, which writes row 1.
+  const float *addend1 = addend_mode == 2 ? addend + n : addend;
   if (staged_ok((uint64_t)k)) {  // a team of at most 31 warps plus the producer
     // 288 threads with at most 112 registers each: two kernels' CTAs fit on an SM
     if (k <= 8192 && staged_fits<FMT, MR, 288>(n, k, sms))
-      return launch_staged<FMT, MR, 288, 2>(w, n, k, x, y, addend, addend_mode, err, sms, stream);
+      return launch_staged<FMT, MR, 288, 2>(w, n, k, x, out, addend, addend_mode, err, sms, stream);
     if (k > 8192 && staged_fits<FMT, 1, 1024>(n, k, sms)) {
       // 1024-thread CTAs have 64 registers per thread: one activation row per launch
-      cudaError_t e = launch_staged<FMT, 1, 1024, 1>(w, n, k, x, y, addend, addend_mode, err, sms, stream);
-      if (MR == 2 && e == cudaSuccess)
-        e = launch_staged<FMT, 1, 1024, 1>(w, n, k, x + k, y + n, addend_mode == 2 ? addend + n : addend,
-                                           addend_mode, err, sms, stream);
+      if (MR == 1)
+        return launch_staged<FMT, 1, 1024, 1>(w, n, k, x, out, addend, addend_mode, err, sms, stream);
+      cudaError_t e = launch_staged<FMT, 1, 1024, 1>(w, n, k, x, without_completion(out), addend,
+                                                     addend_mode, err, sms, stream);
+      if (e == cudaSuccess)
+        e = launch_staged<FMT, 1, 1024, 1>(w, n, k, x + k, rows_from(out, 1), addend1, addend_mode,
+                                           err, sms, stream);
       return e;
     }
   }
-  if (k <= 256 * 32) return launch_simple<FMT, MR, 4, 256>(w, n, k, x, y, addend, addend_mode, sms, stream);
-  cudaError_t e = launch_simple<FMT, 1, 2, 1024>(w, n, k, x, y, addend, addend_mode, sms, stream);
-  if (MR == 2 && e == cudaSuccess)
-    e = launch_simple<FMT, 1, 2, 1024>(w, n, k, x + k, y + n,
-                                       addend_mode == 2 ? addend + n : addend, addend_mode, sms,
+  if (k <= 256 * 32) return launch_simple<FMT, MR, 4, 256>(w, n, k, x, out, addend, addend_mode, sms, stream);
+  if (MR == 1) return launch_simple<FMT, 1, 2, 1024>(w, n, k, x, out, addend, addend_mode, sms, stream);
+  cudaError_t e = launch_simple<FMT, 1, 2, 1024>(w, n, k, x, without_completion(out), addend,
+                                                 addend_mode, sms, stream);
+  if (e == cudaSuccess)
+    e = launch_simple<FMT, 1, 2, 1024>(w, n, k, x + k, rows_from(out, 1), addend1, addend_mode, sms,
                                        stream);
   return e;
 }
 
 cudaError_t launch_gemv(int fmt, const void *w, uint64_t n, uint64_t k, const float *x,
-                        uint64_t m, float *y, const float *addend, int addend_mode, int *err,
-                        int sms, cudaStream_t stream) {
+                        uint64_t m, const OutSpec &out, const float *addend, int addend_mode,
+                        int *err, int sms, cudaStream_t stream) {
   // m <= 2 per launch; larger m is split into row pairs by the caller.
   const int N = (int)n, K = (int)k;
 #define MGB_GEMV_CASE(F)                                                                      \
   case F:                                                                                     \
-    return m == 1 ? launch_fmt<F, 1>(w, N, K, x, y, addend, addend_mode, err, sms, stream)    \
-                  : launch_fmt<F, 2>(w, N, K, x, y, addend, addend_mode, err, sms, stream);
+    return m == 1 ? launch_fmt<F, 1>(w, N, K, x, out, addend, addend_mode, err, sms, stream)  \
+                  : launch_fmt<F, 2>(w, N, K, x, out, addend, addend_mode, err, sms, stream);
   switch (fmt) {
     MGB_GEMV_CASE(Q4_K)
     MGB_GEMV_CASE(Q8_0)

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "outspec.h"
+
 namespace mgb {
 
 // layout.cu
@@ -19,20 +21,20 @@ cudaError_t launch_input_major(int fmt, const void *w, uint64_t k_rows, uint64_t
 // previous kernel on the stream drains; it waits for it before reading x).
 // No scratch: each CTA packs its activations into shared memory.
 cudaError_t launch_gemv(int fmt, const void *w, uint64_t n, uint64_t k, const float *x,
-                        uint64_t m, float *y, const float *addend, int addend_mode, int *err,
-                        int sms, cudaStream_t stream);
+                        uint64_t m, const OutSpec &out, const float *addend, int addend_mode,
+                        int *err, int sms, cudaStream_t stream);
 
 // gemm.cu: tensor-core path (bf16 operands, f32 accumulation) for m > 2.
 uint64_t gemm_workspace_bytes(int fmt, uint64_t m, uint64_t n, uint64_t k);
 bool gemm_supported(int fmt, uint64_t m, uint64_t n, uint64_t k);
 cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const float *x,
-                        uint64_t m, float *y, const float *addend, int addend_mode,
+                        uint64_t m, const OutSpec &out, const float *addend, int addend_mode,
                         void *workspace, uint64_t workspace_bytes, int *err, int sms,
                         cudaStream_t stream);
 
 // the GEMM alone on bf16 activations xb[m, k] (no conversion pass)
 cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, const void *xb,
-                             uint64_t m, float *y, const float *addend, int addend_mode, int *err,
+                             uint64_t m, const OutSpec &out, const float *addend, int addend_mode, int *err,
                              int sms, cudaStream_t stream);
 
 // dense.cu

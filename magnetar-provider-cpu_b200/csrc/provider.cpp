@@ -291,8 +291,9 @@ mgb_status run_matmul(mgb_provider *p, const std::string &kernel, const mgb_kern
       s = ensure_workspace(p, ws);
       if (s != MGB_OK) return s;
     }
-    s = run_qmatmul(w.format, w.buf.ptr, n, k, act, m, static_cast<float *>(product.ptr), nullptr,
-                    0, p->workspace.ptr, p->workspace.bytes, p->dev_err, kernel_pref, p->stream);
+    s = run_qmatmul(w.format, w.buf.ptr, n, k, act, m,
+                    plain_out(static_cast<float *>(product.ptr), n), nullptr, 0, p->workspace.ptr,
+                    p->workspace.bytes, p->dev_err, kernel_pref, p->stream);
     if (s != MGB_OK) {
       free_buf(product);
       return s;

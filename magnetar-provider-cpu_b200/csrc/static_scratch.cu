@@ -72,6 +72,7 @@ extern "C" mgb_status mgb_qmatmul_static_scratch(int32_t format, const void *w, 
   // The scratch is fully rewritten by each call before it is read (nothing in
   // it has to start at zero).  No error word is passed: a bounded device wait
   // that expires leaves y unspecified and is not reported through this call.
-  return run_qmatmul(format, w, n, k, x, m, y, addend, mode, scratch, MGB_STATIC_SCRATCH_BYTES,
-                     nullptr, MGB_KERNEL_AUTO, static_cast<cudaStream_t>(stream));
+  return run_qmatmul(format, w, n, k, x, m, plain_out(y, n), addend, mode, scratch,
+                     MGB_STATIC_SCRATCH_BYTES, nullptr, MGB_KERNEL_AUTO,
+                     static_cast<cudaStream_t>(stream));
 }

@@ -1,0 +1,168 @@
+// Tensor parallelism over output columns: the C ABI of the fused all-gather.
+//
+// Each rank's packed matmul stores its columns into every rank's y (IPC
+// mappings of the peers' buffers over NVLink), and its last CTA publishes the
+// call's epoch into every rank's done words (OutSpec, common.cuh).  A rank then
+// waits for all ranks' epochs with one small stream-ordered kernel.  The
+// column split is the reference's per-thread unit of `packed_matmul`
+// (src/native/mod.rs:135-150): whole stored rows, so no block is cut.
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "../../include/magnetar_b200.h"
+#include "api_internal.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mgb {
+
+static_assert(MGB_MAX_TP == MAX_TP, "C ABI and kernel rank limits differ");
+static_assert(sizeof(cudaIpcMemHandle_t) == MGB_IPC_HANDLE_BYTES, "IPC handle size");
+
+// One warp: lane r polls rank r's done word until it reaches `epoch` (serial
+// number arithmetic, so the epoch may wrap).  Bounded by `timeout_ns` of the
+// global timer and an iteration cap; giving up records ERR_WAIT_TIMEOUT.
+__global__ void tp_wait_kernel(const uint32_t *done, int world, uint32_t epoch,
+                               uint64_t timeout_ns, int *err) {
+  const int lane = threadIdx.x;
+  if (lane >= world) return;
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  uint32_t ns = 32;
+  for (uint32_t i = 0; i < (1u << 26); ++i) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(done + lane) : "memory");
+    if ((int32_t)(v - epoch) >= 0) return;
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > timeout_ns) break;
+    __nanosleep(ns);
+    if (ns < 1024) ns <<= 1;
+  }
+  record_error(err, ERR_WAIT_TIMEOUT);
+}
+
+static mgb_status to_outspec(const mgb_tp_out *o, uint64_t n, OutSpec &spec) {
+  if (!o) return fail(MGB_INVALID_ARGUMENT, "null tensor-parallel output");
+  if (o->world < 1 || o->world > MGB_MAX_TP || o->rank < 0 || o->rank >= o->world)
+    return fail(MGB_INVALID_ARGUMENT, "rank %d of world %d (at most %d ranks)", o->rank, o->world,
+                MGB_MAX_TP);
+  if (!o->cta_counter) return fail(MGB_INVALID_ARGUMENT, "null CTA counter");
+  if (o->col0 + n > o->ldy)
+    return fail(MGB_INVALID_ARGUMENT, "columns %llu..%llu exceed the output row of %llu",
+                (unsigned long long)o->col0, (unsigned long long)(o->col0 + n),
+                (unsigned long long)o->ldy);
+  spec = OutSpec{};
+  for (int r = 0; r < o->world; ++r) {
+    if (!o->y[r] || !o->done[r])
+      return fail(MGB_INVALID_ARGUMENT, "null output or done pointer of rank %d", r);
+    spec.y_ranks[r] = o->y[r];
+    spec.done_ranks[r] = o->done[r];
+  }
+  spec.cta_counter = o->cta_counter;
+  spec.ldy = o->ldy;
+  spec.col0 = o->col0;
+  spec.epoch = o->epoch;
+  spec.world = o->world;
+  spec.rank = o->rank;
+  return MGB_OK;
+}
+
+}  // namespace mgb
+
+using namespace mgb;
+
+extern "C" {
+
+mgb_status mgb_device_alloc(uint64_t bytes, void **out) {
+  if (!out) return fail(MGB_INVALID_ARGUMENT, "null output pointer");
+  *out = nullptr;
+  if (bytes == 0) return fail(MGB_INVALID_ARGUMENT, "zero-byte allocation");
+  void *p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+  e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "zero-filling an allocation");
+  }
+  *out = p;
+  return MGB_OK;
+}
+
+mgb_status mgb_device_free(void *ptr) {
+  if (!ptr) return MGB_OK;
+  cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? MGB_OK : cuda_fail(e, "cudaFree");
+}
+
+mgb_status mgb_ipc_handle(void *ptr, uint8_t *handle_out) {
+  if (!ptr || !handle_out) return fail(MGB_INVALID_ARGUMENT, "null pointer");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  memcpy(handle_out, &h, sizeof(h));
+  return MGB_OK;
+}
+
+mgb_status mgb_ipc_open(const uint8_t *handle, void **out) {
+  if (!handle || !out) return fail(MGB_INVALID_ARGUMENT, "null pointer");
+  *out = nullptr;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void *p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  *out = p;
+  return MGB_OK;
+}
+
+mgb_status mgb_ipc_close(void *mapped) {
+  if (!mapped) return MGB_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(mapped);
+  return e == cudaSuccess ? MGB_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+mgb_status mgb_qmatmul_tp(int32_t format, const void *w, uint64_t n, uint64_t k, const float *x,
+                          uint64_t m, const mgb_tp_out *out, const float *addend,
+                          uint64_t addend_len, void *workspace, uint64_t workspace_bytes,
+                          void *stream) {
+  OutSpec spec;
+  mgb_status s = to_outspec(out, n, spec);
+  if (s != MGB_OK) return s;
+  s = validate_qmatmul(format, w, n, k, x, m, spec.y_ranks[spec.rank]);
+  if (s != MGB_OK) return s;
+  if (m == 0 || n == 0)
+    return fail(MGB_INVALID_ARGUMENT, "an empty tensor-parallel call publishes nothing");
+  int mode = 0;
+  if (addend) {
+    if (addend_len == n) mode = 1;
+    else if (addend_len == m * n) mode = 2;
+    else return fail(MGB_INVALID_ARGUMENT, "addend has %llu values, expected %llu or %llu",
+                     (unsigned long long)addend_len, (unsigned long long)n,
+                     (unsigned long long)(m * n));
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return run_qmatmul(format, w, n, k, x, m, spec, addend, mode, workspace, workspace_bytes,
+                     device_error_flag(dev), MGB_KERNEL_AUTO, static_cast<cudaStream_t>(stream));
+}
+
+mgb_status mgb_tp_wait(const uint32_t *done, int32_t world, uint32_t epoch, uint32_t timeout_ms,
+                       void *stream) {
+  if (!done) return fail(MGB_INVALID_ARGUMENT, "null done words");
+  if (world < 1 || world > MGB_MAX_TP)
+    return fail(MGB_INVALID_ARGUMENT, "world %d (at most %d ranks)", world, MGB_MAX_TP);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t ns = (uint64_t)(timeout_ms ? timeout_ms : 2000) * 1000000ull;
+  tp_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(done, world, epoch, ns,
+                                                                  device_error_flag(dev));
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MGB_OK : cuda_fail(e, "wait launch");
+}
+
+}  // extern "C"

@@ -78,6 +78,20 @@ class Observation(ctypes.Structure):
                 ("kernel", ctypes.c_char * 48), ("detail", ctypes.c_char * 112)]
 
 
+MAX_TP = 8
+TP_SYNC_BYTES = 256
+TP_COUNTER_OFFSET = 128
+IPC_HANDLE_BYTES = 64
+
+
+class TpOut(ctypes.Structure):
+    """`mgb_tp_out`: where one rank's tensor-parallel call writes."""
+    _fields_ = [("y", ctypes.c_void_p * MAX_TP), ("done", ctypes.c_void_p * MAX_TP),
+                ("cta_counter", ctypes.c_void_p), ("ldy", ctypes.c_uint64),
+                ("col0", ctypes.c_uint64), ("epoch", ctypes.c_uint32), ("world", ctypes.c_int32),
+                ("rank", ctypes.c_int32)]
+
+
 _lib = None
 _vp, _u64, _i32, _cp = ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int32, ctypes.c_char_p
 _u64p = ctypes.POINTER(ctypes.c_uint64)
@@ -126,6 +140,14 @@ _SIGNATURES = {
     "mgb_matmul_f32": ([_vp, _u64, _u64, _vp, _u64, _u64, _i32, _i32, _vp, _vp], _i32),
     "mgb_quantize_rows": ([_vp, _u64, _vp, _vp, _vp, _vp], _i32),
     "mgb_take_device_error": ([_i32, _i32p], _i32),
+    "mgb_device_alloc": ([_u64, ctypes.POINTER(_vp)], _i32),
+    "mgb_device_free": ([_vp], _i32),
+    "mgb_ipc_handle": ([_vp, _vp], _i32),
+    "mgb_ipc_open": ([_vp, ctypes.POINTER(_vp)], _i32),
+    "mgb_ipc_close": ([_vp], _i32),
+    "mgb_qmatmul_tp": ([_i32, _vp, _u64, _u64, _vp, _u64, ctypes.POINTER(TpOut), _vp, _u64, _vp,
+                        _u64, _vp], _i32),
+    "mgb_tp_wait": ([_vp, _i32, ctypes.c_uint32, ctypes.c_uint32, _vp], _i32),
 }
 
 
@@ -207,6 +229,65 @@ def take_device_error(device: int = 0) -> int:
     code = ctypes.c_int32(0)
     check(lib().mgb_take_device_error(device, ctypes.byref(code)))
     return code.value
+
+
+# ---- tensor parallelism (device pointers as ints) -------------------------------------
+
+
+def device_alloc(nbytes: int) -> int:
+    """A whole zero-filled cudaMalloc allocation on the current device."""
+    p = ctypes.c_void_p()
+    check(lib().mgb_device_alloc(nbytes, ctypes.byref(p)))
+    return int(p.value)
+
+
+def device_free(ptr: int) -> None:
+    check(lib().mgb_device_free(ptr or None))
+
+
+def ipc_handle(ptr: int) -> bytes:
+    buf = (ctypes.c_uint8 * IPC_HANDLE_BYTES)()
+    check(lib().mgb_ipc_handle(ptr, buf))
+    return bytes(buf)
+
+
+def ipc_open(handle: bytes) -> int:
+    if len(handle) != IPC_HANDLE_BYTES:
+        raise ValueError(f"an IPC handle has {IPC_HANDLE_BYTES} bytes, not {len(handle)}")
+    buf = (ctypes.c_uint8 * IPC_HANDLE_BYTES).from_buffer_copy(handle)
+    p = ctypes.c_void_p()
+    check(lib().mgb_ipc_open(buf, ctypes.byref(p)))
+    return int(p.value)
+
+
+def ipc_close(ptr: int) -> None:
+    check(lib().mgb_ipc_close(ptr or None))
+
+
+def tp_out(y: list[int], done: list[int], cta_counter: int, ldy: int, col0: int, epoch: int,
+           rank: int) -> TpOut:
+    world = len(y)
+    if len(done) != world:
+        raise ValueError("one done pointer per rank")
+    o = TpOut()
+    for r in range(world):
+        o.y[r] = y[r]
+        o.done[r] = done[r]
+    o.cta_counter = cta_counter
+    o.ldy, o.col0, o.epoch, o.world, o.rank = ldy, col0, epoch & 0xFFFFFFFF, world, rank
+    return o
+
+
+def qmatmul_tp(fmt: int, w_ptr: int, n: int, k: int, x_ptr: int, m: int, out: TpOut,
+               addend_ptr: int = 0, addend_len: int = 0, workspace_ptr: int = 0,
+               workspace_bytes: int = 0, stream: int = 0) -> None:
+    check(lib().mgb_qmatmul_tp(fmt, w_ptr, n, k, x_ptr, m, ctypes.byref(out), addend_ptr or None,
+                               addend_len, workspace_ptr or None, workspace_bytes, stream or None))
+
+
+def tp_wait(done_ptr: int, world: int, epoch: int, timeout_ms: int = 0, stream: int = 0) -> None:
+    check(lib().mgb_tp_wait(done_ptr or None, world, epoch & 0xFFFFFFFF, timeout_ms,
+                            stream or None))
 
 
 # ---- the Provider ---------------------------------------------------------------------

@@ -4,12 +4,18 @@ A packed weight's stored rows are the matmul's output columns, and each stored
 row is a whole sequence of blocks, so the rows split across ranks without
 touching a block: rank g of G holds stored rows [g N/G, (g+1) N/G) (the unit the
 reference's CPU pool partitions on, `packed_matmul`, src/native/mod.rs:135-150).
-Every rank multiplies the same activations by its shard; the [M, N/G] outputs
-are then all-gathered (NCCL over NVLink between B200s; gloo on CPU for the host
-logic's tests) and interleaved back to [M, N].
+Every rank multiplies the same activations by its shard and every rank ends
+with the full [M, N].  Two exchanges:
 
-This module is the host side of the multi-GPU path: it owns the sharding and the
-exchange, the kernels stay the single-GPU ones.
+- `FusedShardedPackedMatmul` (the B200 path): the kernels store each output
+  column straight into every rank's y over NVLink (peers' buffers mapped with
+  CUDA IPC), then publish the call's epoch; a rank waits for all epochs with
+  one stream-ordered kernel (`mgb_qmatmul_tp`, `mgb_tp_wait`).  No collective
+  launch, no gather buffer, no interleave pass: the transfer overlaps the tiles
+  still computing.
+- `ShardedPackedMatmul` + `gather_columns`: the rank's [M, N/G] block, then an
+  NCCL (gloo on CPU, for the host logic's tests) all-gather and an interleave
+  back to [M, N] — the library baseline.
 """
 
 from __future__ import annotations
@@ -103,3 +109,112 @@ class ShardedPackedMatmul:
 
     def __call__(self, x, group=None):
         return gather_columns(self.local(x), group)
+
+
+class _DeviceArray:
+    """A raw device pointer as a CUDA array (for torch.as_tensor)."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...]):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": "<f4", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class FusedShardedPackedMatmul(ShardedPackedMatmul):
+    """The sharded matmul with the all-gather fused into the kernels' stores.
+
+    Each rank owns two y buffers of [max_m, N] f32 and 256 bytes of
+    synchronisation words (`mgb_device_alloc`), and maps every peer's with CUDA
+    IPC (handles exchanged once with `all_gather_object`).  Call e writes into
+    buffer e % 2 of every rank, then waits (on the stream) until every rank has
+    published epoch e.  The returned tensor views this rank's buffer: it stays
+    valid until the call after next, which rewrites it.  Two buffers suffice:
+    rank A writes buffer b for call e+2 only after it has seen every peer's
+    epoch e+1, and a peer publishes e+1 only after its stream has finished all
+    work queued before that call, including its reads of call e's result."""
+
+    def __init__(self, fmt: int, ggml_shard: np.ndarray, n: int, k: int, world: int, rank: int,
+                 max_m: int, group=None, device=None, timeout_ms: int = 2000):
+        import torch.distributed as dist
+
+        import magnetar_b200 as mgb
+
+        super().__init__(fmt, ggml_shard, n, k, world, rank, device)
+        if world > mgb.MAX_TP:
+            raise ValueError(f"at most {mgb.MAX_TP} ranks")
+        self.max_m, self.group, self.timeout_ms = max_m, group, timeout_ms
+        self._own: list[int] = []
+        self._mapped: list[int] = []
+        try:
+            self.sync = self._alloc(mgb.TP_SYNC_BYTES)
+            self.slots = [self._alloc(max_m * n * 4) for _ in range(2)]
+            mine = [mgb.ipc_handle(p) for p in (self.sync, *self.slots)]
+            handles: list = [None] * world
+            if world > 1:
+                dist.all_gather_object(handles, mine, group=group)
+            else:
+                handles = [mine]
+            peers = []
+            for r, hs in enumerate(handles):
+                if r == rank:
+                    peers.append((self.sync, *self.slots))
+                else:
+                    ptrs = []
+                    for h in hs:
+                        ptrs.append(mgb.ipc_open(h))
+                        self._mapped.append(ptrs[-1])
+                    peers.append(tuple(ptrs))
+            if world > 1:
+                dist.barrier(group=group)
+        except Exception:
+            self.close()
+            raise
+        self.done = [p[0] for p in peers]
+        self.y_slots = [[p[1 + s] for p in peers] for s in range(2)]
+        self.epoch = 0
+
+    def _alloc(self, nbytes: int) -> int:
+        import magnetar_b200 as mgb
+
+        ptr = mgb.device_alloc(nbytes)
+        self._own.append(ptr)
+        return ptr
+
+    def __call__(self, x, group=None):
+        """y [M, N] (every rank's columns) for device activations x [M, K] (f32)."""
+        import torch
+
+        import magnetar_b200 as mgb
+
+        m = x.shape[0]
+        if not 0 < m <= self.max_m:
+            raise ValueError(f"{m} activation rows (1..{self.max_m})")
+        self.epoch += 1
+        slot = self.epoch & 1
+        out = mgb.tp_out(self.y_slots[slot], self.done, self.sync + mgb.TP_COUNTER_OFFSET,
+                         ldy=self.n, col0=self.rank * self.n_loc, epoch=self.epoch, rank=self.rank)
+        ws_bytes = mgb.qmatmul_workspace_bytes(self.fmt, m, self.n_loc, self.k)
+        if ws_bytes and (self._ws is None or self._ws.numel() < ws_bytes):
+            self._ws = torch.empty(ws_bytes, dtype=torch.uint8, device=self.device)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        mgb.qmatmul_tp(self.fmt, self.weight.data_ptr(), self.n_loc, self.k, x.data_ptr(), m, out,
+                       workspace_ptr=self._ws.data_ptr() if ws_bytes else 0,
+                       workspace_bytes=ws_bytes, stream=stream)
+        mgb.tp_wait(self.sync, self.world, self.epoch, self.timeout_ms, stream)
+        return torch.as_tensor(_DeviceArray(self.slots[slot], (m, self.n)), device=self.device)
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers and frees this rank's.  Collective: every
+        rank calls it (no peer may still be writing into this rank's buffers)."""
+        import torch
+        import torch.distributed as dist
+
+        import magnetar_b200 as mgb
+
+        torch.cuda.synchronize(self.device)
+        if self.world > 1 and dist.is_initialized():
+            dist.barrier(group=self.group)
+        for p in self._mapped:
+            mgb.ipc_close(p)
+        for p in self._own:
+            mgb.device_free(p)
+        self._mapped, self._own = [], []

@@ -83,3 +83,36 @@ def test_null_arguments_are_rejected_without_device_work():
     assert lib.mgb_qmatmul(mgb.Q4_K, None, 1, 96, None, 1, None, None, 0, None, 0, None) == \
         mgb.EXECUTION_FAILED
     assert "activations have 96 columns" in mgb.last_error()
+
+
+def test_tensor_parallel_outputs_are_checked_before_device_work():
+    lib = mgb.lib()
+    fake = 1 << 40  # never dereferenced: every case fails validation first
+    good = mgb.tp_out([fake, fake], [fake, fake], fake, ldy=512, col0=256, epoch=1, rank=1)
+
+    def call(out):
+        return lib.mgb_qmatmul_tp(mgb.Q4_K, fake, 256, 256, fake, 1, ctypes.byref(out), None, 0,
+                                  None, 0, None)
+
+    bad = mgb.tp_out([fake] * 2, [fake] * 2, fake, ldy=512, col0=256, epoch=1, rank=2)
+    assert call(bad) == mgb.INVALID_ARGUMENT and "rank 2 of world 2" in mgb.last_error()
+    bad = mgb.tp_out([fake] * 2, [fake] * 2, 0, ldy=512, col0=256, epoch=1, rank=1)
+    assert call(bad) == mgb.INVALID_ARGUMENT and "CTA counter" in mgb.last_error()
+    bad = mgb.tp_out([fake] * 2, [fake] * 2, fake, ldy=500, col0=256, epoch=1, rank=1)
+    assert call(bad) == mgb.INVALID_ARGUMENT and "exceed the output row" in mgb.last_error()
+    bad = mgb.tp_out([fake, 0], [fake] * 2, fake, ldy=512, col0=256, epoch=1, rank=1)
+    assert call(bad) == mgb.INVALID_ARGUMENT and "rank 1" in mgb.last_error()
+    with pytest.raises(ValueError):
+        mgb.tp_out([fake] * 2, [fake], fake, ldy=512, col0=0, epoch=1, rank=0)
+    nine = mgb.TpOut()
+    nine.world, nine.rank, nine.cta_counter = 9, 0, fake
+    assert call(nine) == mgb.INVALID_ARGUMENT
+    assert lib.mgb_qmatmul_tp(mgb.Q4_K, fake, 256, 256, fake, 1, None, None, 0, None, 0, None) \
+        == mgb.INVALID_ARGUMENT
+    # the shape checks of mgb_qmatmul apply to the shard
+    assert lib.mgb_qmatmul_tp(mgb.Q4_K, fake, 256, 96, fake, 1, ctypes.byref(good), None, 0, None,
+                              0, None) == mgb.EXECUTION_FAILED
+    assert lib.mgb_tp_wait(None, 2, 1, 0, None) == mgb.INVALID_ARGUMENT
+    assert lib.mgb_tp_wait(fake, 0, 1, 0, None) == mgb.INVALID_ARGUMENT
+    assert lib.mgb_ipc_open(None, None) == mgb.INVALID_ARGUMENT
+    assert lib.mgb_device_alloc(16, None) == mgb.INVALID_ARGUMENT

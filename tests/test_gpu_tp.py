@@ -1,0 +1,195 @@
+"""GPU parity of the fused tensor-parallel path (`mgb_qmatmul_tp`, `mgb_tp_wait`).
+
+Each rank's kernels store its columns into every rank's y and publish the
+call's epoch.  On one GPU the ranks are emulated: rank 0's and rank 1's calls
+run one after the other on the same stream with two local y buffers and two
+sets of synchronisation words, and the waits run after both calls have
+finished (no kernel waits on another kernel that may still be running on
+the same GPU).  With two GPUs, two processes run the real path over NVLink.
+
+Every output column is computed by the same kernel code as the unsharded
+call (the split is by whole stored rows, `packed_matmul`,
+src/native/mod.rs:135-150), so the gathered y must equal the unsharded
+`mgb_qmatmul` bit for bit, and the oracle within the kernels' tolerances.
+"""
+
+from __future__ import annotations
+
+import datetime
+import multiprocessing as mp
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import magnetar_b200 as mgb
+import synthetic
+import tp
+
+pytestmark = pytest.mark.gpu
+
+GEMV_TOL, GEMM_TOL = 1e-3, 5e-3
+
+
+@pytest.fixture(scope="module")
+def torch_cuda(cuda_device):
+    import torch
+
+    torch.cuda.set_device(cuda_device)
+    return torch
+
+
+def _device_layout(torch, fmt, ggml, rows, cols):
+    src = torch.from_numpy(np.ascontiguousarray(ggml)).cuda()
+    out = torch.empty(mgb.packed_bytes(fmt, rows, cols), dtype=torch.uint8, device="cuda")
+    mgb.repack(fmt, src.data_ptr(), rows, cols, out.data_ptr(),
+               torch.cuda.current_stream().cuda_stream)
+    return out
+
+
+def _unsharded(torch, fmt, w, n, k, xd):
+    m = xd.shape[0]
+    wd = _device_layout(torch, fmt, w, n, k)
+    y = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    ws_bytes = mgb.qmatmul_workspace_bytes(fmt, m, n, k)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+    mgb.qmatmul(fmt, wd.data_ptr(), n, k, xd.data_ptr(), m, y.data_ptr(),
+                workspace_ptr=ws.data_ptr(), workspace_bytes=ws_bytes,
+                stream=torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    return y.cpu().numpy()
+
+
+CASES = [
+    # fmt, n, k, m: GEMV (one and two rows), the GEMM, the two-launch GEMV
+    # (k > 8192), the direct-load GEMV (k % 256 != 0)
+    (synthetic.Q4_K, 512, 1024, 1),
+    (synthetic.Q4_K, 512, 1024, 2),
+    (synthetic.Q4_K, 512, 1024, 5),
+    (synthetic.Q4_K, 1024, 2048, 130),
+    (synthetic.Q8_0, 256, 512, 3),
+    (synthetic.IQ4_NL, 256, 512, 2),
+    (synthetic.Q4_0, 256, 512, 64),
+    (synthetic.Q4_K, 256, 16384, 2),
+    (synthetic.Q8_0, 128, 96, 2),
+    (synthetic.Q8_0, 64, 8224, 2),
+]
+
+
+@pytest.mark.parametrize("fmt,n,k,m", CASES)
+def test_emulated_two_ranks_gather_every_column(torch_cuda, oracle, fmt, n, k, m):
+    torch = torch_cuda
+    world = 2
+    w = synthetic.packed_weights(fmt, n, k, seed=21)
+    x = synthetic.activations(m, k, seed=22)
+    xd = torch.from_numpy(x).cuda()
+    shards = [_device_layout(torch, fmt, tp.shard_packed(fmt, w, n, k, world, r), n // world, k)
+              for r in range(world)]
+    ys = [torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda") for _ in range(world)]
+    sync = [mgb.device_alloc(mgb.TP_SYNC_BYTES) for _ in range(world)]
+    ws_bytes = mgb.qmatmul_workspace_bytes(fmt, m, n // world, k)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+    sp = torch.cuda.current_stream().cuda_stream
+    try:
+        for epoch in (1, 2, 3):  # the CTA counters must come back to zero each call
+            for r in range(world):
+                out = mgb.tp_out([y.data_ptr() for y in ys], sync,
+                                 sync[r] + mgb.TP_COUNTER_OFFSET, ldy=n, col0=r * (n // world),
+                                 epoch=epoch, rank=r)
+                mgb.qmatmul_tp(fmt, shards[r].data_ptr(), n // world, k, xd.data_ptr(), m, out,
+                               workspace_ptr=ws.data_ptr(), workspace_bytes=ws_bytes, stream=sp)
+            for r in range(world):
+                mgb.tp_wait(sync[r], world, epoch, 2000, sp)
+            torch.cuda.synchronize()
+            assert mgb.take_device_error(torch.cuda.current_device()) == 0
+            for r in range(world):
+                words = torch.as_tensor(tp._DeviceArray(sync[r], (mgb.TP_SYNC_BYTES // 4,)),
+                                        device="cuda").view(torch.int32).cpu().numpy()
+                assert list(words[:world]) == [epoch] * world
+                assert words[mgb.TP_COUNTER_OFFSET // 4] == 0
+        got = [y.cpu().numpy() for y in ys]
+    finally:
+        for p in sync:
+            mgb.device_free(p)
+    np.testing.assert_array_equal(got[0], got[1])
+    np.testing.assert_array_equal(got[0], _unsharded(torch, fmt, w, n, k, xd))
+    oracle.assert_close(got[0], oracle.packed_matmul(fmt, w, n, k, x),
+                        GEMV_TOL if m <= 2 else GEMM_TOL, f"tp fmt {fmt} m {m}")
+
+
+def test_wait_for_an_epoch_nobody_publishes_times_out(torch_cuda):
+    """The bounded wait gives up, records device error 1 and the context stays usable."""
+    torch = torch_cuda
+    sync = mgb.device_alloc(mgb.TP_SYNC_BYTES)
+    try:
+        assert mgb.take_device_error(torch.cuda.current_device()) == 0
+        mgb.tp_wait(sync, 2, 7, timeout_ms=20, stream=torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert mgb.take_device_error(torch.cuda.current_device()) == 1
+        assert float(torch.ones(4, device="cuda").sum()) == 4.0
+    finally:
+        mgb.device_free(sync)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank: int, world: int, port: int, out) -> None:
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    op = None
+    try:
+        fmt, n, k = synthetic.Q4_K, 1024, 2048
+        w = synthetic.packed_weights(fmt, n, k, seed=31)
+        op = tp.FusedShardedPackedMatmul(fmt, tp.shard_packed(fmt, w, n, k, world, rank), n, k,
+                                         world, rank, max_m=64)
+        mismatches = []
+        for call, m in enumerate([1, 2, 64, 5, 1, 64]):
+            xd = torch.from_numpy(synthetic.activations(m, k, seed=40 + call)).to(dev)
+            y = op(xd).cpu().numpy()
+            ref = _unsharded(torch, fmt, w, n, k, xd)
+            if not np.array_equal(y, ref):
+                mismatches.append((call, m, float(np.nanmax(np.abs(y - ref)))))
+        torch.cuda.synchronize()
+        err = mgb.take_device_error(rank)
+        out.put((rank, mismatches, err))
+    except Exception as e:  # reported to the parent; the barrier below still runs
+        out.put((rank, repr(e), -1))
+    finally:
+        if op is not None:
+            op.close()
+        dist.destroy_process_group()
+
+
+def test_two_gpus_fused_gather_matches_unsharded(torch_cuda):
+    torch = torch_cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = []
+    try:
+        for _ in procs:
+            results.append(out.get(timeout=300))
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    for rank, mismatches, err in sorted(results):
+        assert mismatches == [] and err == 0, (rank, mismatches, err)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
