@@ -7,7 +7,7 @@
 // CTA tile: BM activation rows (1 or 2 accumulators of 128 rows) x BN weight
 // rows (the MMA N, <= 256, a multiple of 16), K in steps of 64 (one 128-byte
 // swizzle atom of bf16).  Two shared-memory rings: operand stages (the
-// activation tile and the bf16 W tile of a K step, 3 deep), each with one
+// activation tile and the bf16 W tile of a K step, 3 to 6 deep), each with one
 // `full` barrier (the activation TMA bytes + one arrival per dequantising
 // warp) and one `empty` barrier (the MMAs' commit), so the MMA issuer waits
 // and commits once per step; and packed-W stages (quant and scale boxes from
@@ -25,7 +25,10 @@
 //   warps 3-10 dequantise the staged packed W into the bf16 B operand
 //              (K-major, SWIZZLE_128B written by hand), fence the async proxy
 //              and arrive on full[s] and p_empty[s]; after the last stage they
-//              drain TMEM with tcgen05.ld and write y (+ the addend).
+//              drain TMEM with tcgen05.ld and write y (+ the addend): straight
+//              from registers for one output, through shared memory in whole
+//              row segments when every rank's y receives the tile (fused
+//              all-gather over NVLink).
 // Every CTA loads its own tiles from this GPU's HBM (no cluster-shared loads).
 // Every wait is bounded; on expiry the kernel records ERR_WAIT_TIMEOUT, skips
 // the remaining work, waits (bounded) for its own copies and MMAs, frees TMEM
@@ -131,6 +134,24 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float v[8]) {
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 consecutive columns of this warp's 32 TMEM lanes: lane i gets row i.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float v[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // ---- dequantisation of one 32-value run into 64 bytes of bf16 ----------------------
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
@@ -227,6 +248,94 @@ __device__ __forceinline__ void dequant_run(const uint8_t *wq_row, const uint8_t
 }
 
 // ---- the kernel ----------------------------------------------------------------------
+
+// ---- epilogue ------------------------------------------------------------------------
+
+// Drains this warp's 32 TMEM lanes (lane quarter `quarter`) of `nsub`
+// accumulator blocks into y.  Block b holds output rows row0 + 128 b + 32
+// quarter + lane at TMEM columns b * sub_stride + c for tile columns c <
+// tile_cols (output columns n0 + c); `half` picks this warp's alternate
+// column chunks (two warps per quarter).  One output rank: each lane stores
+// its row's 8-column pieces directly (the L2 merges the warp's row segments).
+// Several ranks: 32-column chunks go through a padded 32 x 33 square of
+// shared memory (`square`, this warp's own) so that the warp's stores cover
+// whole 128-byte row segments: full-size writes over NVLink.
+__device__ __forceinline__ void drain_accumulators(const GemmParams &p, uint32_t tmem_base,
+                                                   int nsub, int sub_stride, int row0, int n0,
+                                                   int tile_cols, int quarter, int half, int lane,
+                                                   float *square) {
+  const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
+  if (p.out.world == 1) {
+    float *y = p.out.y_ranks[0];
+    for (int sub = 0; sub < nsub; ++sub) {
+      const int row = row0 + sub * 128 + quarter * 32 + lane;
+      for (int c = 8 * half; c < tile_cols; c += 16) {
+        float v[8];
+        tmem_ld8(lane_base + (uint32_t)(sub * sub_stride + c), v);
+        if (row >= p.m) continue;
+        const int col = n0 + c;
+        float *yr = y + (size_t)row * p.out.ldy + p.out.col0;
+        if (col + 8 <= p.n && p.addend_mode == 0 && p.vec_out) {
+          reinterpret_cast<float4 *>(yr + col)[0] = make_float4(v[0], v[1], v[2], v[3]);
+          reinterpret_cast<float4 *>(yr + col)[1] = make_float4(v[4], v[5], v[6], v[7]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            if (col + e < p.n) {
+              float o = v[e];
+              if (p.addend_mode == 1) o = o + p.addend[col + e];
+              else if (p.addend_mode == 2) o = o + p.addend[(size_t)row * p.n + col + e];
+              yr[col + e] = o;
+            }
+          }
+        }
+      }
+    }
+    return;
+  }
+  const int sub_lane = lane >> 3, c4 = (lane & 7) * 4;  // store lanes: 4 rows x 8 float4
+  for (int sub = 0; sub < nsub; ++sub) {
+    const int rbase = row0 + sub * 128 + quarter * 32;
+    for (int c = 32 * half; c < tile_cols; c += 64) {
+      float v[32];
+      tmem_ld32(lane_base + (uint32_t)(sub * sub_stride + c), v);
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) square[lane * 33 + j] = v[j];
+      __syncwarp();
+      const int col = n0 + c + c4;  // this lane's first column (a multiple of 4)
+#pragma unroll 2
+      for (int r0 = 0; r0 < 32; r0 += 4) {
+        const int rr = r0 + sub_lane;
+        const int row = rbase + rr;
+        float o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[e] = square[rr * 33 + c4 + e];
+        if (row >= p.m || c + c4 >= tile_cols || col >= p.n) continue;
+        if (p.addend_mode == 1) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (col + e < p.n) o[e] = o[e] + p.addend[col + e];
+        } else if (p.addend_mode == 2) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (col + e < p.n) o[e] = o[e] + p.addend[(size_t)row * p.n + col + e];
+        }
+        // this call's column col lands at col0 + col of every output rank's y
+        const size_t off = (size_t)row * p.out.ldy + p.out.col0 + col;
+        if (p.vec_out && col + 4 <= p.n) {
+          for (int r = 0; r < p.out.world; ++r)
+            *reinterpret_cast<float4 *>(p.out.y_ranks[r] + off) = make_float4(o[0], o[1], o[2], o[3]);
+        } else {
+          for (int r = 0; r < p.out.world; ++r)
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (col + e < p.n) p.out.y_ranks[r][off + e] = o[e];
+        }
+      }
+    }
+  }
+}
 
 __device__ __forceinline__ void grid_dependency_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -407,45 +516,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mbar_arrive(&p_empty[sp]);
       }
     }
-    // epilogue: TMEM lanes of this warp's quarter -> y rows; the two warps of
-    // a quarter take alternate 8-column chunks
+    // epilogue: TMEM lanes of this warp's quarter -> y rows
     const bool finished = mbar_wait(done, 0, p.err);
     tc_fence_after();
     // tcgen05.ld is warp-collective: the whole warp drains TMEM or none of it
-    if (__all_sync(0xffffffffu, finished && !*(volatile int *)abort_flag)) {
-      const int quarter = warp & 3;
-      const int half = (warp - 3) / 4;
-      for (int sub = 0; sub < SUBS; ++sub) {
-        const int row = m0 + sub * 128 + quarter * 32 + lane;
-        for (int c = 8 * half; c < p.bn; c += 16) {
-          float v[8];
-          tmem_ld8(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * 256 + c), v);
-          if (row < p.m) {
-            const int col = n0 + c;
-            // this call's column col lands at col0 + col of every output rank's y
-            if (col + 8 <= p.n && p.addend_mode == 0 && p.vec_out) {
-              for (int r = 0; r < p.out.world; ++r) {
-                float4 *yr = reinterpret_cast<float4 *>(p.out.y_ranks[r] + (size_t)row * p.out.ldy +
-                                                        p.out.col0 + col);
-                yr[0] = make_float4(v[0], v[1], v[2], v[3]);
-                yr[1] = make_float4(v[4], v[5], v[6], v[7]);
-              }
-            } else {
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                if (col + e < p.n) {
-                  float o = v[e];
-                  if (p.addend_mode == 1) o = o + p.addend[col + e];
-                  else if (p.addend_mode == 2) o = o + p.addend[(size_t)row * p.n + col + e];
-                  for (int r = 0; r < p.out.world; ++r)
-                    p.out.y_ranks[r][(size_t)row * p.out.ldy + p.out.col0 + col + e] = o;
-                }
-              }
-            }
-          }
-        }
-      }
-    }
+    const bool drain = __all_sync(0xffffffffu, finished && !*(volatile int *)abort_flag);
+    if (drain)
+      drain_accumulators(p, tmem_base, SUBS, 256, m0, n0, p.bn, warp & 3, (warp - 3) / 4, lane,
+                         reinterpret_cast<float *>(smem) + (warp - 3) * (32 * 33));
   }
   out_fence(p.out);
   tc_fence_before();
@@ -572,33 +650,34 @@ cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const fl
 }
 
 cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, const void *xb,
-                             uint64_t m, const OutSpec &out, const float *addend, int addend_mode, int *err,
-                             int sms, cudaStream_t stream) {
+                             uint64_t m, const OutSpec &out, const float *addend, int addend_mode,
+                             int *err, int sms, cudaStream_t stream) {
   if (!gemm_supported(fmt, m, n, k) || (reinterpret_cast<uintptr_t>(w) & 15) ||
       (reinterpret_cast<uintptr_t>(xb) & 15))
     return cudaErrorInvalidValue;
-  // more than 128 activation rows: CTA pairs sharing each MMA (cta_group::2)
   const Layout L(fmt, n, k);
   const TileChoice t = choose_tiles(m, n, sms);
-  GemmParams p;
+  GemmParams p = {};
   p.m = (int)m;
   p.n = (int)n;
   p.k = (int)k;
-  p.bn = t.bn;
   p.qbytes = fmt == Q8_0 ? 64 : 32;
+  p.bn = t.bn;
   p.a_bytes = 16384u * t.subs;
   p.b_bytes = (uint32_t)ceil_div((uint64_t)t.bn * 128u, 1024) * 1024;
   p.wq_bytes = (uint32_t)ceil_div((uint64_t)t.bn * p.qbytes, 1024) * 1024;
   p.ws_bytes = (uint32_t)ceil_div((uint64_t)t.bn * 16, 1024) * 1024;
   p.pstage_bytes = p.wq_bytes + p.ws_bytes;
   p.ptx_bytes = (uint32_t)t.bn * (uint32_t)p.qbytes + (uint32_t)t.bn * 16u;
-  // operand stages (activation tile + bf16 W tile, 3 deep) and packed-W stages
-  // (streamed from HBM, 3+ deep)
+  const dim3 grid((unsigned)ceil_div(n, (uint64_t)t.bn), (unsigned)ceil_div(m, 128ull * t.subs));
+  // Narrow tiles (few weight rows per CTA) run their K loop faster with more
+  // operand stages in flight: as many as fit (up to 6), then packed stages (up
+  // to 8).
   const uint32_t budget = 225 * 1024 - 1024 /*align slack*/ - 512 /*barriers*/;
   const uint32_t ab = p.a_bytes + p.b_bytes;
-  int sa = 3, sp = 3;
-  while (sa * ab + sp * p.pstage_bytes > budget && sa > 2) --sa;
+  int sa = 2, sp = 3;
   if (sa * ab + sp * p.pstage_bytes > budget) return cudaErrorInvalidValue;
+  while (sa < 6 && (sa + 1) * ab + sp * p.pstage_bytes <= budget) ++sa;
   while (sp < 8 && sa * ab + (sp + 1) * p.pstage_bytes <= budget) ++sp;
   p.astages = sa;
   p.bstages = sa;
@@ -622,19 +701,18 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
     return cudaErrorInvalidValue;
 
   const size_t smem = (size_t)sa * ab + (size_t)sp * p.pstage_bytes + 1024 + 512;
-  dim3 grid((unsigned)ceil_div(n, (uint64_t)t.bn), (unsigned)ceil_div(m, 128ull * t.subs));
   cudaError_t e = cudaSuccess;
-#define MGB_GEMM_LAUNCH(F, SUBS)                                                               \
+#define MGB_GEMM_LAUNCH(KERN)                                                                  \
   do {                                                                                         \
-    auto kern = gemm_kernel<F, SUBS>;                                                          \
+    auto kern = KERN;                                                                          \
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \
     if (e != cudaSuccess) return e;                                                            \
     e = launch_dependent(kern, grid, dim3(NUM_THREADS), smem, stream, map_a, map_wq, map_ws, p); \
   } while (0)
-#define MGB_GEMM_FMT(F)                          \
-  case F:                                        \
-    if (t.subs == 2) MGB_GEMM_LAUNCH(F, 2);      \
-    else MGB_GEMM_LAUNCH(F, 1);                  \
+#define MGB_GEMM_FMT(F)                                     \
+  case F:                                                   \
+    if (t.subs == 2) MGB_GEMM_LAUNCH((gemm_kernel<F, 2>));  \
+    else MGB_GEMM_LAUNCH((gemm_kernel<F, 1>));              \
     break;
   switch (fmt) {
     MGB_GEMM_FMT(Q4_K)

@@ -89,6 +89,7 @@ struct mgb_provider {
   std::deque<mgb_observation> observations;
   uint64_t obs_seq = 0;
   DevBuf workspace;
+  cudaMemPool_t pool = nullptr;  // this Provider's stream-ordered device memory
   int *dev_err = nullptr;
   uint64_t materializations = 0;
   double materialize_ms = 0.0;
@@ -109,22 +110,31 @@ void observe(mgb_provider *p, int32_t kind, const std::string &kernel, const std
   p->observations.push_back(o);
 }
 
-void free_buf(DevBuf &b) {
-  if (b.ptr) cudaFree(b.ptr);
+// Device buffers come from the Provider's own memory pool, in the order of its
+// stream: a free is queued behind the work that still reads the buffer (no
+// host synchronisation), and the pool keeps freed memory for the next
+// allocation of the step (no cudaMalloc / cudaFree per tensor).
+void free_buf(mgb_provider *p, DevBuf &b) {
+  if (b.ptr) cudaFreeAsync(b.ptr, p->stream);
   b.ptr = nullptr;
   b.bytes = 0;
 }
 
-// Reuses `b` when it already holds `bytes`, else reallocates; fallible.
+// Reuses `b` when it already holds `bytes`, else reallocates; fallible.  An
+// allocation the device cannot satisfy returns the pool's idle memory to the
+// device and tries once more before it is denied.
 mgb_status ensure_buf(mgb_provider *p, DevBuf &b, uint64_t bytes) {
   if (b.ptr && b.bytes == bytes) return MGB_OK;
-  if (b.ptr) {
-    cudaStreamSynchronize(p->stream);
-    free_buf(b);
-  }
+  if (b.ptr) free_buf(p, b);
   if (!bytes) return MGB_OK;
   void *ptr = nullptr;
-  cudaError_t e = cudaMalloc(&ptr, bytes);
+  cudaError_t e = cudaMallocFromPoolAsync(&ptr, bytes, p->pool, p->stream);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    cudaStreamSynchronize(p->stream);
+    cudaMemPoolTrimTo(p->pool, 0);
+    e = cudaMallocFromPoolAsync(&ptr, bytes, p->pool, p->stream);
+  }
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(MGB_MEMORY_DENIED, "device allocation of %llu bytes denied: %s",
@@ -138,8 +148,7 @@ mgb_status ensure_buf(mgb_provider *p, DevBuf &b, uint64_t bytes) {
 bool forget_packed(mgb_provider *p, const std::string &id) {
   auto it = p->packed.find(id);
   if (it == p->packed.end()) return false;
-  cudaStreamSynchronize(p->stream);
-  free_buf(it->second.buf);
+  free_buf(p, it->second.buf);
   p->packed.erase(it);
   return true;
 }
@@ -147,8 +156,7 @@ bool forget_packed(mgb_provider *p, const std::string &id) {
 bool forget_tensor(mgb_provider *p, const std::string &id) {
   auto it = p->storage.find(id);
   if (it == p->storage.end()) return false;
-  cudaStreamSynchronize(p->stream);
-  free_buf(it->second.buf);
+  free_buf(p, it->second.buf);
   p->storage.erase(it);
   return true;
 }
@@ -173,7 +181,7 @@ mgb_status expand(mgb_provider *p, const Packed &w, DevBuf &out) {
   cudaError_t e = launch_dequantize(w.format, w.buf.ptr, w.stored_rows, w.stored_cols,
                                     static_cast<float *>(stored.ptr), p->stream);
   if (e != cudaSuccess) {
-    free_buf(stored);
+    free_buf(p, stored);
     return cuda_fail(e, "dequantize launch");
   }
   if (!w.transposed) {
@@ -182,13 +190,12 @@ mgb_status expand(mgb_provider *p, const Packed &w, DevBuf &out) {
     // logical [stored_cols, stored_rows]: the transpose of the stored rows
     s = ensure_buf(p, out, elems * 4);
     if (s != MGB_OK) {
-      free_buf(stored);
+      free_buf(p, stored);
       return s;
     }
     e = launch_transpose(static_cast<const float *>(stored.ptr), w.stored_rows, w.stored_cols,
                          static_cast<float *>(out.ptr), p->stream);
-    cudaStreamSynchronize(p->stream);
-    free_buf(stored);
+    free_buf(p, stored);
     if (e != cudaSuccess) return cuda_fail(e, "transpose launch");
   }
   p->materializations++;
@@ -295,7 +302,7 @@ mgb_status run_matmul(mgb_provider *p, const std::string &kernel, const mgb_kern
                     plain_out(static_cast<float *>(product.ptr), n), nullptr, 0, p->workspace.ptr,
                     p->workspace.bytes, p->dev_err, kernel_pref, p->stream);
     if (s != MGB_OK) {
-      free_buf(product);
+      free_buf(p, product);
       return s;
     }
     out_shape = {m, n};
@@ -312,7 +319,7 @@ mgb_status run_matmul(mgb_provider *p, const std::string &kernel, const mgb_kern
     cudaError_t e = launch_input_major(w.format, w.buf.ptr, w.stored_rows, w.stored_cols, act, m,
                                        static_cast<float *>(product.ptr), p->stream);
     if (e != cudaSuccess) {
-      free_buf(product);
+      free_buf(p, product);
       return cuda_fail(e, "input-major launch");
     }
     out_shape = {m, n};
@@ -327,7 +334,7 @@ mgb_status run_matmul(mgb_provider *p, const std::string &kernel, const mgb_kern
     const uint64_t m = attrs.transpose_a ? a.cols : a.rows, k = attrs.transpose_a ? a.rows : a.cols;
     const uint64_t k2 = attrs.transpose_b ? b.cols : b.rows, n = attrs.transpose_b ? b.rows : b.cols;
     if (k != k2) {
-      free_buf(b.owned);
+      free_buf(p, b.owned);
       return fail(MGB_EXECUTION_FAILED, "matmul inner dimension mismatch: %llu vs %llu",
                   (unsigned long long)k, (unsigned long long)k2);
     }
@@ -339,22 +346,19 @@ mgb_status run_matmul(mgb_provider *p, const std::string &kernel, const mgb_kern
       if (e != cudaSuccess) s = cuda_fail(e, "matmul launch");
     }
     if (b.owned.ptr) {
-      cudaStreamSynchronize(p->stream);
-      free_buf(b.owned);
+      free_buf(p, b.owned);
     }
     if (s != MGB_OK) {
-      free_buf(product);
+      free_buf(p, product);
       return s;
     }
     out_shape = {m, n};
   }
   if (a.owned.ptr) {
-    cudaStreamSynchronize(p->stream);
-    free_buf(a.owned);
+    free_buf(p, a.owned);
   }
   if (rounded.ptr) {
-    cudaStreamSynchronize(p->stream);
-    free_buf(rounded);
+    free_buf(p, rounded);
   }
 
   // matmul-bias: add(product, bias); matmul-residual: add(residual, product)
@@ -362,7 +366,7 @@ mgb_status run_matmul(mgb_provider *p, const std::string &kernel, const mgb_kern
     Operand c;
     s = input_f32(p, n_inputs > 2 ? inputs[2] : nullptr, 2, c);
     if (s != MGB_OK) {
-      free_buf(product);
+      free_buf(p, product);
       return s;
     }
     const uint64_t len = out_shape[0] * out_shape[1], cols = out_shape[1];
@@ -372,24 +376,23 @@ mgb_status run_matmul(mgb_provider *p, const std::string &kernel, const mgb_kern
     const bool row = c.shape == std::vector<uint64_t>{cols} ||
                      c.shape == std::vector<uint64_t>{1, cols};
     if (kernel == "matmul-bias" && !same && !row) {
-      free_buf(product);
+      free_buf(p, product);
       return fail(MGB_EXECUTION_FAILED,
                   "add expects b to match a's shape %s or broadcast as [%llu]/[1, %llu], got %s",
                   shape_str(out_shape).c_str(), (unsigned long long)cols,
                   (unsigned long long)cols, shape_str(c.shape).c_str());
     }
     if (kernel == "matmul-residual" && !same) {
-      free_buf(product);
+      free_buf(p, product);
       return fail(MGB_EXECUTION_FAILED, "shape mismatch: %s vs %s", shape_str(c.shape).c_str(),
                   shape_str(out_shape).c_str());
     }
     cudaError_t e = launch_add(static_cast<float *>(product.ptr), len, c.ptr, clen, cols, p->stream);
     if (c.owned.ptr) {
-      cudaStreamSynchronize(p->stream);
-      free_buf(c.owned);
+      free_buf(p, c.owned);
     }
     if (e != cudaSuccess) {
-      free_buf(product);
+      free_buf(p, product);
       return cuda_fail(e, "epilogue launch");
     }
   }
@@ -464,9 +467,24 @@ mgb_status mgb_provider_create(const mgb_settings *settings, mgb_provider **out)
   p->settings = st;
   p->sms = device_sms(st.device);
   e = cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = st.device;
+    e = cudaMemPoolCreate(&p->pool, &props);
+  }
+  if (e == cudaSuccess) {
+    // freed memory stays in the pool until an allocation needs it elsewhere
+    uint64_t keep = UINT64_MAX;
+    e = cudaMemPoolSetAttribute(p->pool, cudaMemPoolAttrReleaseThreshold, &keep);
+  }
   if (e == cudaSuccess) e = cudaMalloc(&p->dev_err, sizeof(int));
   if (e == cudaSuccess) e = cudaMemset(p->dev_err, 0, sizeof(int));
   if (e != cudaSuccess) {
+    if (p->dev_err) cudaFree(p->dev_err);
+    if (p->pool) cudaMemPoolDestroy(p->pool);
+    if (p->stream) cudaStreamDestroy(p->stream);
     delete p;
     return cuda_fail(e, "provider set-up");
   }
@@ -493,9 +511,11 @@ void mgb_provider_destroy(mgb_provider *p) {
     if (kv.second.start) cudaEventDestroy(kv.second.start);
     if (kv.second.stop) cudaEventDestroy(kv.second.stop);
   }
-  for (auto &kv : p->storage) free_buf(kv.second.buf);
-  for (auto &kv : p->packed) free_buf(kv.second.buf);
-  free_buf(p->workspace);
+  for (auto &kv : p->storage) free_buf(p, kv.second.buf);
+  for (auto &kv : p->packed) free_buf(p, kv.second.buf);
+  free_buf(p, p->workspace);
+  if (p->stream) cudaStreamSynchronize(p->stream);
+  if (p->pool) cudaMemPoolDestroy(p->pool);
   if (p->dev_err) cudaFree(p->dev_err);
   if (p->stream) cudaStreamDestroy(p->stream);
   delete p;
@@ -577,7 +597,7 @@ mgb_status mgb_write_tensor(mgb_provider *p, const char *id, const uint64_t *sha
     cudaError_t e = cudaMemcpyAsync(buf.ptr, data, elems * 4, cudaMemcpyHostToDevice, p->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(p->stream);
     if (e != cudaSuccess) {
-      free_buf(buf);
+      free_buf(p, buf);
       return cuda_fail(e, "tensor upload");
     }
   }
@@ -608,15 +628,15 @@ mgb_status mgb_write_packed_weight(mgb_provider *p, const char *id, int32_t form
   if (s != MGB_OK) return s;
   s = ensure_buf(p, layout, len);
   if (s != MGB_OK) {
-    free_buf(staging);
+    free_buf(p, staging);
     return s;
   }
   cudaError_t e = cudaMemcpyAsync(staging.ptr, bytes, len, cudaMemcpyHostToDevice, p->stream);
   if (e == cudaSuccess) e = launch_repack(format, staging.ptr, stored_rows, stored_cols, layout.ptr, p->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(p->stream);
-  free_buf(staging);
+  free_buf(p, staging);
   if (e != cudaSuccess) {
-    free_buf(layout);
+    free_buf(p, layout);
     return cuda_fail(e, "packed weight upload");
   }
   forget_tensor(p, id);
@@ -669,8 +689,7 @@ mgb_status mgb_read_tensor(mgb_provider *p, const char *id, float *out, uint64_t
     }
   }
   if (owned.ptr) {
-    cudaStreamSynchronize(p->stream);
-    free_buf(owned);
+    free_buf(p, owned);
   }
   return s;
 }
@@ -739,10 +758,10 @@ mgb_status mgb_copy_tensor(mgb_provider *p, const char *from, const char *to) {
     cudaError_t e = cudaMemcpyAsync(copy.ptr, src.ptr, elems * 4, cudaMemcpyDeviceToDevice, p->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(p->stream);
     if (e != cudaSuccess) {
-      free_buf(copy);
+      free_buf(p, copy);
       return cuda_fail(e, "tensor copy");
     }
-    if (src.owned.ptr) free_buf(src.owned);
+    if (src.owned.ptr) free_buf(p, src.owned);
   }
   forget_packed(p, to);
   put_tensor(p, to, src.shape, copy);
@@ -755,6 +774,13 @@ mgb_status mgb_device_memory(mgb_provider *p, uint64_t *free_bytes, uint64_t *to
   size_t f = 0, t = 0;
   cudaError_t e = cudaMemGetInfo(&f, &t);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemGetInfo");
+  // memory the pool holds for reuse is free for this Provider's tensors
+  uint64_t reserved = 0, used = 0;
+  if (p->pool &&
+      cudaMemPoolGetAttribute(p->pool, cudaMemPoolAttrReservedMemCurrent, &reserved) == cudaSuccess &&
+      cudaMemPoolGetAttribute(p->pool, cudaMemPoolAttrUsedMemCurrent, &used) == cudaSuccess &&
+      reserved > used)
+    f += reserved - used;
   *free_bytes = f;
   *total_bytes = t;
   return MGB_OK;
