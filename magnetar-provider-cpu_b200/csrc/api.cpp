@@ -35,21 +35,34 @@ mgb_status cuda_fail(cudaError_t e, const char *what) {
 void clear_error() { g_last_error.clear(); }
 
 bool format_supported(int32_t format) {
-  return format == MGB_FORMAT_Q8_0 || format == MGB_FORMAT_Q4_K ||
+  return format == MGB_FORMAT_Q8_0 || format == MGB_FORMAT_Q4_K || format == MGB_FORMAT_Q6_K ||
          format == MGB_FORMAT_IQ4_NL || format == MGB_FORMAT_Q4_0;
+}
+
+uint64_t format_block_elements(int32_t format) {
+  return format == MGB_FORMAT_Q4_K || format == MGB_FORMAT_Q6_K ? 256 : 32;
 }
 
 uint64_t ggml_bytes(int32_t format, uint64_t rows, uint64_t cols) {
   if (!format_supported(format)) return 0;
-  const uint64_t be = format == MGB_FORMAT_Q4_K ? 256 : 32;
-  const uint64_t bb = format == MGB_FORMAT_Q4_K ? 144 : (format == MGB_FORMAT_Q8_0 ? 34 : 18);
-  return rows * (cols / be) * bb;
+  const uint64_t bb = format == MGB_FORMAT_Q4_K   ? 144
+                      : format == MGB_FORMAT_Q6_K ? 210
+                      : format == MGB_FORMAT_Q8_0 ? 34
+                                                  : 18;
+  return rows * (cols / format_block_elements(format)) * bb;
+}
+
+uint64_t device_bytes(int32_t format, uint64_t rows, uint64_t cols) {
+  // the ggml byte count, except Q6_K's 32-byte (not 18-byte) scale header per
+  // 256 values
+  if (format == MGB_FORMAT_Q6_K) return rows * (cols / 256) * 224;
+  return ggml_bytes(format, rows, cols);
 }
 
 mgb_status check_packed_shape(int32_t format, uint64_t rows, uint64_t cols) {
   if (!format_supported(format))
     return fail(MGB_DECLINED, "packed format %d is not executed by this Provider", format);
-  const uint64_t be = format == MGB_FORMAT_Q4_K ? 256 : 32;
+  const uint64_t be = format_block_elements(format);
   if (cols == 0 || cols % be)
     return fail(MGB_INVALID_ARGUMENT, "stored columns %llu are not a multiple of the block size %llu",
                 (unsigned long long)cols, (unsigned long long)be);
@@ -122,7 +135,7 @@ mgb_status validate_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t 
                             uint64_t m, float *y) {
   if (!format_supported(format))
     return fail(MGB_UNSUPPORTED, "packed format %d is not executed by this Provider", format);
-  if (k == 0 || k % 32 || (format == MGB_FORMAT_Q4_K && k % 256))
+  if (k == 0 || k % format_block_elements(format))
     return fail(MGB_EXECUTION_FAILED,
                 "packed matmul: activations have %llu columns, not a whole number of blocks",
                 (unsigned long long)k);
@@ -165,7 +178,7 @@ const char *mgb_status_name(int32_t status) {
 int32_t mgb_abi_version(void) { return MGB_ABI_VERSION; }
 
 uint64_t mgb_packed_bytes(int32_t format, uint64_t stored_rows, uint64_t stored_cols) {
-  return ggml_bytes(format, stored_rows, stored_cols);
+  return device_bytes(format, stored_rows, stored_cols);
 }
 
 mgb_status mgb_repack(int32_t format, const void *ggml_blocks, uint64_t stored_rows,

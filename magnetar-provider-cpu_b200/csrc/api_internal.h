@@ -15,7 +15,10 @@ mgb_status cuda_fail(cudaError_t e, const char *what);
 void clear_error();
 
 bool format_supported(int32_t format);
+uint64_t format_block_elements(int32_t format);
 uint64_t ggml_bytes(int32_t format, uint64_t rows, uint64_t cols);
+// bytes of the device layout (quant plane + scale plane)
+uint64_t device_bytes(int32_t format, uint64_t rows, uint64_t cols);
 mgb_status check_packed_shape(int32_t format, uint64_t rows, uint64_t cols);
 int *device_error_flag(int device);
 

@@ -14,28 +14,32 @@
 namespace mgb {
 
 // Format codes: the reference's `FORMATS` order (src/native/quant.rs:71-87).
-enum Format : int { Q8_0 = 0, Q4_K = 1, IQ4_NL = 5, Q4_0 = 13 };
+enum Format : int { Q8_0 = 0, Q4_K = 1, Q6_K = 2, IQ4_NL = 5, Q4_0 = 13 };
 
 constexpr int RUN = 32;  // values per run (src/native/quant.rs:19)
 
 __host__ __device__ inline bool supported(int f) {
-  return f == Q8_0 || f == Q4_K || f == IQ4_NL || f == Q4_0;
+  return f == Q8_0 || f == Q4_K || f == Q6_K || f == IQ4_NL || f == Q4_0;
 }
-__host__ __device__ inline int block_elements(int f) { return f == Q4_K ? 256 : 32; }
+__host__ __device__ inline int block_elements(int f) { return f == Q4_K || f == Q6_K ? 256 : 32; }
 __host__ __device__ inline int block_bytes(int f) {
-  return f == Q4_K ? 144 : (f == Q8_0 ? 34 : 18);
+  return f == Q4_K ? 144 : f == Q6_K ? 210 : (f == Q8_0 ? 34 : 18);
 }
 
 // Device layout of an [n stored rows x k stored cols] packed matrix: the
 // quant plane (n rows of `qs_row` bytes: one 16-byte run of nibble pairs for
-// the 4-bit formats, 32 bytes per run for Q8_0) followed by the scale plane
-// (n rows of k/16 bytes: Q4_K's 16-byte d/dmin/scales header per 256 values,
-// or one f16 scale per 32 values).  The byte count equals the ggml blocks'.
+// the 4-bit formats, 32 bytes per run for Q8_0; Q6_K: 48 bytes per 64 values,
+// the two runs' low-nibble pairs then their high 2-bit fields, 8 bytes per
+// run) followed by the scale plane (n rows of `sc_row` bytes: Q4_K's 16-byte
+// d/dmin/scales header per 256 values; Q6_K's 32-byte header per 256 values,
+// its 16 int8 scales then d; or one f16 scale per 32 values).  The byte count
+// equals the ggml blocks' except Q6_K's (224 bytes per 256 values against
+// 210: the header is padded so every copy stays 16-byte aligned).
 struct Layout {
   uint64_t n, k, qs_row, sc_row, qs_bytes, total;
   __host__ __device__ Layout(int f, uint64_t n_, uint64_t k_) : n(n_), k(k_) {
-    qs_row = f == Q8_0 ? k : k / 2;
-    sc_row = k / 16;
+    qs_row = f == Q8_0 ? k : f == Q6_K ? k / 4 * 3 : k / 2;
+    sc_row = f == Q6_K ? k / 8 : k / 16;
     qs_bytes = n * qs_row;
     total = qs_bytes + n * sc_row;
   }
@@ -78,6 +82,23 @@ __device__ __forceinline__ void q4k_scale_min(int j, uint32_t h1, uint32_t h2, u
   const uint64_t b = ((uint64_t)h3 << 32) | h2;
   sc = (uint32_t)(a >> (6 * j)) & 63;
   m = (uint32_t)(b >> (16 + 6 * j)) & 63;
+}
+
+// Q6_K: the quant plane offsets of run u's nibble pairs (16 bytes) and high
+// 2-bit fields (8 bytes) within its row.
+__host__ __device__ inline uint64_t q6k_nib_offset(uint64_t u) { return (u / 2) * 48 + (u % 2) * 16; }
+__host__ __device__ inline uint64_t q6k_high_offset(uint64_t u) { return (u / 2) * 48 + 32 + (u % 2) * 8; }
+
+// Q6_K: the 6-bit codes (q + 32) of the 8 values of nibble word wd of a run,
+// in the nibble-pair order: ev = values 8 wd + 0, 2, 4, 6, od = values
+// 8 wd + 1, 3, 5, 7, one per byte.  hw is the run's high word for wd's half
+// (wd / 2): its byte j holds the high bits of values 16 a + 8 b + 2 j (bits
+// 4 b, 4 b + 1) and 16 a + 8 b + 2 j + 1 (bits 4 b + 2, 4 b + 3), b = wd % 2.
+__device__ __forceinline__ void q6k_codes(uint32_t nib_word, uint32_t hw, int wd, uint32_t &ev,
+                                          uint32_t &od) {
+  const int b = wd & 1;
+  ev = (nib_word & 0x0F0F0F0Fu) | (((hw >> (4 * b)) & 0x03030303u) << 4);
+  od = ((nib_word >> 4) & 0x0F0F0F0Fu) | (((hw >> (4 * b + 2)) & 0x03030303u) << 4);
 }
 
 // ---- device error flag -------------------------------------------------------------

@@ -55,7 +55,8 @@ struct GemmParams {
   int astages;          // activation-tile ring
   int bstages;          // bf16 W-tile ring
   int pstages;          // packed-W ring
-  int qbytes;           // packed quant bytes per weight row per K step (32 or 64)
+  int qbytes;           // packed quant bytes per weight row per K step (32, 48 or 64)
+  int wsw;              // scale-plane bytes per weight row per 256 values (16 or 32)
   uint32_t a_bytes;     // per activation stage
   uint32_t b_bytes;     // per W-tile stage
   uint32_t wq_bytes;    // per packed stage
@@ -182,6 +183,31 @@ __device__ __forceinline__ void dq_nib_linear(const uint4 &qs, float s, float mn
   }
 }
 
+// Q6_K: 6-bit codes c (nibble pairs plus the high 2-bit fields of the two
+// halves, hw[0] and hw[1]) with value = s_h * (c - 32), s_h the scale of the
+// value's 16-value half: the nibble formula with the code in the mantissa.
+__device__ __forceinline__ void dq_q6k(const uint4 &qs, const uint2 &hw, float s0, float s1,
+                                       uint4 out[4]) {
+  const uint32_t words[4] = {qs.x, qs.y, qs.z, qs.w};
+#pragma unroll
+  for (int wd = 0; wd < 4; ++wd) {
+    const float s = wd < 2 ? s0 : s1;
+    const float a = 256.f * s, c = -(128.f * s + 32.f * s);
+    const float2 a2 = make_float2(a, a), c2 = make_float2(c, c);
+    uint32_t ev, od;
+    q6k_codes(words[wd], wd < 2 ? hw.x : hw.y, wd, ev, od);
+    uint32_t p[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float f0 = __uint_as_float(__byte_perm(ev, 0x3F000000u, 0x7054u | ((uint32_t)i << 8)));
+      const float f1 = __uint_as_float(__byte_perm(od, 0x3F000000u, 0x7054u | ((uint32_t)i << 8)));
+      const float2 v = __ffma2_rn(make_float2(f0, f1), a2, c2);
+      p[i] = pack_bf16(v.x, v.y);
+    }
+    out[wd] = make_uint4(p[0], p[1], p[2], p[3]);
+  }
+}
+
 // Biased bytes (b + 128, byte order = value order) times d.
 __device__ __forceinline__ void dq_bytes(const uint32_t u[8], float d, uint4 out[4]) {
 #pragma unroll
@@ -216,7 +242,14 @@ template <int FMT>
 __device__ __forceinline__ void dequant_run(const uint8_t *wq_row, const uint8_t *ws_row, int kt,
                                             int j, const uint32_t lut[4], uint4 out[4]) {
   const int sub = (kt & 3) * 2 + j;  // run index within the 8 runs the scale box covers
-  if (FMT == Q4_K) {
+  if (FMT == Q6_K) {
+    // this K step's 48 bytes: the two runs' nibble pairs, then their high words
+    const uint4 qs = *reinterpret_cast<const uint4 *>(wq_row + j * 16);
+    const uint2 hw = *reinterpret_cast<const uint2 *>(wq_row + 32 + j * 8);
+    const float d = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(ws_row + 16));
+    const uint16_t sp = *reinterpret_cast<const uint16_t *>(ws_row + 2 * sub);
+    dq_q6k(qs, hw, d * (float)(int8_t)(sp & 0xFF), d * (float)(int8_t)(sp >> 8), out);
+  } else if (FMT == Q4_K) {
     const uint4 qs = *reinterpret_cast<const uint4 *>(wq_row + j * 16);
     const uint4 h = *reinterpret_cast<const uint4 *>(ws_row);
     const float d = f16_bits_to_f32(h.x), dmin = f16_bits_to_f32(h.x >> 16);
@@ -438,7 +471,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint8_t *st = pk0 + (size_t)s * p.pstage_bytes;
         mbar_arrive_expect_tx(&p_full[s], p.ptx_bytes);
         tma_load_2d(st, &map_wq, kt * p.qbytes, n0, &p_full[s]);
-        tma_load_2d(st + p.wq_bytes, &map_ws, (kt / 4) * 16, n0, &p_full[s]);
+        tma_load_2d(st + p.wq_bytes, &map_ws, (kt / 4) * p.wsw, n0, &p_full[s]);
         issued = kt + 1;
       }
       for (int kt = (issued > SP ? issued - SP : 0); kt < issued; ++kt)
@@ -499,7 +532,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int it = t; it < items; it += DQ_THREADS) {
         const int row = it >> 1, j = it & 1;
         uint4 out[4];
-        dequant_run<FMT>(wq + row * p.qbytes, ws + row * 16, kt, j, lut, out);
+        dequant_run<FMT>(wq + row * p.qbytes, ws + row * p.wsw, kt, j, lut, out);
         uint8_t *dst_row = bt + row * 128;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -661,14 +694,15 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
   p.m = (int)m;
   p.n = (int)n;
   p.k = (int)k;
-  p.qbytes = fmt == Q8_0 ? 64 : 32;
+  p.qbytes = fmt == Q8_0 ? 64 : fmt == Q6_K ? 48 : 32;
+  p.wsw = fmt == Q6_K ? 32 : 16;
   p.bn = t.bn;
   p.a_bytes = 16384u * t.subs;
   p.b_bytes = (uint32_t)ceil_div((uint64_t)t.bn * 128u, 1024) * 1024;
   p.wq_bytes = (uint32_t)ceil_div((uint64_t)t.bn * p.qbytes, 1024) * 1024;
-  p.ws_bytes = (uint32_t)ceil_div((uint64_t)t.bn * 16, 1024) * 1024;
+  p.ws_bytes = (uint32_t)ceil_div((uint64_t)t.bn * p.wsw, 1024) * 1024;
   p.pstage_bytes = p.wq_bytes + p.ws_bytes;
-  p.ptx_bytes = (uint32_t)t.bn * (uint32_t)p.qbytes + (uint32_t)t.bn * 16u;
+  p.ptx_bytes = (uint32_t)t.bn * (uint32_t)(p.qbytes + p.wsw);
   const dim3 grid((unsigned)ceil_div(n, (uint64_t)t.bn), (unsigned)ceil_div(m, 128ull * t.subs));
   // Narrow tiles (few weight rows per CTA) run their K loop faster with more
   // operand stages in flight: as many as fit (up to 6), then packed stages (up
@@ -696,8 +730,8 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
       !make_map_2d(&map_wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, L.qs_row, n, L.qs_row,
                    (uint32_t)p.qbytes, (uint32_t)t.bn, CU_TENSOR_MAP_SWIZZLE_NONE) ||
       !make_map_2d(&map_ws, CU_TENSOR_MAP_DATA_TYPE_UINT8,
-                   static_cast<const uint8_t *>(w) + L.qs_bytes, L.sc_row, n, L.sc_row, 16,
-                   (uint32_t)t.bn, CU_TENSOR_MAP_SWIZZLE_NONE))
+                   static_cast<const uint8_t *>(w) + L.qs_bytes, L.sc_row, n, L.sc_row,
+                   (uint32_t)p.wsw, (uint32_t)t.bn, CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
 
   const size_t smem = (size_t)sa * ab + (size_t)sp * p.pstage_bytes + 1024 + 512;
@@ -716,6 +750,7 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
     break;
   switch (fmt) {
     MGB_GEMM_FMT(Q4_K)
+    MGB_GEMM_FMT(Q6_K)
     MGB_GEMM_FMT(Q8_0)
     MGB_GEMM_FMT(IQ4_NL)
     MGB_GEMM_FMT(Q4_0)

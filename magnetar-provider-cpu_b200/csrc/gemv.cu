@@ -85,6 +85,7 @@ __device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c) {
 // otherwise).
 struct XRun {
   float dx, sum;
+  float hs[2];  // sums of values 0..15 and 16..31 (Q6_K: one scale per half)
   uint32_t hi[8], lo[8];
 };
 
@@ -105,6 +106,13 @@ __device__ __forceinline__ void pack_run(const float (&v)[32], bool pair_order, 
     for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
   const float amax = mx[0];
   r.sum = s;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 16 * h; i < 16 * h + 16; i += 4) t += (v[i] + v[i + 1]) + (v[i + 2] + v[i + 3]);
+    r.hs[h] = t;
+  }
   r.dx = amax / 32767.f;
   const float inv = amax > 0.f ? 32767.f / amax : 0.f;
   uint32_t b[32];
@@ -183,7 +191,29 @@ template <int FMT, int MR>
 __device__ __forceinline__ void run_partials(const uint4 &qa, const uint4 &qb, const uint4 &hd,
                                              uint32_t dh, int j, const XRun (&x)[MR],
                                              const uint32_t lut[4], float (&part)[MR]) {
-  if (FMT == Q4_K) {
+  if (FMT == Q6_K) {
+    // qa: nibble pairs; qb.x, qb.y: the two high words; hd: the 16 int8
+    // scales of the super-block; dh: d
+    const float d = f16_bits_to_f32(dh);
+    const uint32_t sw = (j < 2 ? hd.x : j < 4 ? hd.y : j < 6 ? hd.z : hd.w) >> (16 * (j & 1));
+    const float s0 = d * (float)(int8_t)(sw & 0xFF), s1 = d * (float)(int8_t)((sw >> 8) & 0xFF);
+    const uint32_t words[4] = {qa.x, qa.y, qa.z, qa.w};
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      int sh[2] = {0, 0}, sl[2] = {0, 0};
+#pragma unroll
+      for (int wd = 0; wd < 4; ++wd) {
+        uint32_t ev, od;
+        q6k_codes(words[wd], wd < 2 ? qb.x : qb.y, wd, ev, od);
+        sh[wd >> 1] = dp4a_us(ev, x[m].hi[2 * wd], sh[wd >> 1]);
+        sh[wd >> 1] = dp4a_us(od, x[m].hi[2 * wd + 1], sh[wd >> 1]);
+        sl[wd >> 1] = dp4a_uu(ev, x[m].lo[2 * wd], sl[wd >> 1]);
+        sl[wd >> 1] = dp4a_uu(od, x[m].lo[2 * wd + 1], sl[wd >> 1]);
+      }
+      part[m] = ((s0 * x[m].dx) * (float)(sh[0] * 256 + sl[0]) - (32.f * s0) * x[m].hs[0]) +
+                ((s1 * x[m].dx) * (float)(sh[1] * 256 + sl[1]) - (32.f * s1) * x[m].hs[1]);
+    }
+  } else if (FMT == Q4_K) {
     const float d = f16_bits_to_f32(hd.x), dmin = f16_bits_to_f32(hd.x >> 16);
     uint32_t sc, mn;
     q4k_scale_min(j, hd.y, hd.z, hd.w, sc, mn);
@@ -216,9 +246,16 @@ __device__ __forceinline__ void run_partials(const uint4 &qa, const uint4 &qb, c
 // of its integer dot product and the multiplier of its activation sum, so that
 // the run contributes (s * dx) * dot - m * sum.  Q4_K: s = d * scale_j,
 // m = dmin * min_j; Q4_0: s = d, m = 8 d (q - 8); Q8_0, IQ4_NL: s = d, m = 0.
+// Q6_K: the two halves' scales d * sc (each half contributes
+// (s * dx) * dot - 32 s * sum over its 16 values).
 template <int FMT>
 __device__ __forceinline__ float2 decode_run_scale(const uint8_t *srow, int uu) {
-  if (FMT == Q4_K) {
+  if (FMT == Q6_K) {  // the scales of the run's two halves (q - 32: no separate min)
+    const uint8_t *hd = srow + (uu >> 3) * 32;
+    const float d = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(hd + 16));
+    const uint16_t sp = *reinterpret_cast<const uint16_t *>(hd + 2 * (uu & 7));
+    return make_float2(d * (float)(int8_t)(sp & 0xFF), d * (float)(int8_t)(sp >> 8));
+  } else if (FMT == Q4_K) {
     const uint4 hd = *reinterpret_cast<const uint4 *>(srow + (uu >> 3) * 16);
     const float d = f16_bits_to_f32(hd.x), dmin = f16_bits_to_f32(hd.x >> 16);
     uint32_t sc, mn;
@@ -246,6 +283,46 @@ __device__ __forceinline__ void rows_partials(const uint8_t *q, size_t q_stride,
     sm[i] = dec[(size_t)i * dec_stride];
 #pragma unroll
     for (int m = 0; m < MR; ++m) sh[i][m] = sl[i][m] = 0;
+  }
+  if (FMT == Q6_K) {
+    uint4 qa[RPT];
+    uint2 qh[RPT];
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+      qa[i] = *reinterpret_cast<const uint4 *>(q + (size_t)i * q_stride + q6k_nib_offset(uu));
+      qh[i] = *reinterpret_cast<const uint2 *>(q + (size_t)i * q_stride + q6k_high_offset(uu));
+    }
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {  // the run's halves: one scale each
+#pragma unroll
+      for (int i = 0; i < RPT; ++i)
+#pragma unroll
+        for (int m = 0; m < MR; ++m) sh[i][m] = sl[i][m] = 0;
+#pragma unroll
+      for (int wd = 2 * hf; wd < 2 * hf + 2; ++wd)
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) {
+          const uint32_t v = wd == 0 ? qa[i].x : wd == 1 ? qa[i].y : wd == 2 ? qa[i].z : qa[i].w;
+          uint32_t ev, od;
+          q6k_codes(v, hf == 0 ? qh[i].x : qh[i].y, wd, ev, od);
+#pragma unroll
+          for (int m = 0; m < MR; ++m) {
+            sh[i][m] = dp4a_us(ev, x[m].hi[2 * wd], sh[i][m]);
+            sh[i][m] = dp4a_us(od, x[m].hi[2 * wd + 1], sh[i][m]);
+            sl[i][m] = dp4a_uu(ev, x[m].lo[2 * wd], sl[i][m]);
+            sl[i][m] = dp4a_uu(od, x[m].lo[2 * wd + 1], sl[i][m]);
+          }
+        }
+#pragma unroll
+      for (int i = 0; i < RPT; ++i)
+#pragma unroll
+        for (int m = 0; m < MR; ++m) {
+          const float sc = hf == 0 ? sm[i].x : sm[i].y;
+          const float c = (sc * x[m].dx) * (float)(sh[i][m] * 256 + sl[i][m]) - (32.f * sc) * x[m].hs[hf];
+          part[i * MR + m] = hf == 0 ? c : part[i * MR + m] + c;
+        }
+    }
+    return;
   }
   if (FMT == Q8_0) {
 #pragma unroll
@@ -314,7 +391,7 @@ __device__ __forceinline__ void rows_partials(const uint8_t *q, size_t q_stride,
 template <int FMT, int MR>
 __device__ __forceinline__ void load_x(const float *__restrict__ x, int k, int u, bool active,
                                        XRun (&xr)[MR]) {
-  constexpr bool pair = FMT == Q4_K || FMT == Q4_0;
+  constexpr bool pair = FMT == Q4_K || FMT == Q4_0 || FMT == Q6_K;
 #pragma unroll
   for (int m = 0; m < MR; ++m) {
     float v[32];
@@ -583,11 +660,18 @@ __global__ void __launch_bounds__(MAXT, 1)
         if (FMT == Q8_0) {
           qa = ld_stream_v4(qrow + (size_t)u * 32);
           qb = ld_stream_v4(qrow + (size_t)u * 32 + 16);
+        } else if (FMT == Q6_K) {
+          qa = ld_stream_v4(qrow + q6k_nib_offset((uint64_t)u));
+          const uint2 h2 = __ldg(reinterpret_cast<const uint2 *>(qrow + q6k_high_offset((uint64_t)u)));
+          qb = make_uint4(h2.x, h2.y, 0, 0);
         } else {
           qa = ld_stream_v4(qrow + (size_t)u * 16);
         }
         if (FMT == Q4_K) hd = __ldg(reinterpret_cast<const uint4 *>(srow + (size_t)(u >> 3) * 16));
-        else dh = ld_nc_u16(srow + (size_t)u * 2);
+        else if (FMT == Q6_K) {
+          hd = __ldg(reinterpret_cast<const uint4 *>(srow + (size_t)(u >> 3) * 32));
+          dh = ld_nc_u16(srow + (size_t)(u >> 3) * 32 + 16);
+        } else dh = ld_nc_u16(srow + (size_t)u * 2);
         float pm[MR];
         run_partials<FMT, MR>(qa, qb, hd, dh, u & 7, xr, lut, pm);
 #pragma unroll
@@ -775,6 +859,7 @@ cudaError_t launch_gemv(int fmt, const void *w, uint64_t n, uint64_t k, const fl
                   : launch_fmt<F, 2>(w, N, K, x, out, addend, addend_mode, err, sms, stream);
   switch (fmt) {
     MGB_GEMV_CASE(Q4_K)
+    MGB_GEMV_CASE(Q6_K)
     MGB_GEMV_CASE(Q8_0)
     MGB_GEMV_CASE(IQ4_NL)
     MGB_GEMV_CASE(Q4_0)

@@ -2,7 +2,7 @@
 // and the bit-exact dequantisation of that layout back to f32.
 //
 // Dequantised values equal the reference `decode` + `dequantize_row`
-// (src/native/quant.rs:100-195, :1700-1711) bit for bit: every product and
+// (src/native/quant.rs:100-195, Q6_K :136-149, :1700-1711) bit for bit: every product and
 // difference is rounded on its own (__fmul_rn / __fsub_rn, never an FMA), as
 // Rust evaluates `scale * q - min` with `scale = d * sc`, `min = dmin * m`.
 #include "common.cuh"
@@ -61,6 +61,36 @@ __global__ void repack_kernel(int fmt, const uint8_t *__restrict__ src, uint64_t
         for (int i = 0; i < 8; ++i) sc[b * 16 + 4 + i] = (uint8_t)(lo >> (8 * i));
         for (int i = 0; i < 4; ++i) sc[b * 16 + 12 + i] = (uint8_t)(hi >> (8 * i));
       }
+    } else if (fmt == Q6_K) {
+      // run r = 4 h + g of the block: low nibbles in the 32 bytes at
+      // 64 h + 32 (g % 2) (shift 4 (g / 2)), high 2 bits in the 32 bytes at
+      // 128 + 32 h (shift 2 g); codes c = q + 32 in 0..63
+      const uint64_t b = u / 8;
+      const int r = (int)(u % 8), h = r / 4, g = r % 4;
+      const uint8_t *blk = row_src + b * 210;
+      const uint8_t *low = blk + 64 * h + 32 * (g % 2), *high = blk + 128 + 32 * h;
+      uint8_t c[32];
+      for (int i = 0; i < 32; ++i)
+        c[i] = (uint8_t)(((low[i] >> (4 * (g / 2))) & 0xF) | (((high[i] >> (2 * g)) & 3) << 4));
+      uint8_t *nib = qs + q6k_nib_offset(u);
+      for (int i = 0; i < 16; ++i) nib[i] = (uint8_t)((c[2 * i] & 0xF) | ((c[2 * i + 1] & 0xF) << 4));
+      uint32_t hw[2] = {0, 0};
+      for (int a = 0; a < 2; ++a)
+        for (int bb = 0; bb < 2; ++bb)
+          for (int j = 0; j < 4; ++j) {
+            const int v = 16 * a + 8 * bb + 2 * j;
+            hw[a] |= (uint32_t)(c[v] >> 4) << (8 * j + 4 * bb);
+            hw[a] |= (uint32_t)(c[v + 1] >> 4) << (8 * j + 4 * bb + 2);
+          }
+      *reinterpret_cast<uint2 *>(qs + q6k_high_offset(u)) = make_uint2(hw[0], hw[1]);
+      if (r == 0) {
+        // header: the 16 int8 scales (scale 2 r + p covers values 16 p .. of
+        // run r), then d, then zeros
+        for (int i = 0; i < 16; ++i) sc[b * 32 + i] = blk[192 + i];
+        sc[b * 32 + 16] = blk[208];
+        sc[b * 32 + 17] = blk[209];
+        for (int i = 18; i < 32; ++i) sc[b * 32 + i] = 0;
+      }
     } else if (fmt == Q8_0) {
       const uint8_t *blk = row_src + u * 34;
       for (int i = 0; i < 32; ++i) qs[u * 32 + i] = blk[2 + i];
@@ -80,18 +110,41 @@ __global__ void repack_kernel(int fmt, const uint8_t *__restrict__ src, uint64_t
   }
 }
 
-// The 32 quant values of run `u` of `row` (as ints) and the run's scale and min.
+// The 32 quant values of run `u` of `row` (as ints) and the run's scale and
+// min of each 16-value half (the same for both halves except Q6_K's scales).
 __device__ __forceinline__ void decode_run(int fmt, const uint8_t *__restrict__ w, const Layout &L,
-                                           uint64_t row, uint64_t u, int q[32], float &scale,
-                                           float &min) {
+                                           uint64_t row, uint64_t u, int q[32], float scale[2],
+                                           float min[2]) {
   const uint8_t *sc = w + L.qs_bytes + row * L.sc_row;
+  if (fmt == Q6_K) {
+    const uint8_t *qrow = w + row * L.qs_row;
+    const uint4 v = *reinterpret_cast<const uint4 *>(qrow + q6k_nib_offset(u));
+    const uint2 hh = *reinterpret_cast<const uint2 *>(qrow + q6k_high_offset(u));
+    const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+    for (int wd = 0; wd < 4; ++wd) {
+      uint32_t ev, od;
+      q6k_codes(words[wd], wd < 2 ? hh.x : hh.y, wd, ev, od);
+      for (int j = 0; j < 4; ++j) {
+        q[8 * wd + 2 * j] = (int)((ev >> (8 * j)) & 0xFF) - 32;
+        q[8 * wd + 2 * j + 1] = (int)((od >> (8 * j)) & 0xFF) - 32;
+      }
+    }
+    const uint8_t *hd = sc + (u / 8) * 32;
+    const float d = f16_bits_to_f32(hd[16] | (hd[17] << 8));
+    const int r = (int)(u % 8);
+    for (int p = 0; p < 2; ++p) {
+      scale[p] = __fmul_rn(d, (float)(int8_t)hd[2 * r + p]);
+      min[p] = 0.0f;
+    }
+    return;
+  }
   if (fmt == Q8_0) {
     const uint4 a = *reinterpret_cast<const uint4 *>(w + row * L.qs_row + u * 32);
     const uint4 b = *reinterpret_cast<const uint4 *>(w + row * L.qs_row + u * 32 + 16);
     const uint32_t words[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     for (int i = 0; i < 32; ++i) q[i] = (int)(int8_t)((words[i / 4] >> (8 * (i % 4))) & 0xff);
-    scale = f16_bits_to_f32(sc[u * 2] | (sc[u * 2 + 1] << 8));
-    min = 0.0f;
+    scale[0] = scale[1] = f16_bits_to_f32(sc[u * 2] | (sc[u * 2 + 1] << 8));
+    min[0] = min[1] = 0.0f;
     return;
   }
   const uint4 v = *reinterpret_cast<const uint4 *>(w + row * L.qs_row + u * 16);
@@ -105,11 +158,11 @@ __device__ __forceinline__ void decode_run(int fmt, const uint8_t *__restrict__ 
     const float d = f16_bits_to_f32(h.x), dmin = f16_bits_to_f32(h.x >> 16);
     uint32_t s, m;
     q4k_scale_min((int)(u % 8), h.y, h.z, h.w, s, m);
-    scale = __fmul_rn(d, (float)s);
-    min = __fmul_rn(dmin, (float)m);
+    scale[0] = scale[1] = __fmul_rn(d, (float)s);
+    min[0] = min[1] = __fmul_rn(dmin, (float)m);
   } else {
-    scale = f16_bits_to_f32(sc[u * 2] | (sc[u * 2 + 1] << 8));
-    min = 0.0f;
+    scale[0] = scale[1] = f16_bits_to_f32(sc[u * 2] | (sc[u * 2 + 1] << 8));
+    min[0] = min[1] = 0.0f;
   }
 }
 
@@ -121,12 +174,13 @@ __global__ void dequantize_kernel(int fmt, const uint8_t *__restrict__ w, uint64
        t += (uint64_t)gridDim.x * blockDim.x) {
     const uint64_t row = t / runs_per_row, u = t % runs_per_row;
     int q[32];
-    float scale, min;
+    float scale[2], min[2];
     decode_run(fmt, w, L, row, u, q, scale, min);
     float4 *o = reinterpret_cast<float4 *>(out + row * k + u * RUN);
     for (int i = 0; i < 8; ++i) {
       float v[4];
-      for (int e = 0; e < 4; ++e) v[e] = __fsub_rn(__fmul_rn(scale, (float)q[4 * i + e]), min);
+      for (int e = 0; e < 4; ++e)
+        v[e] = __fsub_rn(__fmul_rn(scale[i / 4], (float)q[4 * i + e]), min[i / 4]);
       o[i] = make_float4(v[0], v[1], v[2], v[3]);
     }
   }
@@ -151,9 +205,9 @@ __global__ void input_major_kernel(int fmt, const uint8_t *__restrict__ w, uint6
       const float a = x[r * k_rows + j];
       if (a == 0.0f) continue;
       int q[32];
-      float scale, min;
+      float scale[2], min[2];
       decode_run(fmt, w, L, j, u, q, scale, min);
-      const float v = __fsub_rn(__fmul_rn(scale, (float)q[i]), min);
+      const float v = __fsub_rn(__fmul_rn(scale[i / 16], (float)q[i]), min[i / 16]);
       acc = __fadd_rn(acc, __fmul_rn(a, v));
     }
     y[t] = acc;

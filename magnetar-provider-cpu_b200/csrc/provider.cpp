@@ -626,7 +626,7 @@ mgb_status mgb_write_packed_weight(mgb_provider *p, const char *id, int32_t form
   DevBuf staging, layout;
   s = ensure_buf(p, staging, len);
   if (s != MGB_OK) return s;
-  s = ensure_buf(p, layout, len);
+  s = ensure_buf(p, layout, device_bytes(format, stored_rows, stored_cols));
   if (s != MGB_OK) {
     free_buf(p, staging);
     return s;

@@ -28,8 +28,8 @@ KERNEL_NOT_FOUND, TIMEOUT, MEMORY_DENIED, UNKNOWN_HANDLE, NOT_FOUND = 5, 6, 7, 8
 INVALID_ARGUMENT, CUDA_ERROR, NCCL_ERROR, UNSUPPORTED = 10, 11, 12, 13
 
 Q8_0, Q4_K, Q6_K, IQ4_NL, Q4_0 = 0, 1, 2, 5, 13
-FORMATS = {"q8_0": Q8_0, "q4_k": Q4_K, "iq4_nl": IQ4_NL, "q4_0": Q4_0}
-BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), IQ4_NL: (32, 18), Q4_0: (32, 18)}
+FORMATS = {"q8_0": Q8_0, "q4_k": Q4_K, "q6_k": Q6_K, "iq4_nl": IQ4_NL, "q4_0": Q4_0}
+BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), IQ4_NL: (32, 18), Q4_0: (32, 18)}
 KERNEL_AUTO, KERNEL_GEMV, KERNEL_GEMM = 0, 1, 2
 MAX_RANK = 8
 

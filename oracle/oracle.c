@@ -14,13 +14,13 @@
 
 int orc_supported(int format) {
     return format == ORC_Q8_0 || format == ORC_Q4_K || format == ORC_IQ4_NL ||
-           format == ORC_Q4_0;
+           format == ORC_Q4_0 || format == ORC_Q6_K || format == ORC_Q5_K;
 }
 
 int orc_block_elements(int format) {
     switch (format) {
     case ORC_Q8_0: case ORC_IQ4_NL: case ORC_Q4_0: return 32;
-    case ORC_Q4_K: return 256;
+    case ORC_Q4_K: case ORC_Q6_K: case ORC_Q5_K: return 256;
     default: return 0;
     }
 }
@@ -29,6 +29,8 @@ int orc_block_bytes(int format) {
     switch (format) {
     case ORC_Q8_0: return 34;
     case ORC_Q4_K: return 144;
+    case ORC_Q6_K: return 210;
+    case ORC_Q5_K: return 176;
     case ORC_IQ4_NL: case ORC_Q4_0: return 18;
     default: return 0;
     }
@@ -83,7 +85,7 @@ const int8_t *orc_iq4nl_values(void) { return IQ4NL; }
 const int8_t *orc_q4_0_values(void) { return Q40; }
 
 /* ---- decode (src/native/quant.rs:100-280: Q8_0 :102-109, Q4_K :110-121,
- *      IQ4_NL / Q4_0 :180-195) ------------------------------------------------------- */
+ *      Q5_K :122-135, Q6_K :136-149, IQ4_NL / Q4_0 :180-195) --------------------------- */
 
 int orc_decode_run(int format, const uint8_t *block, int run, orc_run *out) {
     switch (format) {
@@ -104,6 +106,39 @@ int orc_decode_run(int format, const uint8_t *block, int run, orc_run *out) {
         for (int i = 0; i < ORC_RUN; i++) out->q[i] = (int8_t)((qs[i] >> shift) & 0xF);
         out->scale[0] = out->scale[1] = d * (float)sc;
         out->min[0] = out->min[1] = dmin * (float)m;
+        return 0;
+    }
+    case ORC_Q5_K: {
+        /* d, dmin; scales as Q4_K; run r's low nibbles in the 32 bytes at
+           48 + 32 (r / 2) (shift 4 (r % 2)), its fifth bits at bit r of the
+           32 bytes at 16 */
+        float d = half_at(block, 0);
+        float dmin = half_at(block, 2);
+        uint8_t sc, m;
+        orc_scale_min_k4(run, block + 4, &sc, &m);
+        int chunk = run / 2, shift = 4 * (run % 2);
+        const uint8_t *low = block + 48 + 32 * chunk, *high = block + 16;
+        for (int i = 0; i < ORC_RUN; i++)
+            out->q[i] = (int8_t)(((low[i] >> shift) & 0xF) | (((high[i] >> run) & 1) << 4));
+        out->scale[0] = out->scale[1] = d * (float)sc;
+        out->min[0] = out->min[1] = dmin * (float)m;
+        return 0;
+    }
+    case ORC_Q6_K: {
+        /* d at 208; run r = 4 h + g: low nibbles in the 32 bytes at
+           64 h + 32 (g % 2) (shift 4 (g / 2)), high 2 bits in the 32 bytes at
+           128 + 32 h (shift 2 g), q - 32; one int8 scale per 16 values at
+           192 + 8 h + 2 g + p; no min */
+        float d = half_at(block, 208);
+        int h = run / 4, g = run % 4;
+        const uint8_t *low = block + 64 * h + 32 * (g % 2), *high = block + 128 + 32 * h;
+        int ls = 4 * (g / 2), hs = 2 * g;
+        for (int i = 0; i < ORC_RUN; i++)
+            out->q[i] = (int8_t)((((low[i] >> ls) & 0xF) | (((high[i] >> hs) & 3) << 4)) - 32);
+        for (int p = 0; p < 2; p++) {
+            out->scale[p] = d * (float)(int8_t)block[192 + 8 * h + 2 * g + p];
+            out->min[p] = 0.0f;
+        }
         return 0;
     }
     case ORC_IQ4_NL:

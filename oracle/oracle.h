@@ -53,7 +53,7 @@ typedef struct orc_run {
     float min[2];
 } orc_run;
 
-/* 1 when the oracle decodes `format` (Q8_0, Q4_K, IQ4_NL, Q4_0), else 0. */
+/* 1 when the oracle decodes `format` (Q8_0, Q4_K, Q5_K, Q6_K, IQ4_NL, Q4_0), else 0. */
 int orc_supported(int format);
 /* Weights per block (32 or 256) and bytes per block; 0 for unknown formats. */
 int orc_block_elements(int format);

@@ -17,8 +17,9 @@ HERE = pathlib.Path(__file__).resolve().parent
 LIB_PATH = HERE / "_build" / "liboracle_mgb.so"
 BASELINE_PATH = HERE / "_build" / "libcpu_baseline_mgb.so"
 
-Q8_0, Q4_K, IQ4_NL, Q4_0 = 0, 1, 5, 13
-BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), IQ4_NL: (32, 18), Q4_0: (32, 18)}
+Q8_0, Q4_K, Q6_K, IQ4_NL, Q5_K, Q4_0 = 0, 1, 2, 5, 12, 13
+BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), IQ4_NL: (32, 18), Q5_K: (256, 176),
+         Q4_0: (32, 18)}
 
 _lib = None
 _baseline = None

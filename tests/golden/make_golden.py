@@ -10,6 +10,8 @@ the build container, so this script uses it as the independent definition:
 - Q4_K   gguf/quants.py:475-523   value = (d * sc) * q - (dmin * m)
 - IQ4_NL gguf/quants.py:1330-1349 value = d * kvalues[i]
 - Q4_0   gguf/quants.py:220-251   value = d * (q - 8)
+- Q5_K   gguf/quants.py:525-549   value = (d * sc) * q - (dmin * m), q 5-bit
+- Q6_K   gguf/quants.py:552-573   value = (d * sc) * (q - 32), q 6-bit, int8 sc per 16
 
 Each fixture holds packed bytes and gguf-py's f32 output.  Two byte sources
 per format: the reference's own test generator (src/native/tests.rs:34-67,
@@ -28,7 +30,8 @@ import numpy as np
 HERE = pathlib.Path(__file__).resolve().parent
 
 # name, reference format code (src/native/quant.rs:71-87), block elements, block bytes
-FORMATS = [("q8_0", 0, 32, 34), ("q4_k", 1, 256, 144), ("iq4_nl", 5, 32, 18), ("q4_0", 13, 32, 18)]
+FORMATS = [("q8_0", 0, 32, 34), ("q4_k", 1, 256, 144), ("iq4_nl", 5, 32, 18), ("q4_0", 13, 32, 18),
+           ("q6_k", 2, 256, 210), ("q5_k", 12, 256, 176)]
 
 
 def xorshift32(state: int) -> int:
@@ -42,7 +45,7 @@ def reference_packed(code: int, block_bytes: int, block_elems: int, rows: int, c
                      seed: int) -> np.ndarray:
     """src/native/tests.rs:45-67 `packed`: random bytes, then each f16 field
     overwritten with exponent 3..7 and a random mantissa."""
-    half_offsets = {1: [0, 2]}.get(code, [0])
+    half_offsets = {1: [0, 2], 12: [0, 2], 2: [208]}.get(code, [0])
     s = (seed * 2654435761 + 1) & 0xFFFFFFFF
     out = bytearray()
     for _ in range(rows * cols // block_elems):
@@ -65,7 +68,8 @@ def gguf_dequantize(name: str, data: np.ndarray, rows: int, cols: int) -> np.nda
     from gguf import quants
     from gguf.constants import GGMLQuantizationType as T
 
-    qtype = {"q8_0": T.Q8_0, "q4_k": T.Q4_K, "iq4_nl": T.IQ4_NL, "q4_0": T.Q4_0}[name]
+    qtype = {"q8_0": T.Q8_0, "q4_k": T.Q4_K, "iq4_nl": T.IQ4_NL, "q4_0": T.Q4_0, "q6_k": T.Q6_K,
+             "q5_k": T.Q5_K}[name]
     with np.errstate(all="ignore"):
         out = quants.dequantize(data.reshape(rows, -1), qtype)
     return np.asarray(out, dtype=np.float32).reshape(rows, cols)

@@ -38,7 +38,8 @@ def test_status_names_and_packed_sizes():
     assert mgb.packed_bytes(mgb.Q4_K, 4096, 4096) == 9_437_184
     assert mgb.packed_bytes(mgb.Q8_0, 14336, 4096) == 62_390_272
     assert mgb.packed_bytes(mgb.IQ4_NL, 14336, 4096) == 33_030_144
-    assert mgb.packed_bytes(mgb.Q6_K, 1, 256) == 0  # declined format
+    assert mgb.packed_bytes(mgb.Q6_K, 14336, 4096) == 14336 * 16 * 224  # padded header
+    assert mgb.packed_bytes(3, 1, 256) == 0  # Q2_K: declined format
     # decode GEMV: no scratch; prefill GEMM: the bf16 activations
     assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 1, 4096, 4096) == 0
     assert mgb.qmatmul_workspace_bytes(mgb.Q8_0, 2, 14336, 4096) == 0
@@ -78,7 +79,7 @@ def test_null_arguments_are_rejected_without_device_work():
     assert lib.mgb_kernel_advertisement_get(99, ctypes.byref(mgb.Advertisement())) == \
         mgb.INVALID_ARGUMENT
     # a format the Provider does not execute, or a ragged shape, is refused up front
-    assert lib.mgb_qmatmul(mgb.Q6_K, None, 1, 256, None, 1, None, None, 0, None, 0, None) == \
+    assert lib.mgb_qmatmul(3, None, 1, 256, None, 1, None, None, 0, None, 0, None) == \
         mgb.UNSUPPORTED
     assert lib.mgb_qmatmul(mgb.Q4_K, None, 1, 96, None, 1, None, None, 0, None, 0, None) == \
         mgb.EXECUTION_FAILED

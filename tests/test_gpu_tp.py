@@ -74,6 +74,9 @@ CASES = [
     (synthetic.Q4_K, 256, 16384, 2),
     (synthetic.Q8_0, 128, 96, 2),
     (synthetic.Q8_0, 64, 8224, 2),
+    (synthetic.Q6_K, 512, 1024, 1),
+    (synthetic.Q6_K, 512, 1024, 96),
+    (synthetic.Q6_K, 128, 32768, 2),
 ]
 
 

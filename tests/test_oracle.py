@@ -16,7 +16,7 @@ import numpy as np
 import pytest
 
 GOLDEN = pathlib.Path(__file__).resolve().parent / "golden" / "dequant_gguf.npz"
-FORMAT_CODES = {"q8_0": 0, "q4_k": 1, "iq4_nl": 5, "q4_0": 13}
+FORMAT_CODES = {"q8_0": 0, "q4_k": 1, "iq4_nl": 5, "q4_0": 13, "q6_k": 2, "q5_k": 12}
 
 
 def _same_bits(a: np.ndarray, b: np.ndarray) -> bool:
@@ -96,6 +96,46 @@ def test_q4k_six_bit_scales_known_answer(oracle):
     assert np.all(got[128:160] == 63 * 1 - 33) and np.all(got[160:192] == 63 * 2 - 33)
 
 
+def test_q6k_known_answer(oracle):
+    # q code c (0..63) of value i of the block = (i * 7) % 64, so every code
+    # appears; scales s_t = t - 8 (negative, zero and positive int8), d = 0.25.
+    codes = [(i * 7) % 64 for i in range(256)]
+    ql, qh = bytearray(128), bytearray(64)
+    for run in range(8):
+        h, g = run // 4, run % 4
+        for i in range(32):
+            c = codes[32 * run + i]
+            ql[64 * h + 32 * (g % 2) + i] |= (c & 0xF) << (4 * (g // 2))
+            qh[32 * h + i] |= (c >> 4) << (2 * g)
+    scales = bytes((t - 8) & 0xFF for t in range(16))
+    block = bytes(ql) + bytes(qh) + scales + _f16(0.25)
+    got = oracle.dequantize(2, np.frombuffer(block, dtype=np.uint8), 1, 256)[0]
+    expected = [np.float32(np.float32(0.25) * np.float32(i // 16 - 8)) * np.float32(codes[i] - 32)
+                for i in range(256)]
+    assert np.array_equal(got, np.array(expected, dtype=np.float32))
+
+
+def test_q5k_known_answer(oracle):
+    # 5-bit codes (i * 5) % 32; Q4_K's scale layout (scale j + 1, min j, < 16)
+    codes = [(i * 5) % 32 for i in range(256)]
+    qh, ql = bytearray(32), bytearray(128)
+    for run in range(8):
+        for i in range(32):
+            c = codes[32 * run + i]
+            ql[32 * (run // 2) + i] |= (c & 0xF) << (4 * (run % 2))
+            qh[i] |= (c >> 4) << run
+    scales = bytearray(12)
+    for j in range(4):
+        scales[j] = j + 1
+        scales[j + 4] = j
+        scales[j + 8] = (j + 5) | ((j + 4) << 4)
+    block = _f16(0.5) + _f16(0.125) + bytes(scales) + bytes(qh) + bytes(ql)
+    got = oracle.dequantize(12, np.frombuffer(block, dtype=np.uint8), 1, 256)[0]
+    expected = [np.float32(0.5 * (i // 32 + 1)) * np.float32(codes[i]) - np.float32(0.125 * (i // 32))
+                for i in range(256)]
+    assert np.array_equal(got, np.array(expected, dtype=np.float32))
+
+
 def test_q8_0_and_iq4_known_answers(oracle):
     q = np.arange(-16, 16, dtype=np.int8)
     block = _f16(0.125) + q.tobytes()
@@ -129,7 +169,7 @@ def test_matmul_propagates_nan_through_zero(oracle):
     assert np.isnan(oracle.matmul(a, b)[0, 0])
 
 
-@pytest.mark.parametrize("fmt", [0, 1, 5, 13])
+@pytest.mark.parametrize("fmt", [0, 1, 2, 5, 12, 13])
 def test_packed_matmul_equals_dense_reference(oracle, fmt):
     # src/native/tests.rs:134-154 restated: f32 activations are bit-identical to
     # the dense oracle (same per-element values, same sequential order), int8
@@ -158,7 +198,7 @@ def test_odd_run_counts(oracle, fmt):
                         oracle.matmul(oracle.int8_rounded(a), dense, False, True), 2e-5)
 
 
-@pytest.mark.parametrize("fmt", [0, 1, 5, 13])
+@pytest.mark.parametrize("fmt", [0, 1, 2, 5, 12, 13])
 def test_input_major_axpy(oracle, fmt):
     # src/native/tests.rs:194-210: stored rows = input rows
     w = oracle.test_packed(fmt, 64, 256, 61)
@@ -174,7 +214,7 @@ def test_shape_errors_are_reported(oracle):
     with pytest.raises(ValueError):
         oracle.packed_matmul(1, w, 4, 256, np.zeros((1, 128), np.float32))
     with pytest.raises(ValueError):
-        oracle.dequantize(2, w, 1, 256)  # Q6_K is declined by this oracle
+        oracle.dequantize(3, w, 1, 256)  # Q2_K is declined by this oracle
 
 
 def test_bias_broadcast(oracle):
