@@ -41,8 +41,8 @@ def test_executor_stores_packed_weights(provider, oracle):
     with mgb.B200Provider(packed_weights=False) as declining:
         assert declining.write_packed_weight_tensor("w", mgb.Q4_K, 4, 256, True, w) == "Declined"
     # a format this Provider does not execute is declined (the Runtime loads f32)
-    assert provider.write_packed_weight_tensor("q6", mgb.Q6_K, 1, 256, True,
-                                               np.zeros(210, np.uint8)) == "Declined"
+    assert provider.write_packed_weight_tensor("q2", 3, 1, 256, True,  # Q2_K
+                                               np.zeros(84, np.uint8)) == "Declined"
 
 
 def test_packed_weights_survive_opaque_writes_and_yield_to_copies(provider, oracle):
