@@ -18,6 +18,10 @@ over one batch.  Metric: TFLOP/s (2*M*N*K per step), whole job.
   its event-timed average duration, against MEASURED_PEAKS.json's burst bf16.
 - gemv: config 0 (Q4_K decode GEMV 1x4096 x 4096x4096) weight GB/s, as the
   second half of the BASELINE metric.
+- formats: every format the Provider executes (Q4_K, Q6_K, Q8_0, IQ4_NL,
+  Q4_0) at config 2's K=4096, N=14336: decode GEMV (M=1) weight GB/s and the
+  prefill step (M=512) TFLOP/s, each over a CUDA graph of back-to-back
+  launches on rotating weight copies (--no-formats skips it).
 - cpu_baseline: the reference's own CPU path (int8 activations, AVX2 kernels,
   persistent pool), restated in C (oracle/cpu_baseline.c), on a sample of
   the same workload, on every host core.
@@ -359,49 +363,62 @@ def run_b200(args) -> None:
            "d2h_bytes_per_step": d2h, "ms_per_step": e2e_s * 1e3, "steps": e2e_steps,
            "path": path, "timing": "wall clock per rank, max over ranks"}
 
-    # second half of the metric: config 0 decode GEMV weight GB/s (rank 0's GPU)
-    gemv = None
-    if rank == 0:
-        gw = synthetic.packed_weights(fmt, GEMV_N, GEMV_K)
-        gb = mgb.packed_bytes(fmt, GEMV_N, GEMV_K)
-        RV = max(2, -(-3 * L2_BYTES // gb))
+    def graph_ms(gfmt: int, m: int, n: int, k: int, min_launches: int) -> tuple[float, int, int, int]:
+        """Device time per `mgb_qmatmul` (x [m, k] f32 -> y [m, n] f32) over
+        replays of one CUDA graph of back-to-back launches, one per weight copy,
+        with enough copies to exceed 3x L2.  Returns (ms, weight bytes,
+        copies, replays)."""
+        gw = synthetic.packed_weights(gfmt, n, k)
+        gb = mgb.packed_bytes(gfmt, n, k)
+        copies = max(2, -(-3 * L2_BYTES // gb))
         src = torch.from_numpy(gw).to(dev)
         GW = []
-        for _ in range(RV):
+        for _ in range(copies):
             b = torch.empty(gb, dtype=torch.uint8, device=dev)
-            mgb.repack(fmt, src.data_ptr(), GEMV_N, GEMV_K, b.data_ptr(), sp)
+            mgb.repack(gfmt, src.data_ptr(), n, k, b.data_ptr(), sp)
             GW.append(b)
-        gx = torch.from_numpy(synthetic.activations(1, GEMV_K)).to(dev)
-        gy = torch.empty((1, GEMV_N), dtype=torch.float32, device=dev)
-        gws_bytes = mgb.qmatmul_workspace_bytes(fmt, 1, GEMV_N, GEMV_K)
+        del src
+        gx = torch.from_numpy(synthetic.activations(m, k)).to(dev)
+        gy = torch.empty((m, n), dtype=torch.float32, device=dev)
+        gws_bytes = mgb.qmatmul_workspace_bytes(gfmt, m, n, k)
         gws = torch.empty(max(gws_bytes, 16), dtype=torch.uint8, device=dev)
-
-        # RV back-to-back GEMVs (one per weight copy) captured once as a CUDA
-        # graph: replays time the device, not Python's launch overhead
         cap = torch.cuda.Stream(device=dev)
         graph = torch.cuda.CUDAGraph()
         cap.wait_stream(stream)
         with torch.cuda.stream(cap):
-            for i in range(RV):  # warm the launch path outside capture
-                mgb.qmatmul(fmt, GW[i].data_ptr(), GEMV_N, GEMV_K, gx.data_ptr(), 1,
-                            gy.data_ptr(), workspace_ptr=gws.data_ptr(),
-                            workspace_bytes=gws_bytes, stream=cap.cuda_stream)
+            for i in range(copies):  # warm the launch path outside capture
+                mgb.qmatmul(gfmt, GW[i].data_ptr(), n, k, gx.data_ptr(), m, gy.data_ptr(),
+                            workspace_ptr=gws.data_ptr(), workspace_bytes=gws_bytes,
+                            stream=cap.cuda_stream)
             with torch.cuda.graph(graph, stream=cap):
-                for i in range(RV):
-                    mgb.qmatmul(fmt, GW[i].data_ptr(), GEMV_N, GEMV_K, gx.data_ptr(), 1,
-                                gy.data_ptr(), workspace_ptr=gws.data_ptr(),
-                                workspace_bytes=gws_bytes,
+                for i in range(copies):
+                    mgb.qmatmul(gfmt, GW[i].data_ptr(), n, k, gx.data_ptr(), m, gy.data_ptr(),
+                                workspace_ptr=gws.data_ptr(), workspace_bytes=gws_bytes,
                                 stream=torch.cuda.current_stream().cuda_stream)
         stream.wait_stream(cap)
-
-        def gemv_replay(_i: int) -> None:
-            graph.replay()
-
-        saved_world, world = world, 1  # single-GPU timing, no collectives
-        reps = max(5, -(-max(args.steps, 200) // RV))
-        g_ms = timed(gemv_replay, reps, 3) / (reps * RV)
-        world = saved_world
+        reps = max(3, -(-min_launches // copies))
+        ms = timed_local(lambda _i: graph.replay(), reps, 3) / (reps * copies)
         del graph
+        return ms, gb, copies, reps
+
+    def timed_local(fn, steps: int, warmup: int) -> float:
+        for i in range(warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(steps):
+            fn(i)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        return t0.elapsed_time(t1)
+
+    # second half of the metric: config 0 decode GEMV weight GB/s (rank 0's GPU)
+    gemv = None
+    formats = None
+    if rank == 0:
+        g_ms, gb, RV, reps = graph_ms(fmt, 1, GEMV_N, GEMV_K, max(args.steps, 200))
         algo = gb + GEMV_K * 4 + GEMV_N * 4
         gbs = algo / (g_ms * 1e-3) / 1e9
         gemv = {"metric": "Q4_K decode GEMV weight GB/s (config0: x[1,4096] x W[4096x4096])",
@@ -413,6 +430,22 @@ def run_b200(args) -> None:
                           "back-to-back launches (activation pack + GEMV each, programmatic "
                           "dependent launches)",
                 "traffic": profile_traffic("gemv_q4k_config0")}
+
+        # every format the Provider executes, at config 2's shape (K = 4096,
+        # N = 14336): decode GEMV (M = 1) weight GB/s and prefill step (M = 512,
+        # activation cast + tcgen05 GEMM) TFLOP/s, same graph timing
+        if not args.no_formats:
+            formats = {}
+            for name, f in (("q4_k", mgb.Q4_K), ("q6_k", mgb.Q6_K), ("q8_0", mgb.Q8_0),
+                            ("iq4_nl", mgb.IQ4_NL), ("q4_0", mgb.Q4_0)):
+                v_ms, vb, _, _ = graph_ms(f, 1, N, K, 100)
+                v_gbs = (vb + K * 4 + N * 4) / (v_ms * 1e-3) / 1e9
+                p_ms, _, _, _ = graph_ms(f, M, N, K, 40)
+                formats[name] = {"gemv_us": v_ms * 1e3, "gemv_gbs": v_gbs,
+                                 "gemv_frac_hbm": v_gbs / pk["hbm_gbs"],
+                                 "prefill_us": p_ms * 1e3,
+                                 "prefill_tflops": 2.0 * M * N * K / (p_ms * 1e-3) / 1e12,
+                                 "device_bytes": vb}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -433,7 +466,7 @@ def run_b200(args) -> None:
                                       "mgb_tp_wait)" if world > 1 else "")},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": (3 if world > 1 else 2) * args.steps, "clocks": clocks,
-                "gemv": gemv, "tp_baseline_nccl": nccl}
+                "gemv": gemv, "formats": formats, "tp_baseline_nccl": nccl}
         print(json.dumps(line), flush=True)
     if op is not None:
         op.close()
@@ -449,6 +482,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-formats", action="store_true", help="skip the per-format table")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
