@@ -18,8 +18,8 @@ over one batch.  Metric: TFLOP/s (2*M*N*K per step), whole job.
   its event-timed average duration, against MEASURED_PEAKS.json's burst bf16.
 - gemv: config 0 (Q4_K decode GEMV 1x4096 x 4096x4096) weight GB/s, as the
   second half of the BASELINE metric.
-- formats: every format the Provider executes (Q4_K, Q6_K, Q8_0, IQ4_NL,
-  Q4_0) at config 2's K=4096, N=14336: decode GEMV (M=1) weight GB/s and the
+- formats: every format the Provider executes (Q4_K, Q5_K, Q6_K, Q8_0,
+  IQ4_NL, Q4_0) at config 2's K=4096, N=14336: decode GEMV (M=1) weight GB/s and the
   prefill step (M=512) TFLOP/s, each over a CUDA graph of back-to-back
   launches on rotating weight copies (--no-formats skips it).
 - cpu_baseline: the reference's own CPU path (int8 activations, AVX2 kernels,
@@ -436,8 +436,8 @@ def run_b200(args) -> None:
         # activation cast + tcgen05 GEMM) TFLOP/s, same graph timing
         if not args.no_formats:
             formats = {}
-            for name, f in (("q4_k", mgb.Q4_K), ("q6_k", mgb.Q6_K), ("q8_0", mgb.Q8_0),
-                            ("iq4_nl", mgb.IQ4_NL), ("q4_0", mgb.Q4_0)):
+            for name, f in (("q4_k", mgb.Q4_K), ("q5_k", mgb.Q5_K), ("q6_k", mgb.Q6_K),
+                            ("q8_0", mgb.Q8_0), ("iq4_nl", mgb.IQ4_NL), ("q4_0", mgb.Q4_0)):
                 v_ms, vb, _, _ = graph_ms(f, 1, N, K, 100)
                 v_gbs = (vb + K * 4 + N * 4) / (v_ms * 1e-3) / 1e9
                 p_ms, _, _, _ = graph_ms(f, M, N, K, 40)

@@ -49,8 +49,9 @@ typedef enum mgb_status {
 } mgb_status;
 
 /* Packed block formats.  Codes follow the reference's `FORMATS` order
- * (src/native/quant.rs:71-87).  This Provider stores Q8_0, Q4_K, Q6_K, IQ4_NL
- * and Q4_0 and declines the rest (the Runtime then loads those weights as f32). */
+ * (src/native/quant.rs:71-87).  This Provider stores Q8_0, Q4_K, Q5_K, Q6_K,
+ * IQ4_NL and Q4_0 and declines the rest (the Runtime then loads those weights
+ * as f32). */
 enum {
     MGB_FORMAT_Q8_0 = 0,
     MGB_FORMAT_Q4_K = 1,
@@ -248,7 +249,8 @@ mgb_status mgb_observations(mgb_provider *provider, mgb_observation *out, size_t
  * ggml blocks rearranged into a quant plane (each 32-value run's quants in 16
  * or 32 aligned bytes, value pairs adjacent) followed by a scale plane (Q4_K:
  * the 16-byte d/dmin/scales header per super-block; Q8_0, IQ4_NL, Q4_0: the
- * f16 scale per block; Q6_K: the quant plane holds 48 bytes per 64 values,
+ * f16 scale per block; Q5_K: Q4_K's header followed by each run's 32 fifth
+ * bits, 48 bytes per 256 values; Q6_K: the quant plane holds 48 bytes per 64 values,
  * the two runs' low-nibble pairs then their high 2-bit fields, and the scale
  * plane a 32-byte header per 256 values, the 16 int8 scales then d).  Same
  * bits and byte count as the ggml blocks, except Q6_K's padded header (224

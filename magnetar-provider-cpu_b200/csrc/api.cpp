@@ -36,17 +36,19 @@ void clear_error() { g_last_error.clear(); }
 
 bool format_supported(int32_t format) {
   return format == MGB_FORMAT_Q8_0 || format == MGB_FORMAT_Q4_K || format == MGB_FORMAT_Q6_K ||
-         format == MGB_FORMAT_IQ4_NL || format == MGB_FORMAT_Q4_0;
+         format == MGB_FORMAT_Q5_K || format == MGB_FORMAT_IQ4_NL || format == MGB_FORMAT_Q4_0;
 }
 
 uint64_t format_block_elements(int32_t format) {
-  return format == MGB_FORMAT_Q4_K || format == MGB_FORMAT_Q6_K ? 256 : 32;
+  return format == MGB_FORMAT_Q4_K || format == MGB_FORMAT_Q6_K || format == MGB_FORMAT_Q5_K ? 256
+                                                                                             : 32;
 }
 
 uint64_t ggml_bytes(int32_t format, uint64_t rows, uint64_t cols) {
   if (!format_supported(format)) return 0;
   const uint64_t bb = format == MGB_FORMAT_Q4_K   ? 144
                       : format == MGB_FORMAT_Q6_K ? 210
+                      : format == MGB_FORMAT_Q5_K ? 176
                       : format == MGB_FORMAT_Q8_0 ? 34
                                                   : 18;
   return rows * (cols / format_block_elements(format)) * bb;

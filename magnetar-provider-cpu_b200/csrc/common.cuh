@@ -14,17 +14,21 @@
 namespace mgb {
 
 // Format codes: the reference's `FORMATS` order (src/native/quant.rs:71-87).
-enum Format : int { Q8_0 = 0, Q4_K = 1, Q6_K = 2, IQ4_NL = 5, Q4_0 = 13 };
+enum Format : int { Q8_0 = 0, Q4_K = 1, Q6_K = 2, IQ4_NL = 5, Q5_K = 12, Q4_0 = 13 };
 
 constexpr int RUN = 32;  // values per run (src/native/quant.rs:19)
 
 __host__ __device__ inline bool supported(int f) {
-  return f == Q8_0 || f == Q4_K || f == Q6_K || f == IQ4_NL || f == Q4_0;
+  return f == Q8_0 || f == Q4_K || f == Q6_K || f == Q5_K || f == IQ4_NL || f == Q4_0;
 }
-__host__ __device__ inline int block_elements(int f) { return f == Q4_K || f == Q6_K ? 256 : 32; }
+__host__ __device__ inline int block_elements(int f) {
+  return f == Q4_K || f == Q6_K || f == Q5_K ? 256 : 32;
+}
 __host__ __device__ inline int block_bytes(int f) {
-  return f == Q4_K ? 144 : f == Q6_K ? 210 : (f == Q8_0 ? 34 : 18);
+  return f == Q4_K ? 144 : f == Q6_K ? 210 : f == Q5_K ? 176 : (f == Q8_0 ? 34 : 18);
 }
+// Super-block formats whose header holds d, dmin and Q4_K's 6-bit scale fields.
+__host__ __device__ inline bool k_scale_min(int f) { return f == Q4_K || f == Q5_K; }
 
 // Device layout of an [n stored rows x k stored cols] packed matrix: the
 // quant plane (n rows of `qs_row` bytes: one 16-byte run of nibble pairs for
@@ -32,14 +36,16 @@ __host__ __device__ inline int block_bytes(int f) {
 // the two runs' low-nibble pairs then their high 2-bit fields, 8 bytes per
 // run) followed by the scale plane (n rows of `sc_row` bytes: Q4_K's 16-byte
 // d/dmin/scales header per 256 values; Q6_K's 32-byte header per 256 values,
-// its 16 int8 scales then d; or one f16 scale per 32 values).  The byte count
-// equals the ggml blocks' except Q6_K's (224 bytes per 256 values against
-// 210: the header is padded so every copy stays 16-byte aligned).
+// its 16 int8 scales then d; Q5_K's 48-byte header per 256 values, Q4_K's 16
+// bytes then each run's 32 fifth bits as one word; or one f16 scale per 32
+// values).  The byte count equals the ggml blocks' except Q6_K's (224 bytes
+// per 256 values against 210: the header is padded so every copy stays
+// 16-byte aligned).
 struct Layout {
   uint64_t n, k, qs_row, sc_row, qs_bytes, total;
   __host__ __device__ Layout(int f, uint64_t n_, uint64_t k_) : n(n_), k(k_) {
     qs_row = f == Q8_0 ? k : f == Q6_K ? k / 4 * 3 : k / 2;
-    sc_row = f == Q6_K ? k / 8 : k / 16;
+    sc_row = f == Q6_K ? k / 8 : f == Q5_K ? k / 256 * 48 : k / 16;
     qs_bytes = n * qs_row;
     total = qs_bytes + n * sc_row;
   }
@@ -99,6 +105,16 @@ __device__ __forceinline__ void q6k_codes(uint32_t nib_word, uint32_t hw, int wd
   const int b = wd & 1;
   ev = (nib_word & 0x0F0F0F0Fu) | (((hw >> (4 * b)) & 0x03030303u) << 4);
   od = ((nib_word >> 4) & 0x0F0F0F0Fu) | (((hw >> (4 * b + 2)) & 0x03030303u) << 4);
+}
+
+// Q5_K: the 5-bit codes of the 8 values of nibble word wd of a run (nibble-pair
+// order, as q6k_codes).  hb is the run's fifth-bit word: byte j holds the
+// fifth bits of values 8 wd + 2 j (bit 2 wd) and 8 wd + 2 j + 1 (bit 2 wd + 1)
+// for wd = 0..3.
+__device__ __forceinline__ void q5k_codes(uint32_t nib_word, uint32_t hb, int wd, uint32_t &ev,
+                                          uint32_t &od) {
+  ev = (nib_word & 0x0F0F0F0Fu) | (((hb >> (2 * wd)) & 0x01010101u) << 4);
+  od = ((nib_word >> 4) & 0x0F0F0F0Fu) | (((hb >> (2 * wd + 1)) & 0x01010101u) << 4);
 }
 
 // ---- device error flag -------------------------------------------------------------

@@ -56,7 +56,7 @@ struct GemmParams {
   int bstages;          // bf16 W-tile ring
   int pstages;          // packed-W ring
   int qbytes;           // packed quant bytes per weight row per K step (32, 48 or 64)
-  int wsw;              // scale-plane bytes per weight row per 256 values (16 or 32)
+  int wsw;              // scale-plane bytes per weight row per 256 values (16, 32 or 48)
   uint32_t a_bytes;     // per activation stage
   uint32_t b_bytes;     // per W-tile stage
   uint32_t wq_bytes;    // per packed stage
@@ -208,6 +208,29 @@ __device__ __forceinline__ void dq_q6k(const uint4 &qs, const uint2 &hw, float s
   }
 }
 
+// Q5_K: nibble pairs plus the run's fifth-bit word; value = s * c - mn with
+// the 5-bit code c, by the nibble formula with the code in the mantissa.
+__device__ __forceinline__ void dq_q5k(const uint4 &qs, uint32_t hb, float s, float mn,
+                                       uint4 out[4]) {
+  const float a = 256.f * s, c = -(128.f * s + mn);
+  const float2 a2 = make_float2(a, a), c2 = make_float2(c, c);
+  const uint32_t words[4] = {qs.x, qs.y, qs.z, qs.w};
+#pragma unroll
+  for (int wd = 0; wd < 4; ++wd) {
+    uint32_t ev, od;
+    q5k_codes(words[wd], hb, wd, ev, od);
+    uint32_t p[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float f0 = __uint_as_float(__byte_perm(ev, 0x3F000000u, 0x7054u | ((uint32_t)i << 8)));
+      const float f1 = __uint_as_float(__byte_perm(od, 0x3F000000u, 0x7054u | ((uint32_t)i << 8)));
+      const float2 v = __ffma2_rn(make_float2(f0, f1), a2, c2);
+      p[i] = pack_bf16(v.x, v.y);
+    }
+    out[wd] = make_uint4(p[0], p[1], p[2], p[3]);
+  }
+}
+
 // Biased bytes (b + 128, byte order = value order) times d.
 __device__ __forceinline__ void dq_bytes(const uint32_t u[8], float d, uint4 out[4]) {
 #pragma unroll
@@ -249,13 +272,17 @@ __device__ __forceinline__ void dequant_run(const uint8_t *wq_row, const uint8_t
     const float d = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(ws_row + 16));
     const uint16_t sp = *reinterpret_cast<const uint16_t *>(ws_row + 2 * sub);
     dq_q6k(qs, hw, d * (float)(int8_t)(sp & 0xFF), d * (float)(int8_t)(sp >> 8), out);
-  } else if (FMT == Q4_K) {
+  } else if (FMT == Q4_K || FMT == Q5_K) {
     const uint4 qs = *reinterpret_cast<const uint4 *>(wq_row + j * 16);
     const uint4 h = *reinterpret_cast<const uint4 *>(ws_row);
     const float d = f16_bits_to_f32(h.x), dmin = f16_bits_to_f32(h.x >> 16);
     uint32_t sc, mn;
     q4k_scale_min(sub, h.y, h.z, h.w, sc, mn);
-    dq_nib_linear(qs, d * (float)sc, dmin * (float)mn, out);
+    if (FMT == Q5_K)
+      dq_q5k(qs, *reinterpret_cast<const uint32_t *>(ws_row + 16 + 4 * sub), d * (float)sc,
+             dmin * (float)mn, out);
+    else
+      dq_nib_linear(qs, d * (float)sc, dmin * (float)mn, out);
   } else if (FMT == Q4_0) {
     const uint4 qs = *reinterpret_cast<const uint4 *>(wq_row + j * 16);
     const uint32_t hb = *reinterpret_cast<const uint16_t *>(ws_row + 2 * sub);
@@ -695,7 +722,7 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
   p.n = (int)n;
   p.k = (int)k;
   p.qbytes = fmt == Q8_0 ? 64 : fmt == Q6_K ? 48 : 32;
-  p.wsw = fmt == Q6_K ? 32 : 16;
+  p.wsw = fmt == Q6_K ? 32 : fmt == Q5_K ? 48 : 16;
   p.bn = t.bn;
   p.a_bytes = 16384u * t.subs;
   p.b_bytes = (uint32_t)ceil_div((uint64_t)t.bn * 128u, 1024) * 1024;
@@ -751,6 +778,7 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
   switch (fmt) {
     MGB_GEMM_FMT(Q4_K)
     MGB_GEMM_FMT(Q6_K)
+    MGB_GEMM_FMT(Q5_K)
     MGB_GEMM_FMT(Q8_0)
     MGB_GEMM_FMT(IQ4_NL)
     MGB_GEMM_FMT(Q4_0)

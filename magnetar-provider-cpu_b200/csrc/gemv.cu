@@ -213,14 +213,34 @@ __device__ __forceinline__ void run_partials(const uint4 &qa, const uint4 &qb, c
       part[m] = ((s0 * x[m].dx) * (float)(sh[0] * 256 + sl[0]) - (32.f * s0) * x[m].hs[0]) +
                 ((s1 * x[m].dx) * (float)(sh[1] * 256 + sl[1]) - (32.f * s1) * x[m].hs[1]);
     }
-  } else if (FMT == Q4_K) {
+  } else if (FMT == Q4_K || FMT == Q5_K) {
     const float d = f16_bits_to_f32(hd.x), dmin = f16_bits_to_f32(hd.x >> 16);
     uint32_t sc, mn;
     q4k_scale_min(j, hd.y, hd.z, hd.w, sc, mn);
     const float s = d * (float)sc, mv = dmin * (float)mn;
+    uint4 q = qa;
+    if (FMT == Q5_K) {  // 5-bit codes in the nibble-pair order (qb.x: the fifth bits)
+      uint32_t e[4], o[4];
+      const uint32_t words[4] = {qa.x, qa.y, qa.z, qa.w};
 #pragma unroll
-    for (int m = 0; m < MR; ++m)
-      part[m] = (s * x[m].dx) * (float)dot_nib(qa, x[m]) - mv * x[m].sum;
+      for (int wd = 0; wd < 4; ++wd) q5k_codes(words[wd], qb.x, wd, e[wd], o[wd]);
+#pragma unroll
+      for (int m = 0; m < MR; ++m) {
+        int sh = 0, sl = 0;
+#pragma unroll
+        for (int wd = 0; wd < 4; ++wd) {
+          sh = dp4a_us(e[wd], x[m].hi[2 * wd], sh);
+          sh = dp4a_us(o[wd], x[m].hi[2 * wd + 1], sh);
+          sl = dp4a_uu(e[wd], x[m].lo[2 * wd], sl);
+          sl = dp4a_uu(o[wd], x[m].lo[2 * wd + 1], sl);
+        }
+        part[m] = (s * x[m].dx) * (float)(sh * 256 + sl) - mv * x[m].sum;
+      }
+    } else {
+#pragma unroll
+      for (int m = 0; m < MR; ++m)
+        part[m] = (s * x[m].dx) * (float)dot_nib(q, x[m]) - mv * x[m].sum;
+    }
   } else if (FMT == Q4_0) {
     const float d = f16_bits_to_f32(dh);
 #pragma unroll
@@ -255,8 +275,8 @@ __device__ __forceinline__ float2 decode_run_scale(const uint8_t *srow, int uu) 
     const float d = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(hd + 16));
     const uint16_t sp = *reinterpret_cast<const uint16_t *>(hd + 2 * (uu & 7));
     return make_float2(d * (float)(int8_t)(sp & 0xFF), d * (float)(int8_t)(sp >> 8));
-  } else if (FMT == Q4_K) {
-    const uint4 hd = *reinterpret_cast<const uint4 *>(srow + (uu >> 3) * 16);
+  } else if (FMT == Q4_K || FMT == Q5_K) {
+    const uint4 hd = *reinterpret_cast<const uint4 *>(srow + (uu >> 3) * (FMT == Q5_K ? 48 : 16));
     const float d = f16_bits_to_f32(hd.x), dmin = f16_bits_to_f32(hd.x >> 16);
     uint32_t sc, mn;
     q4k_scale_min(uu & 7, hd.y, hd.z, hd.w, sc, mn);
@@ -275,7 +295,8 @@ __device__ __forceinline__ float2 decode_run_scale(const uint8_t *srow, int uu) 
 template <int FMT, int MR, int RPT>
 __device__ __forceinline__ void rows_partials(const uint8_t *q, size_t q_stride, const float2 *dec,
                                               size_t dec_stride, int uu, const XRun (&x)[MR],
-                                              const uint32_t lut[4], float (&part)[RPT * MR]) {
+                                              const uint32_t lut[4], float (&part)[RPT * MR],
+                                              const uint8_t *sc = nullptr, size_t sc_stride = 0) {
   int sh[RPT][MR], sl[RPT][MR];
   float2 sm[RPT];
 #pragma unroll
@@ -345,9 +366,14 @@ __device__ __forceinline__ void rows_partials(const uint8_t *q, size_t q_stride,
     }
   } else {
     uint4 qa[RPT];
+    uint32_t hb[RPT];
 #pragma unroll
-    for (int i = 0; i < RPT; ++i)
+    for (int i = 0; i < RPT; ++i) {
       qa[i] = *reinterpret_cast<const uint4 *>(q + (size_t)i * q_stride + uu * 16);
+      hb[i] = FMT == Q5_K ? *reinterpret_cast<const uint32_t *>(sc + (size_t)i * sc_stride +
+                                                                 (uu >> 3) * 48 + 16 + (uu & 7) * 4)
+                          : 0u;
+    }
 #pragma unroll
     for (int wd = 0; wd < 4; ++wd)
 #pragma unroll
@@ -363,9 +389,10 @@ __device__ __forceinline__ void rows_partials(const uint8_t *q, size_t q_stride,
             sl[i][m] = dp4a_su(c0, x[m].lo[2 * wd], sl[i][m]);
             sl[i][m] = dp4a_su(c1, x[m].lo[2 * wd + 1], sl[i][m]);
           }
-        } else {  // Q4_K, Q4_0: nibble pairs
-          const uint32_t ev = v & 0x0F0F0F0Fu;         // values 8wd + 0, 2, 4, 6
-          const uint32_t od = (v >> 4) & 0x0F0F0F0Fu;  // values 8wd + 1, 3, 5, 7
+        } else {  // Q4_K, Q4_0: nibble pairs; Q5_K: plus each value's fifth bit
+          uint32_t ev = v & 0x0F0F0F0Fu;         // values 8wd + 0, 2, 4, 6
+          uint32_t od = (v >> 4) & 0x0F0F0F0Fu;  // values 8wd + 1, 3, 5, 7
+          if (FMT == Q5_K) q5k_codes(v, hb[i], wd, ev, od);
 #pragma unroll
           for (int m = 0; m < MR; ++m) {
             sh[i][m] = dp4a_us(ev, x[m].hi[2 * wd], sh[i][m]);
@@ -381,7 +408,7 @@ __device__ __forceinline__ void rows_partials(const uint8_t *q, size_t q_stride,
 #pragma unroll
     for (int m = 0; m < MR; ++m) {
       const float dot = (float)(sh[i][m] * 256 + sl[i][m]);
-      if (FMT == Q4_K || FMT == Q4_0)
+      if (FMT == Q4_K || FMT == Q4_0 || FMT == Q5_K)
         part[i * MR + m] = (sm[i].x * x[m].dx) * dot - sm[i].y * x[m].sum;
       else
         part[i * MR + m] = (sm[i].x * x[m].dx) * dot + 0.f * x[m].sum;  // NaN / Inf in x reach y
@@ -391,7 +418,7 @@ __device__ __forceinline__ void rows_partials(const uint8_t *q, size_t q_stride,
 template <int FMT, int MR>
 __device__ __forceinline__ void load_x(const float *__restrict__ x, int k, int u, bool active,
                                        XRun (&xr)[MR]) {
-  constexpr bool pair = FMT == Q4_K || FMT == Q4_0 || FMT == Q6_K;
+  constexpr bool pair = FMT == Q4_K || FMT == Q4_0 || FMT == Q6_K || FMT == Q5_K;
 #pragma unroll
   for (int m = 0; m < MR; ++m) {
     float v[32];
@@ -575,7 +602,8 @@ __global__ void __launch_bounds__(MAXT, MINB)
     float part[RPT * MR];
     rows_partials<FMT, MR, RPT>(st + (size_t)team * RPT * L.qs_row, L.qs_row,
                                 dec + ((size_t)s * TR + team * RPT) * runs + uu, runs, uu, xr, lut,
-                                part);
+                                part, st + p.qs_stage_bytes + (size_t)team * RPT * L.sc_row,
+                                L.sc_row);
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
       const bool keep = ok && active && row0 + team * RPT + i < r1;
@@ -668,7 +696,10 @@ __global__ void __launch_bounds__(MAXT, 1)
           qa = ld_stream_v4(qrow + (size_t)u * 16);
         }
         if (FMT == Q4_K) hd = __ldg(reinterpret_cast<const uint4 *>(srow + (size_t)(u >> 3) * 16));
-        else if (FMT == Q6_K) {
+        else if (FMT == Q5_K) {
+          hd = __ldg(reinterpret_cast<const uint4 *>(srow + (size_t)(u >> 3) * 48));
+          qb.x = __ldg(reinterpret_cast<const uint32_t *>(srow + (size_t)(u >> 3) * 48 + 16 + (u & 7) * 4));
+        } else if (FMT == Q6_K) {
           hd = __ldg(reinterpret_cast<const uint4 *>(srow + (size_t)(u >> 3) * 32));
           dh = ld_nc_u16(srow + (size_t)(u >> 3) * 32 + 16);
         } else dh = ld_nc_u16(srow + (size_t)u * 2);
@@ -860,6 +891,7 @@ cudaError_t launch_gemv(int fmt, const void *w, uint64_t n, uint64_t k, const fl
   switch (fmt) {
     MGB_GEMV_CASE(Q4_K)
     MGB_GEMV_CASE(Q6_K)
+    MGB_GEMV_CASE(Q5_K)
     MGB_GEMV_CASE(Q8_0)
     MGB_GEMV_CASE(IQ4_NL)
     MGB_GEMV_CASE(Q4_0)

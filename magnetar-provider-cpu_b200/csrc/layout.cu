@@ -10,6 +10,28 @@
 
 namespace mgb {
 
+// The 16-byte device header of a Q4_K / Q5_K super-block: d, dmin as they are,
+// then the eight 6-bit (scale, min) pairs of get_scale_min_k4 (the 12 bytes at
+// blk + 4) rearranged as 16 contiguous 6-bit fields.
+__device__ void write_k_header(const uint8_t *blk, uint8_t *out) {
+  for (int i = 0; i < 4; ++i) out[i] = blk[i];
+  uint64_t lo = 0, hi = 0;  // bits 0..63 and 64..95 of the 96-bit field array
+  for (int jj = 0; jj < 8; ++jj) {
+    uint8_t s, m;
+    scale_min_k4_bytes(jj, blk + 4, s, m);
+    const int bs = 6 * jj, bm = 48 + 6 * jj;
+    lo |= (uint64_t)s << bs;
+    if (bm < 64) {
+      lo |= (uint64_t)m << bm;
+      if (bm + 6 > 64) hi |= (uint64_t)m >> (64 - bm);
+    } else {
+      hi |= (uint64_t)m << (bm - 64);
+    }
+  }
+  for (int i = 0; i < 8; ++i) out[4 + i] = (uint8_t)(lo >> (8 * i));
+  for (int i = 0; i < 4; ++i) out[12 + i] = (uint8_t)(hi >> (8 * i));
+}
+
 // One thread per 32-value run: gathers the run's quants from its ggml block and
 // writes them as 16 (or 32) bytes holding values (2i, 2i+1) in byte i.
 __global__ void repack_kernel(int fmt, const uint8_t *__restrict__ src, uint64_t n, uint64_t k,
@@ -41,26 +63,37 @@ __global__ void repack_kernel(int fmt, const uint8_t *__restrict__ src, uint64_t
         words[w] = v;
       }
       *reinterpret_cast<uint4 *>(qs + u * 16) = make_uint4(words[0], words[1], words[2], words[3]);
-      if (j == 0) {
-        // header: d, dmin as they are; the eight 6-bit (scale, min) pairs of
-        // get_scale_min_k4 rearranged as 16 contiguous 6-bit fields
-        for (int i = 0; i < 4; ++i) sc[b * 16 + i] = blk[i];
-        uint64_t lo = 0, hi = 0;  // bits 0..63 and 64..95 of the 96-bit field array
-        for (int jj = 0; jj < 8; ++jj) {
-          uint8_t s, m;
-          scale_min_k4_bytes(jj, blk + 4, s, m);
-          const int bs = 6 * jj, bm = 48 + 6 * jj;
-          lo |= (uint64_t)s << bs;
-          if (bm < 64) {
-            lo |= (uint64_t)m << bm;
-            if (bm + 6 > 64) hi |= (uint64_t)m >> (64 - bm);
-          } else {
-            hi |= (uint64_t)m << (bm - 64);
-          }
+      if (j == 0) write_k_header(blk, sc + b * 16);
+    } else if (fmt == Q5_K) {
+      // as Q4_K with the quants at blk + 48 and each value's fifth bit at bit j
+      // of byte i of the 32 bytes at blk + 16 (value i of run j)
+      const uint64_t b = u / 8;
+      const int j = (int)(u % 8);
+      const uint8_t *blk = row_src + b * 176;
+      const uint8_t *chunk = blk + 48 + 32 * (j / 2);
+      const int shift = 4 * (j % 2);
+      uint32_t words[4];
+      for (int w = 0; w < 4; ++w) {
+        uint32_t v = 0;
+        for (int i = 0; i < 4; ++i) {
+          const int e = 2 * (4 * w + i);
+          const uint32_t lo = (chunk[e] >> shift) & 0xF, hi = (chunk[e + 1] >> shift) & 0xF;
+          v |= (lo | (hi << 4)) << (8 * i);
         }
-        for (int i = 0; i < 8; ++i) sc[b * 16 + 4 + i] = (uint8_t)(lo >> (8 * i));
-        for (int i = 0; i < 4; ++i) sc[b * 16 + 12 + i] = (uint8_t)(hi >> (8 * i));
+        words[w] = v;
       }
+      *reinterpret_cast<uint4 *>(qs + u * 16) = make_uint4(words[0], words[1], words[2], words[3]);
+      // the run's fifth bits: byte jj bit 2 wd = value 8 wd + 2 jj, bit 2 wd + 1
+      // = value 8 wd + 2 jj + 1
+      uint32_t hb = 0;
+      for (int wd = 0; wd < 4; ++wd)
+        for (int jj = 0; jj < 4; ++jj) {
+          const int v = 8 * wd + 2 * jj;
+          hb |= (uint32_t)((blk[16 + v] >> j) & 1) << (8 * jj + 2 * wd);
+          hb |= (uint32_t)((blk[16 + v + 1] >> j) & 1) << (8 * jj + 2 * wd + 1);
+        }
+      *reinterpret_cast<uint32_t *>(sc + b * 48 + 16 + 4 * j) = hb;
+      if (j == 0) write_k_header(blk, sc + b * 48);
     } else if (fmt == Q6_K) {
       // run r = 4 h + g of the block: low nibbles in the 32 bytes at
       // 64 h + 32 (g % 2) (shift 4 (g / 2)), high 2 bits in the 32 bytes at
@@ -149,6 +182,25 @@ __device__ __forceinline__ void decode_run(int fmt, const uint8_t *__restrict__ 
   }
   const uint4 v = *reinterpret_cast<const uint4 *>(w + row * L.qs_row + u * 16);
   const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+  if (fmt == Q5_K) {
+    const uint8_t *hd = sc + (u / 8) * 48;
+    const uint32_t hb = *reinterpret_cast<const uint32_t *>(hd + 16 + 4 * (u % 8));
+    for (int wd = 0; wd < 4; ++wd) {
+      uint32_t ev, od;
+      q5k_codes(words[wd], hb, wd, ev, od);
+      for (int j = 0; j < 4; ++j) {
+        q[8 * wd + 2 * j] = (int)((ev >> (8 * j)) & 0xFF);
+        q[8 * wd + 2 * j + 1] = (int)((od >> (8 * j)) & 0xFF);
+      }
+    }
+    const uint4 h = *reinterpret_cast<const uint4 *>(hd);
+    const float d = f16_bits_to_f32(h.x), dmin = f16_bits_to_f32(h.x >> 16);
+    uint32_t s, m;
+    q4k_scale_min((int)(u % 8), h.y, h.z, h.w, s, m);
+    scale[0] = scale[1] = __fmul_rn(d, (float)s);
+    min[0] = min[1] = __fmul_rn(dmin, (float)m);
+    return;
+  }
   for (int i = 0; i < 32; ++i) {
     const uint32_t nib = (words[i / 8] >> (4 * (i % 8))) & 0xF;
     q[i] = fmt == Q4_K ? (int)nib : (fmt == Q4_0 ? (int)nib - 8 : iq4nl_value((int)nib));

@@ -27,9 +27,10 @@ OK, DECLINED, EXECUTION_FAILED, DTYPE_UNSUPPORTED, ATTRIBUTE_UNSUPPORTED = 0, 1,
 KERNEL_NOT_FOUND, TIMEOUT, MEMORY_DENIED, UNKNOWN_HANDLE, NOT_FOUND = 5, 6, 7, 8, 9
 INVALID_ARGUMENT, CUDA_ERROR, NCCL_ERROR, UNSUPPORTED = 10, 11, 12, 13
 
-Q8_0, Q4_K, Q6_K, IQ4_NL, Q4_0 = 0, 1, 2, 5, 13
-FORMATS = {"q8_0": Q8_0, "q4_k": Q4_K, "q6_k": Q6_K, "iq4_nl": IQ4_NL, "q4_0": Q4_0}
-BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), IQ4_NL: (32, 18), Q4_0: (32, 18)}
+Q8_0, Q4_K, Q6_K, IQ4_NL, Q5_K, Q4_0 = 0, 1, 2, 5, 12, 13
+FORMATS = {"q8_0": Q8_0, "q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq4_nl": IQ4_NL, "q4_0": Q4_0}
+BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210), IQ4_NL: (32, 18),
+         Q4_0: (32, 18)}
 KERNEL_AUTO, KERNEL_GEMV, KERNEL_GEMM = 0, 1, 2
 MAX_RANK = 8
 

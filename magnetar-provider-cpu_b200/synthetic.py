@@ -6,6 +6,7 @@ weights are random bytes with controlled scale fields):
           f16 d and dmin ~ U(1e-3, 1e-2) over bytes 0..3 of each 144-byte block;
 - Q8_0:   f16 d ~ U(1e-3, 1e-2), int8 quants ~ U[-127, 127];
 - IQ4_NL, Q4_0: f16 d ~ U(1e-3, 1e-2), uniform 4-bit indices;
+- Q5_K:   as Q4_K over 176-byte blocks (uniform fifth bits);
 - Q6_K:   uniform bytes (uniform 6-bit quants, uniform int8 scales), f16 d
           ~ U(1e-3, 1e-2) at bytes 208..209 of each 210-byte block;
 - activations f32 ~ N(0, 1).
@@ -17,8 +18,9 @@ from __future__ import annotations
 
 import numpy as np
 
-Q8_0, Q4_K, Q6_K, IQ4_NL, Q4_0 = 0, 1, 2, 5, 13
-BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), IQ4_NL: (32, 18), Q4_0: (32, 18)}
+Q8_0, Q4_K, Q6_K, IQ4_NL, Q5_K, Q4_0 = 0, 1, 2, 5, 12, 13
+BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210), IQ4_NL: (32, 18),
+         Q4_0: (32, 18)}
 SEED = 0x5EED
 
 
@@ -33,7 +35,7 @@ def packed_weights(fmt: int, rows: int, cols: int, seed: int = SEED) -> np.ndarr
     rng = np.random.default_rng(seed)
     blocks = rows * cols // elems
     data = rng.integers(0, 256, size=(blocks, bb), dtype=np.uint8)
-    if fmt == Q4_K:
+    if fmt in (Q4_K, Q5_K):
         data[:, 0:2] = _f16_field(rng, blocks)
         data[:, 2:4] = _f16_field(rng, blocks)
     elif fmt == Q6_K:

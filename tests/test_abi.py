@@ -39,6 +39,7 @@ def test_status_names_and_packed_sizes():
     assert mgb.packed_bytes(mgb.Q8_0, 14336, 4096) == 62_390_272
     assert mgb.packed_bytes(mgb.IQ4_NL, 14336, 4096) == 33_030_144
     assert mgb.packed_bytes(mgb.Q6_K, 14336, 4096) == 14336 * 16 * 224  # padded header
+    assert mgb.packed_bytes(mgb.Q5_K, 14336, 4096) == 14336 * 16 * 176
     assert mgb.packed_bytes(3, 1, 256) == 0  # Q2_K: declined format
     # decode GEMV: no scratch; prefill GEMM: the bf16 activations
     assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 1, 4096, 4096) == 0

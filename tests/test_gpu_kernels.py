@@ -20,7 +20,7 @@ import synthetic
 pytestmark = pytest.mark.gpu
 
 GOLDEN = pathlib.Path(__file__).resolve().parent / "golden" / "dequant_gguf.npz"
-FORMATS = [mgb.Q4_K, mgb.Q6_K, mgb.Q8_0, mgb.IQ4_NL, mgb.Q4_0]
+FORMATS = [mgb.Q4_K, mgb.Q5_K, mgb.Q6_K, mgb.Q8_0, mgb.IQ4_NL, mgb.Q4_0]
 GEMV_TOL, GEMM_TOL = 1e-3, 5e-3
 
 
@@ -64,7 +64,7 @@ def _same_bits(a, b):
     return np.array_equal(a[~nan].view(np.uint32), b[~nan].view(np.uint32))
 
 
-@pytest.mark.parametrize("name", ["q4_k", "q6_k", "q8_0", "iq4_nl", "q4_0"])
+@pytest.mark.parametrize("name", ["q4_k", "q5_k", "q6_k", "q8_0", "iq4_nl", "q4_0"])
 @pytest.mark.parametrize("source", ["reference_generator", "random_bytes"])
 def test_dequantize_bit_exact_to_gguf_and_oracle(torch_cuda, oracle, name, source):
     torch = torch_cuda
@@ -97,8 +97,8 @@ def test_dequantize_full_size_bit_exact(torch_cuda, oracle, fmt):
 @pytest.mark.parametrize("m", [1, 2])
 @pytest.mark.parametrize("n,k", [(37, 512), (5, 96), (300, 8192), (64, 14336), (16, 32768)])
 def test_gemv_parity(torch_cuda, oracle, fmt, m, n, k):
-    if fmt in (mgb.Q4_K, mgb.Q6_K) and k % 256:
-        pytest.skip("Q4_K and Q6_K need whole 256-value super-blocks")
+    if fmt in (mgb.Q4_K, mgb.Q5_K, mgb.Q6_K) and k % 256:
+        pytest.skip("the K-quant formats need whole 256-value super-blocks")
     torch = torch_cuda
     w = oracle.test_packed(fmt, n, k, 21)  # the reference's own test generator
     x = oracle.test_activations(m, k, m)
@@ -124,7 +124,7 @@ def test_gemv_config0_q4k_4096(torch_cuda, oracle, fmt):
     oracle.assert_close(y, oracle.packed_matmul(fmt, w, n, k, x), GEMV_TOL, "config 0")
 
 
-@pytest.mark.parametrize("fmt", [mgb.Q8_0, mgb.IQ4_NL, mgb.Q6_K])
+@pytest.mark.parametrize("fmt", [mgb.Q8_0, mgb.IQ4_NL, mgb.Q6_K, mgb.Q5_K])
 @pytest.mark.parametrize("m", [1, 8])
 def test_config2_mixed_formats(torch_cuda, oracle, fmt, m):
     torch = torch_cuda

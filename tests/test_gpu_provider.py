@@ -10,7 +10,7 @@ import pytest
 import magnetar_b200 as mgb
 
 pytestmark = pytest.mark.gpu
-FORMATS = [mgb.Q4_K, mgb.Q6_K, mgb.Q8_0, mgb.IQ4_NL, mgb.Q4_0]
+FORMATS = [mgb.Q4_K, mgb.Q5_K, mgb.Q6_K, mgb.Q8_0, mgb.IQ4_NL, mgb.Q4_0]
 
 
 @pytest.fixture()

@@ -77,6 +77,9 @@ CASES = [
     (synthetic.Q6_K, 512, 1024, 1),
     (synthetic.Q6_K, 512, 1024, 96),
     (synthetic.Q6_K, 128, 32768, 2),
+    (synthetic.Q5_K, 512, 1024, 2),
+    (synthetic.Q5_K, 512, 1024, 96),
+    (synthetic.Q5_K, 128, 32768, 1),
 ]
 
 
