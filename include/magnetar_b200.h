@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define MGB_ABI_VERSION 1
+#define MGB_ABI_VERSION 2
 #define MGB_MAX_RANK 8
 
 /* Status codes.  The kernel errors follow `KernelError` (src/lib.rs:2193-2230,
@@ -133,6 +133,8 @@ typedef struct mgb_kernel_attrs {
     int32_t transpose_b;
     int32_t accumulation_dtype; /* MGB_DTYPE_F32; any other value is rejected (src/lib.rs:2445-2456) */
     int64_t deadline_ms;        /* < 0 none; 0 already elapsed -> MGB_TIMEOUT (src/lib.rs:2372-2380) */
+    int32_t has_scale;          /* `embedding`'s optional "scale" attribute (src/native/mod.rs:439-447) */
+    float scale;
 } mgb_kernel_attrs;
 
 /* `KernelResult` of a completed invocation. */
@@ -174,7 +176,8 @@ mgb_status mgb_provider_shutdown(mgb_provider *provider);
 int32_t mgb_provider_health(mgb_provider *provider);
 /* `Provider::devices` (src/native/mod.rs:919-921). */
 mgb_status mgb_provider_device(mgb_provider *provider, mgb_device_descriptor *out);
-/* `Provider::kernel_advertisements` (src/native/mod.rs:848-864). */
+/* `Provider::kernel_advertisements` (src/native/mod.rs:848-864): the matmul
+ * family and `embedding`. */
 size_t mgb_kernel_advertisement_count(void);
 mgb_status mgb_kernel_advertisement_get(size_t index, mgb_kernel_advertisement *out);
 
@@ -323,6 +326,19 @@ mgb_status mgb_matmul_f32(const float *a, uint64_t a_rows, uint64_t a_cols, cons
  * Synchronises with the device.  No counterpart in the reference (its kernels
  * run synchronously on the calling thread). */
 mgb_status mgb_take_device_error(int32_t device, int32_t *code);
+/* The `embedding` lookup in a packed table (`NativeState::embedding`,
+ * src/native/mod.rs:389-417): out[count, dim] = the dequantised rows of the
+ * tokens `ids` (f32 device values, count of them), times `scale` when
+ * has_scale (src/native/mod.rs:439-447).  An untransposed table is stored
+ * [vocab = stored_rows, dim = stored_cols]; a transposed one [dim =
+ * stored_rows, vocab = stored_cols] (the token's value in every stored row).
+ * Values are bit-exact to the reference's `dequantize_row` / `element`.  Ids
+ * are checked on the device: `bad` (device u32, may be NULL) receives the
+ * position of the first id that is not a whole number below the vocabulary
+ * size, 0xFFFFFFFF when all are valid (that row of out is zeros). */
+mgb_status mgb_embedding(int32_t format, const void *w, uint64_t stored_rows, uint64_t stored_cols,
+                         int32_t transposed, const float *ids, uint64_t count, int32_t has_scale,
+                         float scale, float *out, uint32_t *bad, void *stream);
 /* Int8 activation quantisation (`quantize_rows`, src/native/quant.rs:350-378):
  * values[len], scales[len/32], sums[len/32][2]. */
 mgb_status mgb_quantize_rows(const float *x, uint64_t len, int8_t *values, float *scales,

@@ -246,6 +246,18 @@ mgb_status mgb_qmatmul_bf16(int32_t format, const void *w, uint64_t n, uint64_t 
   return e == cudaSuccess ? MGB_OK : cuda_fail(e, "GEMM launch");
 }
 
+mgb_status mgb_embedding(int32_t format, const void *w, uint64_t stored_rows, uint64_t stored_cols,
+                         int32_t transposed, const float *ids, uint64_t count, int32_t has_scale,
+                         float scale, float *out, uint32_t *bad, void *stream) {
+  mgb_status s = check_packed_shape(format, stored_rows, stored_cols);
+  if (s != MGB_OK) return s == MGB_DECLINED ? fail(MGB_UNSUPPORTED, "%s", mgb_last_error()) : s;
+  if (count && (!w || !ids || !out)) return fail(MGB_INVALID_ARGUMENT, "null device pointer");
+  cudaError_t e = launch_embedding(format, w, stored_rows, stored_cols, transposed != 0, ids, count,
+                                   has_scale != 0, scale, out, bad,
+                                   static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MGB_OK : cuda_fail(e, "embedding launch");
+}
+
 mgb_status mgb_dequantize(int32_t format, const void *w, uint64_t stored_rows, uint64_t stored_cols,
                           float *out, void *stream) {
   mgb_status s = check_packed_shape(format, stored_rows, stored_cols);

@@ -15,6 +15,14 @@ cudaError_t launch_dequantize(int fmt, const void *w, uint64_t n, uint64_t k, fl
                               cudaStream_t stream);
 cudaError_t launch_input_major(int fmt, const void *w, uint64_t k_rows, uint64_t n_cols,
                                const float *x, uint64_t m, float *y, cudaStream_t stream);
+// Packed / f32 table lookups; *bad (when given) receives the position of the
+// first invalid id, 0xFFFFFFFF when every id is valid.
+cudaError_t launch_embedding(int fmt, const void *w, uint64_t stored_rows, uint64_t stored_cols,
+                             int transposed, const float *ids, uint64_t count, int has_scale,
+                             float scale, float *out, uint32_t *bad, cudaStream_t stream);
+cudaError_t launch_embedding_f32(const float *table, uint64_t vocab, uint64_t dim, const float *ids,
+                                 uint64_t count, int has_scale, float scale, float *out,
+                                 uint32_t *bad, cudaStream_t stream);
 
 // gemv.cu: m <= 2.  addend_mode 0 none, 1 row broadcast addend[n], 2 addend[m, n].
 // Launched with programmatic stream serialization (it may start while the

@@ -266,6 +266,68 @@ __global__ void input_major_kernel(int fmt, const uint8_t *__restrict__ w, uint6
   }
 }
 
+// A token id is valid when it is a whole number in [0, vocab) (the
+// reference's `raw_id < 0.0 || raw_id.fract() != 0.0 || raw_id as u64 >=
+// vocab` check; NaN and infinities fail it).
+__device__ __forceinline__ bool valid_token(float raw, uint64_t vocab) {
+  return raw >= 0.0f && floorf(raw) == raw && (double)raw < (double)vocab;
+}
+
+// Packed-table embedding (`NativeState::embedding`, src/native/mod.rs:389-417):
+// out[t, j] = value(token_t, j) (* scale), with value the dequantised
+// element: stored row token_t, column j of an untransposed [vocab, dim] table,
+// or stored row j, column token_t of a transposed [dim, vocab] one.  One
+// thread per output element.  An invalid id writes zeros for its row and
+// records its position (the smallest one wins) in *bad.
+__global__ void embedding_kernel(int fmt, const uint8_t *__restrict__ w, uint64_t stored_rows,
+                                 uint64_t stored_cols, int transposed, const float *__restrict__ ids,
+                                 uint64_t count, int has_scale, float scale, float *__restrict__ out,
+                                 uint32_t *bad) {
+  const Layout L(fmt, stored_rows, stored_cols);
+  const uint64_t vocab = transposed ? stored_cols : stored_rows;
+  const uint64_t dim = transposed ? stored_rows : stored_cols;
+  const uint64_t total = count * dim;
+  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total;
+       e += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t t = e / dim, j = e % dim;
+    const float raw = ids[t];
+    if (!valid_token(raw, vocab)) {
+      out[e] = 0.0f;
+      if (j == 0 && bad) atomicMin(bad, (uint32_t)(t < 0xFFFFFFFEull ? t : 0xFFFFFFFEull));
+      continue;
+    }
+    const uint64_t token = (uint64_t)raw;
+    const uint64_t row = transposed ? j : token, col = transposed ? token : j;
+    int q[32];
+    float sc[2], mn[2];
+    decode_run(fmt, w, L, row, col / RUN, q, sc, mn);
+    const int i = (int)(col % RUN);
+    float v = __fsub_rn(__fmul_rn(sc[i / 16], (float)q[i]), mn[i / 16]);
+    if (has_scale) v = __fmul_rn(v, scale);
+    out[e] = v;
+  }
+}
+
+// The same lookup in an f32 table [vocab, dim] (`f32_embedding`,
+// src/native/mod.rs:238-263), with the optional scale.
+__global__ void embedding_f32_kernel(const float *__restrict__ table, uint64_t vocab, uint64_t dim,
+                                     const float *__restrict__ ids, uint64_t count, int has_scale,
+                                     float scale, float *__restrict__ out, uint32_t *bad) {
+  const uint64_t total = count * dim;
+  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total;
+       e += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t t = e / dim, j = e % dim;
+    const float raw = ids[t];
+    if (!valid_token(raw, vocab)) {
+      out[e] = 0.0f;
+      if (j == 0 && bad) atomicMin(bad, (uint32_t)(t < 0xFFFFFFFEull ? t : 0xFFFFFFFEull));
+      continue;
+    }
+    const float v = table[(uint64_t)raw * dim + j];
+    out[e] = has_scale ? __fmul_rn(v, scale) : v;
+  }
+}
+
 static int grid_for(uint64_t work, int threads) {
   uint64_t blocks = ceil_div(work, threads);
   return (int)(blocks > 65535 * 4 ? 65535 * 4 : (blocks ? blocks : 1));
@@ -282,6 +344,34 @@ cudaError_t launch_dequantize(int fmt, const void *w, uint64_t n, uint64_t k, fl
                               cudaStream_t stream) {
   dequantize_kernel<<<grid_for(n * (k / RUN), 256), 256, 0, stream>>>(
       fmt, static_cast<const uint8_t *>(w), n, k, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_embedding(int fmt, const void *w, uint64_t stored_rows, uint64_t stored_cols,
+                             int transposed, const float *ids, uint64_t count, int has_scale,
+                             float scale, float *out, uint32_t *bad, cudaStream_t stream) {
+  if (bad) {
+    cudaError_t e = cudaMemsetAsync(bad, 0xFF, sizeof(uint32_t), stream);
+    if (e != cudaSuccess) return e;
+  }
+  const uint64_t dim = transposed ? stored_rows : stored_cols;
+  if (count * dim == 0) return cudaSuccess;
+  embedding_kernel<<<grid_for(count * dim, 256), 256, 0, stream>>>(
+      fmt, static_cast<const uint8_t *>(w), stored_rows, stored_cols, transposed, ids, count,
+      has_scale, scale, out, bad);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_embedding_f32(const float *table, uint64_t vocab, uint64_t dim, const float *ids,
+                                 uint64_t count, int has_scale, float scale, float *out,
+                                 uint32_t *bad, cudaStream_t stream) {
+  if (bad) {
+    cudaError_t e = cudaMemsetAsync(bad, 0xFF, sizeof(uint32_t), stream);
+    if (e != cudaSuccess) return e;
+  }
+  if (count * dim == 0) return cudaSuccess;
+  embedding_f32_kernel<<<grid_for(count * dim, 256), 256, 0, stream>>>(table, vocab, dim, ids, count,
+                                                                      has_scale, scale, out, bad);
   return cudaGetLastError();
 }
 

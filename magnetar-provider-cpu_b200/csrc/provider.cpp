@@ -14,6 +14,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
@@ -91,6 +92,7 @@ struct mgb_provider {
   DevBuf workspace;
   cudaMemPool_t pool = nullptr;  // this Provider's stream-ordered device memory
   int *dev_err = nullptr;
+  uint32_t *dev_bad = nullptr;  // first invalid token position of an embedding lookup
   uint64_t materializations = 0;
   double materialize_ms = 0.0;
   std::map<std::string, ProfileEntry> profile;
@@ -401,11 +403,107 @@ mgb_status run_matmul(mgb_provider *p, const std::string &kernel, const mgb_kern
   return MGB_OK;
 }
 
+// An f32 as Rust's `Display` writes it: the shortest digits that read back to
+// the same value, in positional notation ("3", "-0", "2.5", "0.0001",
+// "NaN", "inf").  The reference formats token ids in its errors this way.
+std::string rust_f32(float v) {
+  if (std::isnan(v)) return "NaN";
+  if (std::isinf(v)) return v < 0 ? "-inf" : "inf";
+  const std::string sign = std::signbit(v) ? "-" : "";
+  const float a = std::fabs(v);
+  if (a == 0.0f) return sign + "0";
+  char buf[64];
+  for (int prec = 0; prec < 9; ++prec) {
+    snprintf(buf, sizeof buf, "%.*e", prec, (double)a);
+    if (strtof(buf, nullptr) == a) break;
+  }
+  std::string digits;
+  const char *c = buf;
+  for (; *c && *c != 'e'; ++c)
+    if (*c >= '0' && *c <= '9') digits += *c;
+  const int exp10 = atoi(c + 1);  // value = d.ddd x 10^exp10
+  while (digits.size() > 1 && digits.back() == '0') digits.pop_back();
+  std::string r;
+  if (exp10 >= 0) {
+    const size_t int_len = (size_t)exp10 + 1;
+    if (digits.size() <= int_len) r = digits + std::string(int_len - digits.size(), '0');
+    else r = digits.substr(0, int_len) + "." + digits.substr(int_len);
+  } else {
+    r = "0." + std::string((size_t)(-exp10 - 1), '0') + digits;
+  }
+  return sign + r;
+}
+
+// `embedding` (src/native/mod.rs:389-417, dispatch and "scale" :432-450):
+// inputs [table, ids]; a packed table is read in place (`NativeState::
+// embedding`), an f32 one gathered (`f32_embedding`, :238-263).  Output
+// [ids count, dim].
+mgb_status run_embedding(mgb_provider *p, const mgb_kernel_attrs &attrs, const char *const *inputs,
+                         int32_t n_inputs, const char *output) {
+  const char *tid = n_inputs > 0 ? inputs[0] : nullptr;
+  if (!tid) return fail(MGB_EXECUTION_FAILED, "missing input at index 0");
+  Operand ids;
+  mgb_status s = input_f32(p, n_inputs > 1 ? inputs[1] : nullptr, 1, ids);
+  if (s != MGB_OK) return s;
+  uint64_t count = 1;
+  for (uint64_t d : ids.shape) count *= d;
+  uint64_t vocab = 0, dim = 0;
+  DevBuf product;
+  cudaError_t e = cudaSuccess;
+  auto pk = p->packed.find(tid);
+  if (pk != p->packed.end()) {
+    const Packed &w = pk->second;
+    const std::vector<uint64_t> ls = w.logical_shape();
+    vocab = ls[0];
+    dim = ls[1];
+    s = ensure_buf(p, product, count * dim * 4);
+    if (s == MGB_OK)
+      e = launch_embedding(w.format, w.buf.ptr, w.stored_rows, w.stored_cols, w.transposed ? 1 : 0,
+                           ids.ptr, count, attrs.has_scale, attrs.scale,
+                           static_cast<float *>(product.ptr), p->dev_bad, p->stream);
+  } else {
+    auto st = p->storage.find(tid);
+    if (st == p->storage.end()) s = fail(MGB_EXECUTION_FAILED, "no materialized data for input resource %s", tid);
+    else if (st->second.shape.size() != 2)
+      s = fail(MGB_EXECUTION_FAILED, "embedding table %s has shape %s, not [vocab, dim]", tid,
+               shape_str(st->second.shape).c_str());
+    else {
+      vocab = st->second.shape[0];
+      dim = st->second.shape[1];
+      s = ensure_buf(p, product, count * dim * 4);
+      if (s == MGB_OK)
+        e = launch_embedding_f32(static_cast<const float *>(st->second.buf.ptr), vocab, dim, ids.ptr,
+                                 count, attrs.has_scale, attrs.scale,
+                                 static_cast<float *>(product.ptr), p->dev_bad, p->stream);
+    }
+  }
+  uint32_t bad = 0xFFFFFFFFu;
+  float raw = 0.0f;
+  if (s == MGB_OK && e == cudaSuccess)
+    e = cudaMemcpyAsync(&bad, p->dev_bad, sizeof(bad), cudaMemcpyDeviceToHost, p->stream);
+  if (s == MGB_OK && e == cudaSuccess) e = cudaStreamSynchronize(p->stream);
+  if (s == MGB_OK && e == cudaSuccess && bad != 0xFFFFFFFFu)
+    e = cudaMemcpy(&raw, ids.ptr + bad, sizeof(raw), cudaMemcpyDeviceToHost);
+  if (ids.owned.ptr) free_buf(p, ids.owned);
+  if (s == MGB_OK && e != cudaSuccess) s = cuda_fail(e, "embedding");
+  if (s == MGB_OK && bad != 0xFFFFFFFFu)
+    s = fail(MGB_EXECUTION_FAILED, "token id %s is not below the vocabulary size %llu",
+             rust_f32(raw).c_str(), (unsigned long long)vocab);
+  if (s != MGB_OK) {
+    free_buf(p, product);
+    return s;
+  }
+  forget_packed(p, output);
+  put_tensor(p, output, {count, dim}, product);
+  return MGB_OK;
+}
+
 const mgb_kernel_advertisement ADS[] = {
     {"matmul", "linear-algebra", 2, MGB_DTYPE_F32, MGB_DTYPE_F32, MGB_CANCELLATION_TIMEOUT_ONLY},
     {"matmul-bias", "linear-algebra", 2, MGB_DTYPE_F32, MGB_DTYPE_F32, MGB_CANCELLATION_TIMEOUT_ONLY},
     {"matmul-residual", "linear-algebra", 2, MGB_DTYPE_F32, MGB_DTYPE_F32,
      MGB_CANCELLATION_TIMEOUT_ONLY},
+    {"embedding", "lookup", 2, MGB_DTYPE_F32, MGB_DTYPE_F32, MGB_CANCELLATION_TIMEOUT_ONLY},
 };
 
 int env_flag(const char *name, int dflt) {
@@ -481,8 +579,10 @@ mgb_status mgb_provider_create(const mgb_settings *settings, mgb_provider **out)
   }
   if (e == cudaSuccess) e = cudaMalloc(&p->dev_err, sizeof(int));
   if (e == cudaSuccess) e = cudaMemset(p->dev_err, 0, sizeof(int));
+  if (e == cudaSuccess) e = cudaMalloc(&p->dev_bad, sizeof(uint32_t));
   if (e != cudaSuccess) {
     if (p->dev_err) cudaFree(p->dev_err);
+    if (p->dev_bad) cudaFree(p->dev_bad);
     if (p->pool) cudaMemPoolDestroy(p->pool);
     if (p->stream) cudaStreamDestroy(p->stream);
     delete p;
@@ -517,6 +617,7 @@ void mgb_provider_destroy(mgb_provider *p) {
   if (p->stream) cudaStreamSynchronize(p->stream);
   if (p->pool) cudaMemPoolDestroy(p->pool);
   if (p->dev_err) cudaFree(p->dev_err);
+  if (p->dev_bad) cudaFree(p->dev_bad);
   if (p->stream) cudaStreamDestroy(p->stream);
   delete p;
 }
@@ -797,7 +898,7 @@ mgb_status mgb_submit_kernel(mgb_provider *p, const char *kernel, const mgb_kern
                              uint64_t *handle) {
   if (!p || !kernel || !handle || (n_inputs > 0 && !inputs) || n_inputs < 0)
     return fail(MGB_INVALID_ARGUMENT, "invalid arguments");
-  mgb_kernel_attrs at{0, 0, MGB_DTYPE_F32, -1};
+  mgb_kernel_attrs at{0, 0, MGB_DTYPE_F32, -1, 0, 1.0f};
   if (attrs) at = *attrs;
   std::lock_guard<std::mutex> lock(p->mu);
   cudaSetDevice(p->settings.device);
@@ -810,7 +911,8 @@ mgb_status mgb_submit_kernel(mgb_provider *p, const char *kernel, const mgb_kern
     ex.status = MGB_TIMEOUT;
     ex.reason = "the invocation's deadline elapsed before dispatch";
     observe(p, MGB_OBS_TIMEOUT, kernel, "handle=" + std::to_string(h));
-  } else if (name != "matmul" && name != "matmul-bias" && name != "matmul-residual") {
+  } else if (name != "matmul" && name != "matmul-bias" && name != "matmul-residual" &&
+             name != "embedding") {
     ex.status = MGB_KERNEL_NOT_FOUND;
     ex.reason = "no Kernel named " + name + " is advertised by this Provider";
     observe(p, MGB_OBS_DISPATCH_FAILED, kernel, ex.reason);
@@ -823,7 +925,8 @@ mgb_status mgb_submit_kernel(mgb_provider *p, const char *kernel, const mgb_kern
       cudaEventCreate(&ex.start);
       cudaEventRecord(ex.start, p->stream);
     }
-    mgb_status s = run_matmul(p, name, at, inputs, n_inputs, output);
+    mgb_status s = name == "embedding" ? run_embedding(p, at, inputs, n_inputs, output)
+                                       : run_matmul(p, name, at, inputs, n_inputs, output);
     if (s != MGB_OK) {
       ex.status = s;
       ex.reason = mgb_last_error();

@@ -67,7 +67,8 @@ class Advertisement(ctypes.Structure):
 
 class KernelAttrs(ctypes.Structure):
     _fields_ = [("transpose_a", ctypes.c_int32), ("transpose_b", ctypes.c_int32),
-                ("accumulation_dtype", ctypes.c_int32), ("deadline_ms", ctypes.c_int64)]
+                ("accumulation_dtype", ctypes.c_int32), ("deadline_ms", ctypes.c_int64),
+                ("has_scale", ctypes.c_int32), ("scale", ctypes.c_float)]
 
 
 class KernelResult(ctypes.Structure):
@@ -141,6 +142,8 @@ _SIGNATURES = {
     "mgb_matmul_f32": ([_vp, _u64, _u64, _vp, _u64, _u64, _i32, _i32, _vp, _vp], _i32),
     "mgb_quantize_rows": ([_vp, _u64, _vp, _vp, _vp, _vp], _i32),
     "mgb_take_device_error": ([_i32, _i32p], _i32),
+    "mgb_embedding": ([_i32, _vp, _u64, _u64, _i32, _vp, _u64, _i32, ctypes.c_float, _vp, _vp, _vp],
+                      _i32),
     "mgb_device_alloc": ([_u64, ctypes.POINTER(_vp)], _i32),
     "mgb_device_free": ([_vp], _i32),
     "mgb_ipc_handle": ([_vp, _vp], _i32),
@@ -224,6 +227,14 @@ def dequantize(fmt: int, w_ptr: int, rows: int, cols: int, out_ptr: int, stream:
 def qmatmul_input_major(fmt: int, w_ptr: int, rows: int, cols: int, x_ptr: int, m: int,
                         y_ptr: int, stream: int = 0) -> None:
     check(lib().mgb_qmatmul_input_major(fmt, w_ptr, rows, cols, x_ptr, m, y_ptr, stream or None))
+
+
+def embedding(fmt: int, w_ptr: int, stored_rows: int, stored_cols: int, transposed: bool,
+              ids_ptr: int, count: int, out_ptr: int, scale: float | None = None, bad_ptr: int = 0,
+              stream: int = 0) -> None:
+    check(lib().mgb_embedding(fmt, w_ptr, stored_rows, stored_cols, int(transposed), ids_ptr,
+                              count, int(scale is not None), 1.0 if scale is None else scale,
+                              out_ptr, bad_ptr or None, stream or None))
 
 
 def take_device_error(device: int = 0) -> int:
@@ -455,9 +466,11 @@ class B200Provider:
     # execution
     def submit_kernel(self, kernel: str, inputs: list[str], output: str,
                       transpose_a: bool = False, transpose_b: bool = False,
-                      accumulation_dtype: int = 0, deadline_ms: int | None = None) -> int:
+                      accumulation_dtype: int = 0, deadline_ms: int | None = None,
+                      scale: float | None = None) -> int:
         attrs = KernelAttrs(int(transpose_a), int(transpose_b), accumulation_dtype,
-                            -1 if deadline_ms is None else deadline_ms)
+                            -1 if deadline_ms is None else deadline_ms, int(scale is not None),
+                            1.0 if scale is None else scale)
         arr = (ctypes.c_char_p * max(1, len(inputs)))(*[i.encode() for i in inputs])
         handle = ctypes.c_uint64(0)
         check(lib().mgb_submit_kernel(self._h, kernel.encode(), ctypes.byref(attrs), arr,
@@ -477,6 +490,16 @@ class B200Provider:
         return [{"sequence": arr[i].sequence, "kind": arr[i].kind,
                  "kernel": arr[i].kernel.decode(), "detail": arr[i].detail.decode()}
                 for i in range(written.value)]
+
+    def embedding(self, ids: np.ndarray, table_id: str, output: str = "__e",
+                  scale: float | None = None) -> np.ndarray:
+        """write the ids (f32), submit `embedding`, complete, read [count, dim]."""
+        self.write_tensor("__ids", np.asarray(ids, dtype=np.float32).reshape(-1))
+        h = self.submit_kernel("embedding", [table_id, "__ids"], output, scale=scale)
+        outcome = self.complete_kernel(h)
+        if not outcome.ok:
+            raise MgbError(outcome.status, outcome.reason)
+        return self.read_tensor(output)
 
     def matmul(self, x: np.ndarray, weight_id: str, output: str = "__y", **attrs) -> np.ndarray:
         """write x, submit `matmul`, complete, read y (a convenience for tests)."""

@@ -22,12 +22,12 @@ def test_library_exports_every_header_function():
 
 
 def test_identity_and_advertisements():
-    assert mgb.lib().mgb_abi_version() == 1
+    assert mgb.lib().mgb_abi_version() == 2
     md = mgb.metadata()
     assert md["name"] == "magnetar:provider/b200-native"
     assert md["name"] != "magnetar:provider/reference-cpu"
     ads = mgb.kernel_advertisements()
-    assert [a["name"] for a in ads] == ["matmul", "matmul-bias", "matmul-residual"]
+    assert [a["name"] for a in ads] == ["matmul", "matmul-bias", "matmul-residual", "embedding"]
     assert all(a["rank"] == 2 and a["cancellation"] == 1 for a in ads)
 
 
@@ -118,3 +118,14 @@ def test_tensor_parallel_outputs_are_checked_before_device_work():
     assert lib.mgb_tp_wait(fake, 0, 1, 0, None) == mgb.INVALID_ARGUMENT
     assert lib.mgb_ipc_open(None, None) == mgb.INVALID_ARGUMENT
     assert lib.mgb_device_alloc(16, None) == mgb.INVALID_ARGUMENT
+
+
+def test_embedding_arguments_are_checked_before_device_work():
+    lib = mgb.lib()
+    fake = 1 << 40
+    # a declined format, a ragged table, null pointers
+    assert lib.mgb_embedding(3, fake, 8, 256, 0, fake, 1, 0, 1.0, fake, None, None) == mgb.UNSUPPORTED
+    assert lib.mgb_embedding(mgb.Q4_K, fake, 8, 96, 0, fake, 1, 0, 1.0, fake, None, None) == \
+        mgb.INVALID_ARGUMENT
+    assert lib.mgb_embedding(mgb.Q8_0, None, 8, 64, 0, fake, 1, 0, 1.0, fake, None, None) == \
+        mgb.INVALID_ARGUMENT
