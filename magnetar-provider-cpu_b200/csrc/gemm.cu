@@ -25,10 +25,12 @@
 //   warps 3-10 dequantise the staged packed W into the bf16 B operand
 //              (K-major, SWIZZLE_128B written by hand), fence the async proxy
 //              and arrive on full[s] and p_empty[s]; after the last stage they
-//              drain TMEM with tcgen05.ld and write y (+ the addend): straight
-//              from registers for one output, through shared memory in whole
-//              row segments when every rank's y receives the tile (fused
-//              all-gather over NVLink).
+//              drain TMEM with tcgen05.ld and write y (+ the addend): for one
+//              output of wide tiles, 32 x 32 blocks staged SWIZZLE_128B in
+//              shared memory and written by TMA stores; otherwise straight from
+//              registers, or, when every rank's y receives the tile (fused
+//              all-gather over NVLink), through shared memory in whole row
+//              segments.
 // Every CTA loads its own tiles from this GPU's HBM (no cluster-shared loads).
 // Every wait is bounded; on expiry the kernel records ERR_WAIT_TIMEOUT, skips
 // the remaining work, waits (bounded) for its own copies and MMAs, frees TMEM
@@ -67,6 +69,7 @@ struct GemmParams {
   const float *addend;
   OutSpec out;          // y of this rank, or of every rank (fused all-gather)
   int vec_out;          // every output row start is 16-byte aligned: float4 stores
+  int tma_out;          // one output, no addend, 16-byte rows: TMA stores of 32x32 blocks
   int *err;
 };
 
@@ -152,6 +155,22 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float v[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+
+// ---- TMA stores (shared -> this GPU's global memory) -----------------------------------
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, int x, int y, const void *src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(smem_u32(src))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the shared-memory source of all but the newest `n` committed groups has been read
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // ---- dequantisation of one 32-value run into 64 bytes of bf16 ----------------------
 
@@ -320,11 +339,54 @@ __device__ __forceinline__ void dequant_run(const uint8_t *wq_row, const uint8_t
 // Several ranks: 32-column chunks go through a padded 32 x 33 square of
 // shared memory (`square`, this warp's own) so that the warp's stores cover
 // whole 128-byte row segments: full-size writes over NVLink.
-__device__ __forceinline__ void drain_accumulators(const GemmParams &p, uint32_t tmem_base,
+__device__ __forceinline__ void drain_accumulators(const GemmParams &p, const CUtensorMap *map_y,
+                                                   uint32_t tmem_base,
                                                    int nsub, int sub_stride, int row0, int n0,
                                                    int tile_cols, int quarter, int half, int lane,
                                                    float *square) {
   const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
+  if (p.tma_out) {
+    // 32 x 32 blocks: lane = row; written SWIZZLE_128B into one of this warp's
+    // two 4 KB buffers (16-byte chunk q of row r at r * 128 + ((q ^ (r & 7)) << 4))
+    // and stored by one TMA copy (rows past m, columns past n are clipped); a
+    // partial last block of the tile (tile_cols % 32) is stored directly
+    uint8_t *buf = reinterpret_cast<uint8_t *>(square);
+    int nb = 0;
+    for (int sub = 0; sub < nsub; ++sub) {
+      const int rb = row0 + sub * 128 + quarter * 32;
+      for (int c0 = 32 * half; c0 < tile_cols; c0 += 64) {
+        float v[32];
+        tmem_ld32(lane_base + (uint32_t)(sub * sub_stride + c0), v);
+        if (c0 + 32 <= tile_cols) {
+          uint8_t *b = buf + (nb & 1) * 4096;
+          if (lane == 0) bulk_wait_read<1>();  // the buffer's previous store has read it
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4 *>(b + lane * 128 + ((q ^ (lane & 7)) << 4)) =
+                make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(map_y, n0 + c0, rb, b);
+            bulk_commit();
+          }
+          ++nb;
+        } else {
+          const int row = rb + lane;
+          if (row < p.m) {
+            float *yr = p.out.y_ranks[0] + (size_t)row * p.out.ldy;
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (e < tile_cols - c0 && n0 + c0 + e < p.n) yr[n0 + c0 + e] = v[e];
+          }
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+    return;
+  }
   if (p.out.world == 1) {
     float *y = p.out.y_ranks[0];
     for (int sub = 0; sub < nsub; ++sub) {
@@ -407,7 +469,8 @@ __device__ __forceinline__ void grid_launch_dependents() {
 template <int FMT, int SUBS>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_wq,
-                const __grid_constant__ CUtensorMap map_ws, const GemmParams p) {
+                const __grid_constant__ CUtensorMap map_ws, const __grid_constant__ CUtensorMap map_y,
+                const GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte align the operand area (SWIZZLE_128B atoms).
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -582,8 +645,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // tcgen05.ld is warp-collective: the whole warp drains TMEM or none of it
     const bool drain = __all_sync(0xffffffffu, finished && !*(volatile int *)abort_flag);
     if (drain)
-      drain_accumulators(p, tmem_base, SUBS, 256, m0, n0, p.bn, warp & 3, (warp - 3) / 4, lane,
-                         reinterpret_cast<float *>(smem) + (warp - 3) * (32 * 33));
+      drain_accumulators(p, &map_y, tmem_base, SUBS, 256, m0, n0, p.bn, warp & 3, (warp - 3) / 4,
+                         lane, reinterpret_cast<float *>(smem + (size_t)(warp - 3) * 8192));
   }
   out_fence(p.out);
   tc_fence_before();
@@ -751,7 +814,7 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
     if (reinterpret_cast<uintptr_t>(out.y_ranks[r]) & 15) p.vec_out = 0;
   p.err = err;
 
-  CUtensorMap map_a, map_wq, map_ws;
+  CUtensorMap map_a, map_wq, map_ws, map_y;
   if (!make_map_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xb, k, m, k * 2, KSTEP, 128,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map_2d(&map_wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, L.qs_row, n, L.qs_row,
@@ -760,6 +823,13 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
                    static_cast<const uint8_t *>(w) + L.qs_bytes, L.sc_row, n, L.sc_row,
                    (uint32_t)p.wsw, (uint32_t)t.bn, CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
+  // one output, no addend, 16-byte rows: the epilogue stores 32 x 32 blocks by TMA
+  // (wide tiles only: for narrow ones the per-block waits outweigh the gain)
+  p.tma_out = out.world == 1 && addend_mode == 0 && p.vec_out && out.col0 == 0 && t.bn >= 192;
+  if (p.tma_out && !make_map_2d(&map_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, out.y_ranks[0], n, m,
+                                out.ldy * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B))
+    p.tma_out = 0;
+  if (!p.tma_out) map_y = map_a;  // unused
 
   const size_t smem = (size_t)sa * ab + (size_t)sp * p.pstage_bytes + 1024 + 512;
   cudaError_t e = cudaSuccess;
@@ -768,7 +838,8 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
     auto kern = KERN;                                                                          \
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \
     if (e != cudaSuccess) return e;                                                            \
-    e = launch_dependent(kern, grid, dim3(NUM_THREADS), smem, stream, map_a, map_wq, map_ws, p); \
+    e = launch_dependent(kern, grid, dim3(NUM_THREADS), smem, stream, map_a, map_wq, map_ws,     \
+                         map_y, p);                                                            \
   } while (0)
 #define MGB_GEMM_FMT(F)                                     \
   case F:                                                   \
