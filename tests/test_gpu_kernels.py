@@ -217,3 +217,19 @@ def test_nan_activation_reaches_its_row_only(torch_cuda, oracle, fmt, m):
     assert np.isnan(ref[0]).all()
     assert np.isnan(y[0]).all(), f"{np.isnan(y[0]).sum()} of {n} NaN in row 0"
     assert np.isfinite(y[1:]).all()
+
+
+@pytest.mark.parametrize("m,n,k", [(40, 28672, 256), (300, 14344, 256), (300, 14342, 256)])
+def test_gemm_wide_tile_epilogue_edges(torch_cuda, oracle, m, n, k):
+    """Wide tiles (bn >= 192) store 32x32 output blocks by TMA: rows past m and
+    columns past n are clipped by the tensor map, a tile's partial last block
+    (bn % 32) is stored directly, and an output row length that is not a
+    multiple of 4 floats takes the direct stores throughout."""
+    torch = torch_cuda
+    fmt = mgb.Q4_K
+    w = synthetic.packed_weights(fmt, n, k, seed=m + n)
+    x = synthetic.activations(m, k, seed=m)
+    wdev = _device_layout(torch, fmt, w, n, k)
+    y = _qmatmul(torch, fmt, wdev, n, k, x)
+    assert np.isfinite(y).all()
+    oracle.assert_close(y, oracle.packed_matmul(fmt, w, n, k, x), GEMM_TOL, f"gemm m {m} n {n}")
