@@ -59,6 +59,7 @@ struct GemmParams {
   int pstages;          // packed-W ring
   int qbytes;           // packed quant bytes per weight row per K step (32, 48 or 64)
   int wsw;              // scale-plane bytes per weight row per 256 values (16, 32 or 48)
+  int dq_groups;        // dequant warp groups taking K steps in turn (1, 2 or 4)
   uint32_t a_bytes;     // per activation stage
   uint32_t b_bytes;     // per W-tile stage
   uint32_t wq_bytes;    // per packed stage
@@ -499,13 +500,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   constexpr uint32_t TMEM_COLS = SUBS == 2 ? 512 : 256;
 
   if (threadIdx.x == 0) {
+    // each K step is dequantised by one group of DQ_WARPS / dq_groups warps
+    const int gw = DQ_WARPS / p.dq_groups;
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1 + DQ_WARPS);
+      mbar_init(&full[s], 1 + gw);
       mbar_init(&empty[s], 1);
     }
     for (int s = 0; s < SP; ++s) {
       mbar_init(&p_full[s], 1);
-      mbar_init(&p_empty[s], DQ_WARPS);
+      mbar_init(&p_empty[s], gw);
     }
     mbar_init(done, 1);
     *abort_flag = 0;
@@ -571,22 +574,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc = instr_desc_bf16(128, p.bn);
+      // The descriptors' start address is bits 0..13 (address >> 4) and every
+      // shared-memory address is below 256 KB: a stage's descriptors are the
+      // first stage's plus the offset >> 4, with no carry out of the field.
+      const uint64_t a_desc0 = smem_desc_sw128(smem_u32(a0));
+      const uint64_t b_desc0 = smem_desc_sw128(smem_u32(b0));
+      int s = 0, round = 0;
       for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % S;
-        if (!mbar_wait(&full[s], (kt / S) & 1, p.err)) {
+        if (!mbar_wait(&full[s], round & 1, p.err)) {
           *(volatile int *)abort_flag = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(a0 + (size_t)s * p.a_bytes);
-        const uint32_t b_addr = smem_u32(b0 + (size_t)s * p.b_bytes);
+        const uint64_t ad = a_desc0 + (((uint64_t)s * p.a_bytes) >> 4);
+        const uint64_t bd = b_desc0 + (((uint64_t)s * p.b_bytes) >> 4);
 #pragma unroll
         for (int sub = 0; sub < SUBS; ++sub)
 #pragma unroll
           for (int kk = 0; kk < KSTEP / 16; ++kk)
-            mma_bf16(tmem_base + sub * 256, smem_desc_sw128(a_addr + sub * 16384 + kk * 32),
-                     smem_desc_sw128(b_addr + kk * 32), idesc, (kt | kk) != 0);
+            mma_bf16(tmem_base + sub * 256, ad + (uint64_t)((sub * 16384 + kk * 32) >> 4),
+                     bd + (uint64_t)((kk * 32) >> 4), idesc, (kt | kk) != 0);
         mma_commit(&empty[s]);
+        if (++s == S) {
+          s = 0;
+          ++round;
+        }
       }
       mma_commit(done);  // arrives once every MMA issued above has completed
     }
@@ -604,8 +616,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
     const int items = p.bn * 2;  // (weight row, run) pairs per stage
+    // Narrow tiles have little dequantisation per step, and one warp's pass
+    // through a step (two barrier waits, the proxy fence, two arrivals) is
+    // what bounds them: the warps split into groups that take K steps in
+    // turn, so several steps are in flight.
+    const int gw = DQ_WARPS / p.dq_groups;
+    const int grp = (warp - 3) / gw;
+    const int gt = t - grp * gw * 32;  // thread index within the group
     bool ok = true;
-    for (int kt = 0; kt < KT && ok; ++kt) {
+    for (int kt = grp; kt < KT && ok; kt += p.dq_groups) {
       const int sb = kt % S, sp = kt % SP;
       if (*(volatile int *)abort_flag) break;
       // the stage is free once the MMAs of round (kt / S) - 1 released it, and
@@ -619,7 +638,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint8_t *bt = b0 + (size_t)sb * p.b_bytes;
       const uint8_t *wq = pk0 + (size_t)sp * p.pstage_bytes;
       const uint8_t *ws = wq + p.wq_bytes;
-      for (int it = t; it < items; it += DQ_THREADS) {
+      for (int it = gt; it < items; it += gw * 32) {
         const int row = it >> 1, j = it & 1;
         uint4 out[4];
         dequant_run<FMT>(wq + row * p.qbytes, ws + row * p.wsw, kt, j, lut, out);
@@ -799,10 +818,30 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
   // to 8).
   const uint32_t budget = 225 * 1024 - 1024 /*align slack*/ - 512 /*barriers*/;
   const uint32_t ab = p.a_bytes + p.b_bytes;
-  int sa = 2, sp = 3;
-  if (sa * ab + sp * p.pstage_bytes > budget) return cudaErrorInvalidValue;
-  while (sa < 6 && (sa + 1) * ab + sp * p.pstage_bytes <= budget) ++sa;
-  while (sp < 8 && sa * ab + (sp + 1) * p.pstage_bytes <= budget) ++sp;
+  // Dequant warp groups for narrow tiles (see the kernel).  A group waits on
+  // the slots of its own steps only, and an mbarrier parity wait cannot tell
+  // phase q from phase q - 2: so the previous use of every slot a group waits
+  // on must be a step that group waited on itself.  That holds for the packed
+  // ring when its depth is a multiple of the group count, and for the operand
+  // ring (released in K order by the MMA commits) when it is at least that deep.
+  auto fits = [&](int a, int q) { return (uint32_t)a * ab + (uint32_t)q * p.pstage_bytes <= budget; };
+  int groups = t.bn <= 64 ? 4 : t.bn <= 128 ? 2 : 1;
+  int sa = 2, sp = 2 * groups;
+  while (groups > 1) {
+    sp = 2 * groups;
+    sa = 2;
+    while (sa < 6 && fits(sa + 1, sp)) ++sa;
+    if (fits(sa, sp) && sa >= groups) break;
+    groups /= 2;
+  }
+  if (groups == 1) {
+    sa = 2;
+    sp = 3;
+    if (!fits(sa, sp)) return cudaErrorInvalidValue;
+    while (sa < 6 && fits(sa + 1, sp)) ++sa;
+    while (sp < 8 && fits(sa, sp + 1)) ++sp;
+  }
+  p.dq_groups = groups;
   p.astages = sa;
   p.bstages = sa;
   p.pstages = sp;
