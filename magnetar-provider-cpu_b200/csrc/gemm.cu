@@ -9,9 +9,9 @@
 // swizzle atom of bf16).  Two shared-memory rings: operand stages (the
 // activation tile and the bf16 W tile of a K step, 3 to 6 deep), each with one
 // `full` barrier (the activation TMA bytes + one arrival per dequantising
-// warp) and one `empty` barrier (the MMAs' commit), so the MMA issuer waits
-// and commits once per step; and packed-W stages (quant and scale boxes from
-// HBM, 3+ deep, released by the dequantising warps).  Launched as a
+// warp of the step) and one `empty` barrier (the MMAs' commit), so the MMA
+// issuer waits and commits once per step; and packed-W stages (quant and scale
+// boxes from HBM, 3+ deep, released by the dequantising warps).  Launched as a
 // programmatic dependent: everything but the activation loads (TMEM, barriers,
 // the weight stream, dequantisation) overlaps the previous kernel on the
 // stream.  Warp roles, 352 threads:
@@ -24,7 +24,8 @@
 //              swizzle) on p_full[s].
 //   warps 3-10 dequantise the staged packed W into the bf16 B operand
 //              (K-major, SWIZZLE_128B written by hand), fence the async proxy
-//              and arrive on full[s] and p_empty[s]; after the last stage they
+//              and arrive on full[s] and p_empty[s] (on narrow tiles as 2 or 4
+//              groups that take K steps in turn); after the last stage they
 //              drain TMEM with tcgen05.ld and write y (+ the addend): for one
 //              output of wide tiles, 32 x 32 blocks staged SWIZZLE_128B in
 //              shared memory and written by TMA stores; otherwise straight from
