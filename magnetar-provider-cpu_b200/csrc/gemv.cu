@@ -291,17 +291,20 @@ __device__ __forceinline__ float2 decode_run_scale(const uint8_t *srow, int uu) 
 // rows.  The rows' quant words and decoded factors are loaded first; the
 // integer dot products then run word by word across all rows, so 2 * RPT * MR
 // independent dp4a chains interleave instead of two per row.  Row i's quants
-// start at q + i * q_stride, its factors at dec[i * dec_stride].
+// start at q + i * q_stride, its scale-plane bytes at sc + i * sc_stride; its
+// factors are decoded here (`fused`) or were decoded earlier into
+// dec[i * dec_stride] (the stages that land before the dependency wait).
 template <int FMT, int MR, int RPT>
 __device__ __forceinline__ void rows_partials(const uint8_t *q, size_t q_stride, const float2 *dec,
                                               size_t dec_stride, int uu, const XRun (&x)[MR],
                                               const uint32_t lut[4], float (&part)[RPT * MR],
-                                              const uint8_t *sc = nullptr, size_t sc_stride = 0) {
+                                              const uint8_t *sc = nullptr, size_t sc_stride = 0,
+                                              bool fused = false) {
   int sh[RPT][MR], sl[RPT][MR];
   float2 sm[RPT];
 #pragma unroll
   for (int i = 0; i < RPT; ++i) {
-    sm[i] = dec[(size_t)i * dec_stride];
+    sm[i] = fused ? decode_run_scale<FMT>(sc + (size_t)i * sc_stride, uu) : dec[(size_t)i * dec_stride];
 #pragma unroll
     for (int m = 0; m < MR; ++m) sh[i][m] = sl[i][m] = 0;
   }
@@ -590,10 +593,7 @@ __global__ void __launch_bounds__(MAXT, MINB)
 
   for (int g = 0; g < nstages; ++g) {
     const int s = g % S;
-    if (g >= pre) {
-      wait_stage(g, 64);
-      decode_stage(g);
-    }
+    if (g >= pre) wait_stage(g, 64);  // (its run factors are decoded in rows_partials)
     const uint8_t *st = smem + (size_t)s * p.stage_bytes;
     const int row0 = r0 + g * TR;
     // branch-free over the team's RPT rows (rows past the end of a partial
@@ -603,7 +603,7 @@ __global__ void __launch_bounds__(MAXT, MINB)
     rows_partials<FMT, MR, RPT>(st + (size_t)team * RPT * L.qs_row, L.qs_row,
                                 dec + ((size_t)s * TR + team * RPT) * runs + uu, runs, uu, xr, lut,
                                 part, st + p.qs_stage_bytes + (size_t)team * RPT * L.sc_row,
-                                L.sc_row);
+                                L.sc_row, g >= pre);
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
       const bool keep = ok && active && row0 + team * RPT + i < r1;
