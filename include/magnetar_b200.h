@@ -264,8 +264,15 @@ uint64_t mgb_packed_bytes(int32_t format, uint64_t stored_rows, uint64_t stored_
  * device layout in `out` (device memory of mgb_packed_bytes bytes). */
 mgb_status mgb_repack(int32_t format, const void *ggml_blocks, uint64_t stored_rows,
                       uint64_t stored_cols, void *out, void *stream);
-/* Scratch bytes `mgb_qmatmul` needs for this shape (0 when none). */
+/* Scratch bytes `mgb_qmatmul` wants for this shape (0 when none): the bf16
+ * copy of x and, for m <= 128 rows with k % 512 == 0, two f32 [m, n] planes
+ * with which the tensor-core path splits K across twice as many CTAs and then
+ * sums the two halves (a different f32 summation order, same tolerance).
+ * Any workspace of at least mgb_qmatmul_min_workspace_bytes (the bf16 copy
+ * alone) also takes the tensor-core path, in one K pass; the tensor-parallel
+ * call (mgb_qmatmul_tp) always runs one K pass. */
 uint64_t mgb_qmatmul_workspace_bytes(int32_t format, uint64_t m, uint64_t n, uint64_t k);
+uint64_t mgb_qmatmul_min_workspace_bytes(int32_t format, uint64_t m, uint64_t n, uint64_t k);
 /* y[m, n] = x[m, k] * W^T on `stream`, W (device layout, 16-byte aligned)
  * with its n stored rows the output columns (`packed_matmul`,
  * src/native/mod.rs:109-152).  Device pointers.  `addend` (may be NULL) is added to y:

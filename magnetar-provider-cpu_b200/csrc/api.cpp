@@ -125,9 +125,17 @@ mgb_status run_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, co
   return MGB_OK;
 }
 
-// Scratch the dispatch above uses for m rows: the GEMM's bf16 activations
-// (the GEMV needs none).
+// Scratch the dispatch above uses for m rows: the GEMM's bf16 activations,
+// plus its split-K partial planes where those apply (the GEMV needs none).
 uint64_t qmatmul_scratch_bytes(int32_t format, uint64_t m, uint64_t n, uint64_t k) {
+  if (!format_supported(format)) return 0;
+  if (m > 2 && gemm_supported(format, m, n, k))
+    return gemm_workspace_bytes_preferred(format, m, n, k);
+  return 0;
+}
+
+// The least scratch with which the dispatch still takes the GEMM.
+uint64_t qmatmul_min_scratch_bytes(int32_t format, uint64_t m, uint64_t n, uint64_t k) {
   if (!format_supported(format)) return 0;
   if (m > 2 && gemm_supported(format, m, n, k)) return gemm_workspace_bytes(format, m, n, k);
   return 0;
@@ -197,6 +205,10 @@ mgb_status mgb_repack(int32_t format, const void *ggml_blocks, uint64_t stored_r
 
 uint64_t mgb_qmatmul_workspace_bytes(int32_t format, uint64_t m, uint64_t n, uint64_t k) {
   return qmatmul_scratch_bytes(format, m, n, k);
+}
+
+uint64_t mgb_qmatmul_min_workspace_bytes(int32_t format, uint64_t m, uint64_t n, uint64_t k) {
+  return qmatmul_min_scratch_bytes(format, m, n, k);
 }
 
 mgb_status mgb_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, const float *x,

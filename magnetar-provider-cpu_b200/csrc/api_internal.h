@@ -25,6 +25,7 @@ int *device_error_flag(int device);
 mgb_status validate_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, const float *x,
                             uint64_t m, float *y);
 uint64_t qmatmul_scratch_bytes(int32_t format, uint64_t m, uint64_t n, uint64_t k);
+uint64_t qmatmul_min_scratch_bytes(int32_t format, uint64_t m, uint64_t n, uint64_t k);
 // y = x W^T (+ addend) written where `out` says: one rank's y[m, n] or, for a
 // tensor-parallel call, columns col0.. of every rank's y[m, ldy].
 mgb_status run_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, const float *x,

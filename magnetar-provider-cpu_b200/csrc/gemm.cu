@@ -61,6 +61,7 @@ struct GemmParams {
   int qbytes;           // packed quant bytes per weight row per K step (32, 48 or 64)
   int wsw;              // scale-plane bytes per weight row per 256 values (16, 32 or 48)
   int dq_groups;        // dequant warp groups taking K steps in turn (1, 2 or 4)
+  int ksplit;           // K halves computed by separate CTAs (blockIdx.z), summed after
   uint32_t a_bytes;     // per activation stage
   uint32_t b_bytes;     // per W-tile stage
   uint32_t wq_bytes;    // per packed stage
@@ -390,7 +391,8 @@ __device__ __forceinline__ void drain_accumulators(const GemmParams &p, const CU
     return;
   }
   if (p.out.world == 1) {
-    float *y = p.out.y_ranks[0];
+    // (a split-K CTA writes its partial sums: plane blockIdx.z of [ksplit][m][ldy])
+    float *y = p.out.y_ranks[0] + (size_t)blockIdx.z * p.m * p.out.ldy;
     for (int sub = 0; sub < nsub; ++sub) {
       const int row = row0 + sub * 128 + quarter * 32 + lane;
       for (int c = 8 * half; c < tile_cols; c += 16) {
@@ -497,7 +499,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * p.bn;
   const int m0 = blockIdx.y * (128 * SUBS);
-  const int KT = p.k / KSTEP;
+  const int KT = p.k / KSTEP / p.ksplit;   // this CTA's K steps
+  const int kt0 = (int)blockIdx.z * KT;    // its first K step
   constexpr uint32_t TMEM_COLS = SUBS == 2 ? 512 : 256;
 
   if (threadIdx.x == 0) {
@@ -545,7 +548,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint8_t *st = a0 + (size_t)s * p.a_bytes;
         mbar_arrive_expect_tx(&full[s], p.a_bytes);
         for (int sub = 0; sub < SUBS; ++sub)
-          tma_load_2d(st + sub * 16384, &map_a, kt * KSTEP, m0 + sub * 128, &full[s]);
+          tma_load_2d(st + sub * 16384, &map_a, (kt0 + kt) * KSTEP, m0 + sub * 128, &full[s]);
       }
       // (every activation copy has landed before the MMAs that read it, and
       // the epilogue waits for those)
@@ -564,8 +567,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (*(volatile int *)abort_flag) break;
         uint8_t *st = pk0 + (size_t)s * p.pstage_bytes;
         mbar_arrive_expect_tx(&p_full[s], p.ptx_bytes);
-        tma_load_2d(st, &map_wq, kt * p.qbytes, n0, &p_full[s]);
-        tma_load_2d(st + p.wq_bytes, &map_ws, (kt / 4) * p.wsw, n0, &p_full[s]);
+        tma_load_2d(st, &map_wq, (kt0 + kt) * p.qbytes, n0, &p_full[s]);
+        tma_load_2d(st + p.wq_bytes, &map_ws, ((kt0 + kt) / 4) * p.wsw, n0, &p_full[s]);
         issued = kt + 1;
       }
       for (int kt = (issued > SP ? issued - SP : 0); kt < issued; ++kt)
@@ -642,7 +645,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int it = gt; it < items; it += gw * 32) {
         const int row = it >> 1, j = it & 1;
         uint4 out[4];
-        dequant_run<FMT>(wq + row * p.qbytes, ws + row * p.wsw, kt, j, lut, out);
+        dequant_run<FMT>(wq + row * p.qbytes, ws + row * p.wsw, kt0 + kt, j, lut, out);
         uint8_t *dst_row = bt + row * 128;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -697,6 +700,24 @@ __global__ void f32_to_bf16_kernel(const float *__restrict__ x, __nv_bfloat16 *_
     o.x = pack_bf16(v.x, v.y);
     o.y = pack_bf16(v.z, v.w);
     reinterpret_cast<uint2 *>(out)[i] = o;
+  }
+}
+
+// Split-K: y = the partial planes summed in plane order (+ the addend); a
+// programmatic dependent of the GEMM that wrote them.
+__global__ void splitk_sum_kernel(const float *__restrict__ part, int planes, uint64_t m,
+                                  uint64_t n, float *__restrict__ y,
+                                  const float *__restrict__ addend, int addend_mode) {
+  grid_launch_dependents();
+  grid_dependency_wait();
+  const uint64_t total = m * n;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    float v = part[i];
+    for (int z = 1; z < planes; ++z) v = v + part[z * total + i];
+    if (addend_mode == 1) v = v + addend[i % n];
+    else if (addend_mode == 2) v = v + addend[i];
+    y[i] = v;
   }
 }
 
@@ -766,10 +787,43 @@ uint64_t gemm_workspace_bytes(int, uint64_t m, uint64_t, uint64_t k) {
   return ceil_div(m * k * 2, 256) * 256;
 }
 
+// Split-K for up to 128 activation rows.  A K step of a tile up to ~96
+// columns wide costs about the same (its barriers and the dequantising warps'
+// latency, not its MMAs or its bytes), so where one wave of tiles leaves them
+// that narrow, s CTAs per tile (s = 2 or 4) each take 1/s of K over s-times-
+// wider tiles and a sum pass adds the s partial planes.  s is the largest that
+// keeps tiles at most 112 columns wide, whole 256-value blocks per part, and
+// one wave.
+static int choose_split(uint64_t m, uint64_t n, uint64_t k, int sms) {
+  int best = 1;
+  if (m > 128) return best;
+  for (int s = 2; s <= 4; s *= 2) {
+    if (k % (256ull * s) != 0 || sms / s < 1) break;
+    const TileChoice t = choose_tiles(m, n, sms / s);
+    if (t.bn > 112 || (uint64_t)s * ceil_div(n, (uint64_t)t.bn) > (uint64_t)sms) break;
+    best = s;
+  }
+  return best;
+}
+
+// B200's SM count: the size a caller is told to provide (a launch on a device
+// with fewer SMs splits less when the workspace is short).
+constexpr int kB200Sms = 148;
+
+uint64_t gemm_workspace_bytes_preferred(int fmt, uint64_t m, uint64_t n, uint64_t k) {
+  const uint64_t base = gemm_workspace_bytes(fmt, m, n, k);
+  const int s = choose_split(m, n, k, kB200Sms);
+  return s > 1 ? base + (uint64_t)s * m * n * 4 : base;
+}
+
 bool gemm_supported(int fmt, uint64_t m, uint64_t n, uint64_t k) {
   return supported(fmt) && m >= 1 && n >= 1 && k % 256 == 0 && k >= 256 && m < (1u << 30) &&
          n < (1u << 30) && k < (1u << 24);
 }
+
+cudaError_t launch_gemm_core(int fmt, const void *w, uint64_t n, uint64_t k, const void *xb,
+                             uint64_t m, const OutSpec &out, const float *addend, int addend_mode,
+                             int *err, int sms, cudaStream_t stream, int ksplit);
 
 cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const float *x, uint64_t m,
                         const OutSpec &out, const float *addend, int addend_mode, void *workspace,
@@ -789,17 +843,41 @@ cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const fl
   e = launch_dependent(f32_to_bf16_kernel, dim3((unsigned)blocks), dim3(256), 0,
                                    stream, x, xb, m * k);
   if (e != cudaSuccess) return e;
-  return launch_gemm_bf16(fmt, w, n, k, xb, m, out, addend, addend_mode, err, sms, stream);
+  // one output and room for the partial planes: split K
+  const uint64_t base = gemm_workspace_bytes(fmt, m, n, k);
+  int s = out.world == 1 ? choose_split(m, n, k, sms) : 1;
+  while (s > 1 && workspace_bytes < base + (uint64_t)s * m * n * 4) s /= 2;
+  if (s > 1) {
+    float *part = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + base);
+    e = launch_gemm_core(fmt, w, n, k, xb, m, plain_out(part, n), nullptr, 0, err, sms, stream, s);
+    if (e == cudaSuccess) {
+      uint64_t sblocks = ceil_div(m * n, 256);
+      if (sblocks > (uint64_t)sms * 8) sblocks = (uint64_t)sms * 8;
+      e = launch_dependent(splitk_sum_kernel, dim3((unsigned)sblocks), dim3(256), 0, stream,
+                           (const float *)part, s, m, n, out.y_ranks[0], addend, addend_mode);
+    }
+    return e;
+  }
+  return launch_gemm_core(fmt, w, n, k, xb, m, out, addend, addend_mode, err, sms, stream, 1);
 }
 
 cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, const void *xb,
                              uint64_t m, const OutSpec &out, const float *addend, int addend_mode,
                              int *err, int sms, cudaStream_t stream) {
+  return launch_gemm_core(fmt, w, n, k, xb, m, out, addend, addend_mode, err, sms, stream, 1);
+}
+
+// The GEMM kernel launch; ksplit = 2 or 4 writes the K parts' partial sums
+// into planes 0 .. ksplit-1 of out (one output, ldy = n, no addend).
+cudaError_t launch_gemm_core(int fmt, const void *w, uint64_t n, uint64_t k, const void *xb,
+                             uint64_t m, const OutSpec &out, const float *addend, int addend_mode,
+                             int *err, int sms, cudaStream_t stream, int ksplit) {
   if (!gemm_supported(fmt, m, n, k) || (reinterpret_cast<uintptr_t>(w) & 15) ||
-      (reinterpret_cast<uintptr_t>(xb) & 15))
+      (reinterpret_cast<uintptr_t>(xb) & 15) || (ksplit != 1 && ksplit != 2 && ksplit != 4) ||
+      k % (256ull * ksplit) != 0 || (ksplit > 1 && (out.world != 1 || addend_mode != 0)))
     return cudaErrorInvalidValue;
   const Layout L(fmt, n, k);
-  const TileChoice t = choose_tiles(m, n, sms);
+  const TileChoice t = choose_tiles(m, n, ksplit > 1 ? sms / ksplit : sms);
   GemmParams p = {};
   p.m = (int)m;
   p.n = (int)n;
@@ -813,7 +891,9 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
   p.ws_bytes = (uint32_t)ceil_div((uint64_t)t.bn * p.wsw, 1024) * 1024;
   p.pstage_bytes = p.wq_bytes + p.ws_bytes;
   p.ptx_bytes = (uint32_t)t.bn * (uint32_t)(p.qbytes + p.wsw);
-  const dim3 grid((unsigned)ceil_div(n, (uint64_t)t.bn), (unsigned)ceil_div(m, 128ull * t.subs));
+  const dim3 grid((unsigned)ceil_div(n, (uint64_t)t.bn), (unsigned)ceil_div(m, 128ull * t.subs),
+                  (unsigned)ksplit);
+  p.ksplit = ksplit;
   // Narrow tiles (few weight rows per CTA) run their K loop faster with more
   // operand stages in flight: as many as fit (up to 6), then packed stages (up
   // to 8).
@@ -865,7 +945,8 @@ cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, con
     return cudaErrorInvalidValue;
   // one output, no addend, 16-byte rows: the epilogue stores 32 x 32 blocks by TMA
   // (wide tiles only: for narrow ones the per-block waits outweigh the gain)
-  p.tma_out = out.world == 1 && addend_mode == 0 && p.vec_out && out.col0 == 0 && t.bn >= 192;
+  p.tma_out = out.world == 1 && addend_mode == 0 && p.vec_out && out.col0 == 0 && t.bn >= 192 &&
+              ksplit == 1;
   if (p.tma_out && !make_map_2d(&map_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, out.y_ranks[0], n, m,
                                 out.ldy * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B))
     p.tma_out = 0;

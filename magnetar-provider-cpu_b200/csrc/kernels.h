@@ -33,7 +33,10 @@ cudaError_t launch_gemv(int fmt, const void *w, uint64_t n, uint64_t k, const fl
                         int *err, int sms, cudaStream_t stream);
 
 // gemm.cu: tensor-core path (bf16 operands, f32 accumulation) for m > 2.
+// The minimum scratch is the bf16 activation copy; the preferred size adds two
+// f32 [m, n] planes with which a single-output call of m <= 128 splits K.
 uint64_t gemm_workspace_bytes(int fmt, uint64_t m, uint64_t n, uint64_t k);
+uint64_t gemm_workspace_bytes_preferred(int fmt, uint64_t m, uint64_t n, uint64_t k);
 bool gemm_supported(int fmt, uint64_t m, uint64_t n, uint64_t k);
 cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const float *x,
                         uint64_t m, const OutSpec &out, const float *addend, int addend_mode,

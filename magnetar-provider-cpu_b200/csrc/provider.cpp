@@ -291,10 +291,10 @@ mgb_status run_matmul(mgb_provider *p, const std::string &kernel, const mgb_kern
                   (unsigned long long)k, (unsigned long long)w.stored_cols);
     s = ensure_buf(p, product, m * n * 4);
     if (s != MGB_OK) return s;
-    // scratch for the GEMM's bf16 activations
+    // scratch for the GEMM's bf16 activations (and its split-K partials)
     uint64_t ws = qmatmul_scratch_bytes(w.format, m, n, k);
     if (gemm_supported(w.format, m, n, k) && kernel_pref == MGB_KERNEL_GEMM)
-      ws = gemm_workspace_bytes(w.format, m, n, k);
+      ws = gemm_workspace_bytes_preferred(w.format, m, n, k);
     if (kernel_pref == MGB_KERNEL_GEMV) ws = 0;
     if (ws) {
       s = ensure_workspace(p, ws);

@@ -55,7 +55,7 @@ extern "C" mgb_status mgb_qmatmul_static_scratch(int32_t format, const void *w, 
                      (unsigned long long)addend_len, (unsigned long long)n,
                      (unsigned long long)(m * n));
   }
-  const uint64_t need = qmatmul_scratch_bytes(format, m, n, k);
+  const uint64_t need = qmatmul_min_scratch_bytes(format, m, n, k);
   if (need > MGB_STATIC_SCRATCH_BYTES)
     return fail(MGB_INVALID_ARGUMENT,
                 "m=%llu x k=%llu needs %llu bytes of scratch; the static scratch holds %llu "

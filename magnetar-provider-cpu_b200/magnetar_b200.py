@@ -133,6 +133,7 @@ _SIGNATURES = {
     "mgb_packed_bytes": ([_i32, _u64, _u64], _u64),
     "mgb_repack": ([_i32, _vp, _u64, _u64, _vp, _vp], _i32),
     "mgb_qmatmul_workspace_bytes": ([_i32, _u64, _u64, _u64], _u64),
+    "mgb_qmatmul_min_workspace_bytes": ([_i32, _u64, _u64, _u64], _u64),
     "mgb_qmatmul": ([_i32, _vp, _u64, _u64, _vp, _u64, _vp, _vp, _u64, _vp, _u64, _vp], _i32),
     "mgb_qmatmul_static_scratch": ([_i32, _vp, _u64, _u64, _vp, _u64, _vp, _vp, _u64, _vp],
                                    _i32),
@@ -205,6 +206,10 @@ def repack(fmt: int, ggml_ptr: int, rows: int, cols: int, out_ptr: int, stream: 
 
 def qmatmul_workspace_bytes(fmt: int, m: int, n: int, k: int) -> int:
     return int(lib().mgb_qmatmul_workspace_bytes(fmt, m, n, k))
+
+
+def qmatmul_min_workspace_bytes(fmt: int, m: int, n: int, k: int) -> int:
+    return int(lib().mgb_qmatmul_min_workspace_bytes(fmt, m, n, k))
 
 
 def qmatmul(fmt: int, w_ptr: int, n: int, k: int, x_ptr: int, m: int, y_ptr: int,

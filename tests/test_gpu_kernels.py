@@ -41,11 +41,13 @@ def _device_layout(torch, fmt, ggml: np.ndarray, rows: int, cols: int):
     return out
 
 
-def _qmatmul(torch, fmt, wdev, n, k, x: np.ndarray, addend: np.ndarray | None = None):
+def _qmatmul(torch, fmt, wdev, n, k, x: np.ndarray, addend: np.ndarray | None = None,
+             min_workspace: bool = False):
     m = x.shape[0]
     xd = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).cuda()
     yd = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
-    ws_bytes = mgb.qmatmul_workspace_bytes(fmt, m, n, k)
+    ws_bytes = (mgb.qmatmul_min_workspace_bytes if min_workspace
+                else mgb.qmatmul_workspace_bytes)(fmt, m, n, k)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
     ad = None
     if addend is not None:
@@ -168,6 +170,40 @@ def test_gemm_config1_sampled_columns(torch_cuda, oracle):
     assert err > 0  # bf16 operands do round
     y2 = _qmatmul(torch, fmt, wdev, n, k, x)
     assert np.array_equal(y, y2), "GEMM is deterministic (no split-K atomics)"
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("m,n,k,parts", [(3, 300, 1024, 4), (64, 8192, 4096, 2),
+                                         (128, 1001, 2048, 4), (17, 64, 14336, 4),
+                                         (8, 512, 1536, 2), (64, 14336, 4096, 1)])
+def test_gemm_split_k(torch_cuda, oracle, fmt, m, n, k, parts):
+    """With the preferred workspace a call of m <= 128 rows whose one-wave
+    tiles are narrow splits K over 2 or 4 CTAs per tile and sums the parts in
+    a fixed order: the result is deterministic and matches the oracle, and the
+    one-pass call (minimum workspace) to within the same tolerance."""
+    torch = torch_cuda
+    planes = 0 if parts == 1 else parts
+    assert mgb.qmatmul_workspace_bytes(fmt, m, n, k) == \
+        mgb.qmatmul_min_workspace_bytes(fmt, m, n, k) + planes * m * n * 4
+    w = synthetic.packed_weights(fmt, n, k, seed=m + k)
+    x = synthetic.activations(m, k, seed=n)
+    wdev = _device_layout(torch, fmt, w, n, k)
+    y = _qmatmul(torch, fmt, wdev, n, k, x)
+    assert np.isfinite(y).all()
+    assert np.array_equal(y, _qmatmul(torch, fmt, wdev, n, k, x)), "deterministic"
+    one = _qmatmul(torch, fmt, wdev, n, k, x, min_workspace=True)
+    oracle.assert_close(y, one, GEMM_TOL, f"split vs one pass fmt {fmt} m {m} n {n}")
+    cols = np.unique(np.concatenate([np.linspace(0, n - 1, 64).astype(np.int64),
+                                     np.arange(max(0, n - 8), n)]))
+    ref = oracle.packed_matmul(fmt, synthetic.row_slice(fmt, w, k, cols), len(cols), k, x)
+    oracle.assert_close(y[:, cols], ref, GEMM_TOL, f"split K fmt {fmt} m {m} n {n} k {k}")
+    # the sum pass adds a bias row or a residual after the halves
+    bias = np.linspace(-2, 2, n, dtype=np.float32)
+    yb = _qmatmul(torch, fmt, wdev, n, k, x, bias)
+    assert np.array_equal(yb, (y + bias).astype(np.float32))
+    res = synthetic.activations(m, n, seed=k)
+    yr = _qmatmul(torch, fmt, wdev, n, k, x, res)
+    assert np.array_equal(yr, (y + res).astype(np.float32))
 
 
 @pytest.mark.parametrize("m", [1, 2, 64])

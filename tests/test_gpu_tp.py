@@ -49,10 +49,11 @@ def _device_layout(torch, fmt, ggml, rows, cols):
 
 
 def _unsharded(torch, fmt, w, n, k, xd):
+    # the minimum workspace: one K pass, as every tensor-parallel call runs
     m = xd.shape[0]
     wd = _device_layout(torch, fmt, w, n, k)
     y = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
-    ws_bytes = mgb.qmatmul_workspace_bytes(fmt, m, n, k)
+    ws_bytes = mgb.qmatmul_min_workspace_bytes(fmt, m, n, k)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
     mgb.qmatmul(fmt, wd.data_ptr(), n, k, xd.data_ptr(), m, y.data_ptr(),
                 workspace_ptr=ws.data_ptr(), workspace_bytes=ws_bytes,
