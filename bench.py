@@ -22,6 +22,10 @@ over one batch.  Metric: TFLOP/s (2*M*N*K per step), whole job.
   IQ4_NL, Q4_0) at config 2's K=4096, N=14336: decode GEMV (M=1) weight GB/s and the
   prefill step (M=512) TFLOP/s, each over a CUDA graph of back-to-back
   launches on rotating weight copies (--no-formats skips it).
+- stacks (one GPU): config 3, the Llama-3-8B decode stack (32 layers of
+  Wq/Wk/Wv/Wo/gate/up/down, Q4_K) at M = 1, 16, 64, and config 4, the
+  Llama-3-70B layers (80 layers) at M = 1 and 2048: one CUDA graph per pass
+  over every layer's own weights; weight GB/s and TFLOP/s (--no-stacks skips).
 - cpu_baseline: the reference's own CPU path (int8 activations, AVX2 kernels,
   persistent pool), restated in C (oracle/cpu_baseline.c), on a sample of
   the same workload, on every host core.
@@ -447,6 +451,77 @@ def run_b200(args) -> None:
                                  "prefill_tflops": 2.0 * M * N * K / (p_ms * 1e-3) / 1e12,
                                  "device_bytes": vb}
 
+    def stack(shapes: list[tuple[int, int]], layers: int, m: int) -> dict:
+        """Configs 3 and 4: `layers` layers of Q4_K projections, `shapes` =
+        (n, k) per projection in order, one `mgb_qmatmul` each (M activation
+        rows), captured as one CUDA graph; every layer holds its own device
+        copy of each weight (one host-generated matrix per shape, repacked,
+        then copied on the device), so a pass streams all layers' weights."""
+        per_shape = {}
+        for (n, k) in sorted(set(shapes)):
+            src = torch.from_numpy(synthetic.packed_weights(fmt, n, k, seed=n + k)).to(dev)
+            b = torch.empty(mgb.packed_bytes(fmt, n, k), dtype=torch.uint8, device=dev)
+            mgb.repack(fmt, src.data_ptr(), n, k, b.data_ptr(), sp)
+            per_shape[(n, k)] = b
+            del src
+        layer_w = [[per_shape[s].clone() for s in shapes] for _ in range(layers)]
+        del per_shape
+        xs = {k: torch.from_numpy(synthetic.activations(m, k, seed=k)).to(dev)
+              for k in sorted({k for _, k in shapes})}
+        ys = {n: torch.empty((m, n), dtype=torch.float32, device=dev)
+              for n in sorted({n for n, _ in shapes})}
+        ws_bytes = max(mgb.qmatmul_workspace_bytes(fmt, m, n, k) for n, k in shapes)
+        ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+
+        def one_pass(s: int) -> None:
+            for lw in layer_w:
+                for (n, k), w in zip(shapes, lw):
+                    mgb.qmatmul(fmt, w.data_ptr(), n, k, xs[k].data_ptr(), m, ys[n].data_ptr(),
+                                workspace_ptr=ws.data_ptr(), workspace_bytes=ws_bytes, stream=s)
+
+        cap = torch.cuda.Stream(device=dev)
+        graph = torch.cuda.CUDAGraph()
+        cap.wait_stream(stream)
+        with torch.cuda.stream(cap):
+            one_pass(cap.cuda_stream)  # warm the launch path outside capture
+            with torch.cuda.graph(graph, stream=cap):
+                one_pass(torch.cuda.current_stream().cuda_stream)
+        stream.wait_stream(cap)
+        probe = timed_local(lambda _i: graph.replay(), 1, 1)
+        reps = int(max(2, min(50, 1000.0 / max(probe, 1e-3))))  # about a second
+        pass_ms = timed_local(lambda _i: graph.replay(), reps, 2) / reps
+        del graph
+        wbytes = layers * sum(mgb.packed_bytes(fmt, n, k) for n, k in shapes)
+        flops = 2.0 * m * layers * sum(n * k for n, k in shapes)
+        gbs = wbytes / (pass_ms * 1e-3) / 1e9
+        tfl = flops / (pass_ms * 1e-3) / 1e12
+        out = {"m": m, "ms_per_pass": pass_ms, "tokens_per_s": m / (pass_ms * 1e-3),
+               "weight_bytes": wbytes, "weight_gbs": gbs, "frac_hbm": gbs / pk["hbm_gbs"],
+               "tflops": tfl, "frac_bf16": tfl / pk["bf16_tflops_sustained"],
+               "launches_per_pass": layers * len(shapes), "replays": reps}
+        del layer_w, xs, ys, ws
+        torch.cuda.empty_cache()
+        return out
+
+    # configs 3 and 4 on one GPU: whole projection stacks, one graph per pass
+    stacks = None
+    if rank == 0 and world == 1 and not args.no_stacks:
+        l8 = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096),
+              (14336, 4096), (4096, 14336)]
+        l70 = [(8192, 8192), (1024, 8192), (1024, 8192), (8192, 8192), (28672, 8192),
+               (28672, 8192), (8192, 28672)]
+        stacks = {
+            "config3": {"workload": "Llama-3-8B decode stack: 32 layers x {Wq, Wk, Wv, Wo, "
+                                    "gate, up, down}, Q4_K, random weights",
+                        "passes": [stack(l8, 32, mm) for mm in (1, 16, 64)]},
+            "config4": {"workload": "Llama-3-70B layers: 80 layers x {Wq, Wk, Wv, Wo, gate, "
+                                    "up, down}, Q4_K, random weights",
+                        "passes": [stack(l70, 80, mm) for mm in (1, 2048)]},
+            "peaks": "frac_hbm of the measured HBM copy, frac_bf16 of the measured "
+                     "sustained bf16 (a pass is a long step)",
+            "timing": "CUDA events around replays of one CUDA graph holding one pass "
+                      "(every projection of every layer once; weights far above L2)"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(steps=10, warmup=1)
@@ -466,7 +541,7 @@ def run_b200(args) -> None:
                                       "mgb_tp_wait)" if world > 1 else "")},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": (3 if world > 1 else 2) * args.steps, "clocks": clocks,
-                "gemv": gemv, "formats": formats, "tp_baseline_nccl": nccl}
+                "gemv": gemv, "formats": formats, "stacks": stacks, "tp_baseline_nccl": nccl}
         print(json.dumps(line), flush=True)
     if op is not None:
         op.close()
@@ -483,6 +558,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-formats", action="store_true", help="skip the per-format table")
+    ap.add_argument("--no-stacks", action="store_true",
+                    help="skip the config-3/4 projection stacks (one GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

@@ -48,9 +48,13 @@ namespace mgb {
 namespace {
 
 constexpr int KSTEP = 64;                    // bf16 values per 128-byte row of a stage
-constexpr int DQ_WARPS = 8;                  // warps 3..10: dequantise, then the epilogue
-constexpr int DQ_THREADS = 32 * DQ_WARPS;
-constexpr int NUM_THREADS = 96 + DQ_THREADS;
+// warps 3 .. 3 + DQW - 1 dequantise, then run the epilogue: DQW = 8 for
+// 256-row tiles (there the dequantisation competes with the MMAs for shared
+// memory) and for the two-CTAs-per-SM split-K kernel, 16 for other 128-row
+// tiles (up to 128 activation rows: the weight stream is the work)
+constexpr int dq_warps_for(int subs, bool dual) { return subs == 2 || dual ? 8 : 16; }
+constexpr int EPI_SQUARE_BYTES = 4352;  // a warp's 32 x 33 f32 square, rounded up
+constexpr int EPI_TMA_BYTES = 8192;     // a warp's two 4 KB TMA-store buffers
 
 struct GemmParams {
   int m, n, k;
@@ -141,6 +145,17 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float v[8]) {
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 8 columns summed over `accs` accumulators `stride` columns apart.
+__device__ __forceinline__ void tmem_ld8_sum(uint32_t taddr, int accs, uint32_t stride, float v[8]) {
+  tmem_ld8(taddr, v);
+  if (accs == 2) {
+    float w[8];
+    tmem_ld8(taddr + stride, w);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = v[i] + w[i];
+  }
+}
+
 // 32 consecutive columns of this warp's 32 TMEM lanes: lane i gets row i.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float v[32]) {
   uint32_t r[32];
@@ -157,6 +172,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float v[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_ld32_sum(uint32_t taddr, int accs, uint32_t stride,
+                                              float v[32]) {
+  tmem_ld32(taddr, v);
+  if (accs == 2) {
+    float w[32];
+    tmem_ld32(taddr + stride, w);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = v[i] + w[i];
+  }
 }
 
 // ---- TMA stores (shared -> this GPU's global memory) -----------------------------------
@@ -334,9 +360,11 @@ __device__ __forceinline__ void dequant_run(const uint8_t *wq_row, const uint8_t
 // ---- epilogue ------------------------------------------------------------------------
 
 // Drains this warp's 32 TMEM lanes (lane quarter `quarter`) of `nsub`
-// accumulator blocks into y.  Block b holds output rows row0 + 128 b + 32
+// accumulator blocks into y; with accs == 2 each block is the sum of two
+// accumulators 256 columns apart (even and odd K slices).  Block b holds output rows row0 + 128 b + 32
 // quarter + lane at TMEM columns b * sub_stride + c for tile columns c <
-// tile_cols (output columns n0 + c); `half` picks this warp's alternate
+// tile_cols (output columns n0 + c); `half` (0 .. parts-1) picks this warp's
+// share of the column chunks, taken in turn by the `parts` warps of a quarter
 // column chunks (two warps per quarter).  One output rank: each lane stores
 // its row's 8-column pieces directly (the L2 merges the warp's row segments).
 // Several ranks: 32-column chunks go through a padded 32 x 33 square of
@@ -345,7 +373,8 @@ __device__ __forceinline__ void dequant_run(const uint8_t *wq_row, const uint8_t
 __device__ __forceinline__ void drain_accumulators(const GemmParams &p, const CUtensorMap *map_y,
                                                    uint32_t tmem_base,
                                                    int nsub, int sub_stride, int row0, int n0,
-                                                   int tile_cols, int quarter, int half, int lane,
+                                                   int tile_cols, int quarter, int half, int parts,
+                                                   int accs, int lane,
                                                    float *square) {
   const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
   if (p.tma_out) {
@@ -357,9 +386,9 @@ __device__ __forceinline__ void drain_accumulators(const GemmParams &p, const CU
     int nb = 0;
     for (int sub = 0; sub < nsub; ++sub) {
       const int rb = row0 + sub * 128 + quarter * 32;
-      for (int c0 = 32 * half; c0 < tile_cols; c0 += 64) {
+      for (int c0 = 32 * half; c0 < tile_cols; c0 += 32 * parts) {
         float v[32];
-        tmem_ld32(lane_base + (uint32_t)(sub * sub_stride + c0), v);
+        tmem_ld32_sum(lane_base + (uint32_t)(sub * sub_stride + c0), accs, 256, v);
         if (c0 + 32 <= tile_cols) {
           uint8_t *b = buf + (nb & 1) * 4096;
           if (lane == 0) bulk_wait_read<1>();  // the buffer's previous store has read it
@@ -395,9 +424,9 @@ __device__ __forceinline__ void drain_accumulators(const GemmParams &p, const CU
     float *y = p.out.y_ranks[0] + (size_t)blockIdx.z * p.m * p.out.ldy;
     for (int sub = 0; sub < nsub; ++sub) {
       const int row = row0 + sub * 128 + quarter * 32 + lane;
-      for (int c = 8 * half; c < tile_cols; c += 16) {
+      for (int c = 8 * half; c < tile_cols; c += 8 * parts) {
         float v[8];
-        tmem_ld8(lane_base + (uint32_t)(sub * sub_stride + c), v);
+        tmem_ld8_sum(lane_base + (uint32_t)(sub * sub_stride + c), accs, 256, v);
         if (row >= p.m) continue;
         const int col = n0 + c;
         float *yr = y + (size_t)row * p.out.ldy + p.out.col0;
@@ -422,9 +451,9 @@ __device__ __forceinline__ void drain_accumulators(const GemmParams &p, const CU
   const int sub_lane = lane >> 3, c4 = (lane & 7) * 4;  // store lanes: 4 rows x 8 float4
   for (int sub = 0; sub < nsub; ++sub) {
     const int rbase = row0 + sub * 128 + quarter * 32;
-    for (int c = 32 * half; c < tile_cols; c += 64) {
+    for (int c = 32 * half; c < tile_cols; c += 32 * parts) {
       float v[32];
-      tmem_ld32(lane_base + (uint32_t)(sub * sub_stride + c), v);
+      tmem_ld32_sum(lane_base + (uint32_t)(sub * sub_stride + c), accs, 256, v);
       __syncwarp();
 #pragma unroll
       for (int j = 0; j < 32; ++j) square[lane * 33 + j] = v[j];
@@ -470,8 +499,10 @@ __device__ __forceinline__ void grid_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-template <int FMT, int SUBS>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+// MINB = 2: two CTAs share an SM (half the shared memory, 256 TMEM columns
+// each), so two K pipelines run side by side.
+template <int FMT, int SUBS, int DQW, int MINB>
+__global__ void __launch_bounds__(96 + 32 * DQW, MINB)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_wq,
                 const __grid_constant__ CUtensorMap map_ws, const __grid_constant__ CUtensorMap map_y,
                 const GemmParams p) {
@@ -501,11 +532,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int m0 = blockIdx.y * (128 * SUBS);
   const int KT = p.k / KSTEP / p.ksplit;   // this CTA's K steps
   const int kt0 = (int)blockIdx.z * KT;    // its first K step
-  constexpr uint32_t TMEM_COLS = SUBS == 2 ? 512 : 256;
+  // 128-row tiles alternate two accumulators over the K slices (columns 0 and
+  // 256): consecutive MMAs into one accumulator wait on each other
+  constexpr int ACCS = SUBS == 1 && MINB == 1 ? 2 : 1;
+  constexpr uint32_t TMEM_COLS = MINB == 2 ? 256 : 512;
 
   if (threadIdx.x == 0) {
-    // each K step is dequantised by one group of DQ_WARPS / dq_groups warps
-    const int gw = DQ_WARPS / p.dq_groups;
+    // each K step is dequantised by one group of DQW / dq_groups warps
+    const int gw = DQW / p.dq_groups;
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1 + gw);
       mbar_init(&empty[s], 1);
@@ -596,8 +630,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int sub = 0; sub < SUBS; ++sub)
 #pragma unroll
           for (int kk = 0; kk < KSTEP / 16; ++kk)
-            mma_bf16(tmem_base + sub * 256, ad + (uint64_t)((sub * 16384 + kk * 32) >> 4),
-                     bd + (uint64_t)((kk * 32) >> 4), idesc, (kt | kk) != 0);
+            mma_bf16(tmem_base + (ACCS == 2 ? (kk & 1) : sub) * 256,
+                     ad + (uint64_t)((sub * 16384 + kk * 32) >> 4), bd + (uint64_t)((kk * 32) >> 4),
+                     idesc, (kt | (ACCS == 2 ? kk >> 1 : kk)) != 0);
         mma_commit(&empty[s]);
         if (++s == S) {
           s = 0;
@@ -608,7 +643,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else {
     // ---------------- dequantise W, then the epilogue ----------------
-    const int t = threadIdx.x - 96;  // 0..DQ_THREADS-1
+    const int t = threadIdx.x - 96;  // 0 .. 32 * DQW - 1
     uint32_t lut[4] = {0, 0, 0, 0};
     if (FMT == IQ4_NL) {
 #pragma unroll
@@ -624,7 +659,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // through a step (two barrier waits, the proxy fence, two arrivals) is
     // what bounds them: the warps split into groups that take K steps in
     // turn, so several steps are in flight.
-    const int gw = DQ_WARPS / p.dq_groups;
+    const int gw = DQW / p.dq_groups;
     const int grp = (warp - 3) / gw;
     const int gt = t - grp * gw * 32;  // thread index within the group
     bool ok = true;
@@ -669,7 +704,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const bool drain = __all_sync(0xffffffffu, finished && !*(volatile int *)abort_flag);
     if (drain)
       drain_accumulators(p, &map_y, tmem_base, SUBS, 256, m0, n0, p.bn, warp & 3, (warp - 3) / 4,
-                         lane, reinterpret_cast<float *>(smem + (size_t)(warp - 3) * 8192));
+                         DQW / 4, ACCS, lane,
+                         reinterpret_cast<float *>(
+                             smem + (size_t)(warp - 3) * (p.tma_out ? EPI_TMA_BYTES : EPI_SQUARE_BYTES)));
   }
   out_fence(p.out);
   tc_fence_before();
@@ -787,21 +824,37 @@ uint64_t gemm_workspace_bytes(int, uint64_t m, uint64_t, uint64_t k) {
   return ceil_div(m * k * 2, 256) * 256;
 }
 
-// Split-K for up to 128 activation rows.  A K step of a tile up to ~96
-// columns wide costs about the same (its barriers and the dequantising warps'
-// latency, not its MMAs or its bytes), so where one wave of tiles leaves them
-// that narrow, s CTAs per tile (s = 2 or 4) each take 1/s of K over s-times-
-// wider tiles and a sum pass adds the s partial planes.  s is the largest that
-// keeps tiles at most 112 columns wide, whole 256-value blocks per part, and
-// one wave.
-static int choose_split(uint64_t m, uint64_t n, uint64_t k, int sms) {
-  int best = 1;
+// Split-K for up to 128 activation rows.  A 64-value K step of a tile up to
+// ~112 columns wide costs about the same, ~0.45 us (a copy of the kernel with
+// no loads, no dequantisation and no MMAs still takes ~0.3 us per step), so
+// fewer steps per CTA is what shortens such a call: s CTAs per tile each take
+// 1/s of K and a sum pass adds the s partial planes.  Two forms, measured:
+//  - two CTAs per SM (half the shared memory each), s = 4 or 8 parts of tiles
+//    at most 112 columns wide in one wave of 2 x SMs CTAs: best where the
+//    output is narrow (N = 1024 .. 4096);
+//  - otherwise one CTA per SM, s = 2 or 4, tiles at most 112 columns wide in
+//    one wave (wider tiles make each step dearer than the split saves).
+// Each part is whole 256-value blocks.
+struct SplitChoice {
+  int s;
+  bool dual;
+};
+
+static SplitChoice choose_split(uint64_t m, uint64_t n, uint64_t k, int sms) {
+  SplitChoice best = {1, false};
   if (m > 128) return best;
+  for (int s = 4; s <= 8; s *= 2) {
+    if (k % (256ull * s) != 0) break;
+    const TileChoice t = choose_tiles(m, n, 2 * sms / s);
+    if (t.bn > 112 || (uint64_t)s * ceil_div(n, (uint64_t)t.bn) > 2ull * sms) break;
+    best = {s, true};
+  }
+  if (best.dual) return best;
   for (int s = 2; s <= 4; s *= 2) {
-    if (k % (256ull * s) != 0 || sms / s < 1) break;
+    if (k % (256ull * s) != 0) break;
     const TileChoice t = choose_tiles(m, n, sms / s);
     if (t.bn > 112 || (uint64_t)s * ceil_div(n, (uint64_t)t.bn) > (uint64_t)sms) break;
-    best = s;
+    best = {s, false};
   }
   return best;
 }
@@ -812,7 +865,7 @@ constexpr int kB200Sms = 148;
 
 uint64_t gemm_workspace_bytes_preferred(int fmt, uint64_t m, uint64_t n, uint64_t k) {
   const uint64_t base = gemm_workspace_bytes(fmt, m, n, k);
-  const int s = choose_split(m, n, k, kB200Sms);
+  const int s = choose_split(m, n, k, kB200Sms).s;
   return s > 1 ? base + (uint64_t)s * m * n * 4 : base;
 }
 
@@ -823,7 +876,7 @@ bool gemm_supported(int fmt, uint64_t m, uint64_t n, uint64_t k) {
 
 cudaError_t launch_gemm_core(int fmt, const void *w, uint64_t n, uint64_t k, const void *xb,
                              uint64_t m, const OutSpec &out, const float *addend, int addend_mode,
-                             int *err, int sms, cudaStream_t stream, int ksplit);
+                             int *err, int sms, cudaStream_t stream, int ksplit, bool dual);
 
 cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const float *x, uint64_t m,
                         const OutSpec &out, const float *addend, int addend_mode, void *workspace,
@@ -845,11 +898,13 @@ cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const fl
   if (e != cudaSuccess) return e;
   // one output and room for the partial planes: split K
   const uint64_t base = gemm_workspace_bytes(fmt, m, n, k);
-  int s = out.world == 1 ? choose_split(m, n, k, sms) : 1;
-  while (s > 1 && workspace_bytes < base + (uint64_t)s * m * n * 4) s /= 2;
+  SplitChoice sc = out.world == 1 ? choose_split(m, n, k, sms) : SplitChoice{1, false};
+  while (sc.s > 1 && workspace_bytes < base + (uint64_t)sc.s * m * n * 4) sc.s /= 2;
+  const int s = sc.s;
   if (s > 1) {
     float *part = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + base);
-    e = launch_gemm_core(fmt, w, n, k, xb, m, plain_out(part, n), nullptr, 0, err, sms, stream, s);
+    e = launch_gemm_core(fmt, w, n, k, xb, m, plain_out(part, n), nullptr, 0, err, sms, stream, s,
+                         sc.dual);
     if (e == cudaSuccess) {
       uint64_t sblocks = ceil_div(m * n, 256);
       if (sblocks > (uint64_t)sms * 8) sblocks = (uint64_t)sms * 8;
@@ -858,26 +913,31 @@ cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const fl
     }
     return e;
   }
-  return launch_gemm_core(fmt, w, n, k, xb, m, out, addend, addend_mode, err, sms, stream, 1);
+  return launch_gemm_core(fmt, w, n, k, xb, m, out, addend, addend_mode, err, sms, stream, 1,
+                          false);
 }
 
 cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, const void *xb,
                              uint64_t m, const OutSpec &out, const float *addend, int addend_mode,
                              int *err, int sms, cudaStream_t stream) {
-  return launch_gemm_core(fmt, w, n, k, xb, m, out, addend, addend_mode, err, sms, stream, 1);
+  return launch_gemm_core(fmt, w, n, k, xb, m, out, addend, addend_mode, err, sms, stream, 1,
+                          false);
 }
 
-// The GEMM kernel launch; ksplit = 2 or 4 writes the K parts' partial sums
-// into planes 0 .. ksplit-1 of out (one output, ldy = n, no addend).
+// The GEMM kernel launch; ksplit = 2, 4 or 8 writes the K parts' partial sums
+// into planes 0 .. ksplit-1 of out (one output, ldy = n, no addend).  dual:
+// the two-CTAs-per-SM kernel (up to 128 activation rows).
 cudaError_t launch_gemm_core(int fmt, const void *w, uint64_t n, uint64_t k, const void *xb,
                              uint64_t m, const OutSpec &out, const float *addend, int addend_mode,
-                             int *err, int sms, cudaStream_t stream, int ksplit) {
+                             int *err, int sms, cudaStream_t stream, int ksplit, bool dual) {
   if (!gemm_supported(fmt, m, n, k) || (reinterpret_cast<uintptr_t>(w) & 15) ||
-      (reinterpret_cast<uintptr_t>(xb) & 15) || (ksplit != 1 && ksplit != 2 && ksplit != 4) ||
-      k % (256ull * ksplit) != 0 || (ksplit > 1 && (out.world != 1 || addend_mode != 0)))
+      (reinterpret_cast<uintptr_t>(xb) & 15) ||
+      (ksplit != 1 && ksplit != 2 && ksplit != 4 && ksplit != 8) ||
+      k % (256ull * ksplit) != 0 || (ksplit > 1 && (out.world != 1 || addend_mode != 0)) ||
+      (dual && m > 128))
     return cudaErrorInvalidValue;
   const Layout L(fmt, n, k);
-  const TileChoice t = choose_tiles(m, n, ksplit > 1 ? sms / ksplit : sms);
+  const TileChoice t = choose_tiles(m, n, (dual ? 2 * sms : sms) / ksplit);
   GemmParams p = {};
   p.m = (int)m;
   p.n = (int)n;
@@ -897,7 +957,9 @@ cudaError_t launch_gemm_core(int fmt, const void *w, uint64_t n, uint64_t k, con
   // Narrow tiles (few weight rows per CTA) run their K loop faster with more
   // operand stages in flight: as many as fit (up to 6), then packed stages (up
   // to 8).
-  const uint32_t budget = 225 * 1024 - 1024 /*align slack*/ - 512 /*barriers*/;
+  // (two CTAs per SM: each within half of the SM's 228 KB, less the 1 KB the
+  // runtime reserves per CTA)
+  const uint32_t budget = (dual ? 112 * 1024 : 225 * 1024) - 1024 /*align slack*/ - 512 /*barriers*/;
   const uint32_t ab = p.a_bytes + p.b_bytes;
   // Dequant warp groups for narrow tiles (see the kernel).  A group waits on
   // the slots of its own steps only, and an mbarrier parity wait cannot tell
@@ -906,7 +968,8 @@ cudaError_t launch_gemm_core(int fmt, const void *w, uint64_t n, uint64_t k, con
   // ring when its depth is a multiple of the group count, and for the operand
   // ring (released in K order by the MMA commits) when it is at least that deep.
   auto fits = [&](int a, int q) { return (uint32_t)a * ab + (uint32_t)q * p.pstage_bytes <= budget; };
-  int groups = t.bn <= 64 ? 4 : t.bn <= 128 ? 2 : 1;
+  const int dqw = dq_warps_for(t.subs, dual);
+  int groups = dqw == 16 ? (t.bn <= 128 ? 4 : 2) : (t.bn <= 64 ? 4 : t.bn <= 128 ? 2 : 1);
   int sa = 2, sp = 2 * groups;
   while (groups > 1) {
     sp = 2 * groups;
@@ -945,8 +1008,11 @@ cudaError_t launch_gemm_core(int fmt, const void *w, uint64_t n, uint64_t k, con
     return cudaErrorInvalidValue;
   // one output, no addend, 16-byte rows: the epilogue stores 32 x 32 blocks by TMA
   // (wide tiles only: for narrow ones the per-block waits outweigh the gain)
+  // (the epilogue's per-warp scratch lies in the operand ring)
+  const uint64_t ring_bytes = (uint64_t)sa * ab;
   p.tma_out = out.world == 1 && addend_mode == 0 && p.vec_out && out.col0 == 0 && t.bn >= 192 &&
-              ksplit == 1;
+              ksplit == 1 && ring_bytes >= (uint64_t)dqw * EPI_TMA_BYTES;
+  if (out.world > 1 && ring_bytes < (uint64_t)dqw * EPI_SQUARE_BYTES) return cudaErrorInvalidValue;
   if (p.tma_out && !make_map_2d(&map_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, out.y_ranks[0], n, m,
                                 out.ldy * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B))
     p.tma_out = 0;
@@ -959,13 +1025,17 @@ cudaError_t launch_gemm_core(int fmt, const void *w, uint64_t n, uint64_t k, con
     auto kern = KERN;                                                                          \
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \
     if (e != cudaSuccess) return e;                                                            \
-    e = launch_dependent(kern, grid, dim3(NUM_THREADS), smem, stream, map_a, map_wq, map_ws,     \
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,             \
+                             (int)cudaSharedmemCarveoutMaxShared);                             \
+    if (e != cudaSuccess) return e;                                                            \
+    e = launch_dependent(kern, grid, dim3(96 + 32 * dqw), smem, stream, map_a, map_wq, map_ws,   \
                          map_y, p);                                                            \
   } while (0)
 #define MGB_GEMM_FMT(F)                                     \
   case F:                                                   \
-    if (t.subs == 2) MGB_GEMM_LAUNCH((gemm_kernel<F, 2>));  \
-    else MGB_GEMM_LAUNCH((gemm_kernel<F, 1>));              \
+    if (t.subs == 2) MGB_GEMM_LAUNCH((gemm_kernel<F, 2, 8, 1>));       \
+    else if (dual) MGB_GEMM_LAUNCH((gemm_kernel<F, 1, 8, 2>));         \
+    else MGB_GEMM_LAUNCH((gemm_kernel<F, 1, 16, 1>));                  \
     break;
   switch (fmt) {
     MGB_GEMM_FMT(Q4_K)

@@ -173,14 +173,16 @@ def test_gemm_config1_sampled_columns(torch_cuda, oracle):
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
-@pytest.mark.parametrize("m,n,k,parts", [(3, 300, 1024, 4), (64, 8192, 4096, 2),
-                                         (128, 1001, 2048, 4), (17, 64, 14336, 4),
-                                         (8, 512, 1536, 2), (64, 14336, 4096, 1)])
+@pytest.mark.parametrize("m,n,k,parts", [(3, 300, 1024, 4), (64, 8192, 4096, 4),
+                                         (128, 1001, 2048, 8), (17, 64, 14336, 8),
+                                         (8, 512, 1536, 2), (64, 14336, 4096, 1),
+                                         (200, 1000, 1024, 1)])
 def test_gemm_split_k(torch_cuda, oracle, fmt, m, n, k, parts):
-    """With the preferred workspace a call of m <= 128 rows whose one-wave
-    tiles are narrow splits K over 2 or 4 CTAs per tile and sums the parts in
-    a fixed order: the result is deterministic and matches the oracle, and the
-    one-pass call (minimum workspace) to within the same tolerance."""
+    """With the preferred workspace a call of m <= 128 rows with narrow tiles
+    splits K over 2, 4 or 8 CTAs per tile (4 and 8: two CTAs per SM) and sums
+    the parts in a fixed order: the result is deterministic and matches the
+    oracle, and the one-pass call (minimum workspace) to within the same
+    tolerance."""
     torch = torch_cuda
     planes = 0 if parts == 1 else parts
     assert mgb.qmatmul_workspace_bytes(fmt, m, n, k) == \
