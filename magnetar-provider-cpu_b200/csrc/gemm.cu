@@ -14,7 +14,8 @@
 // boxes from HBM, 3+ deep, released by the dequantising warps).  Launched as a
 // programmatic dependent: everything but the activation loads (TMEM, barriers,
 // the weight stream, dequantisation) overlaps the previous kernel on the
-// stream.  Warp roles, 352 threads:
+// stream.  Warp roles, 96 + 32 * DQW threads (DQW dequantising warps: 8 for
+// 256-row tiles and for the two-CTAs-per-SM split-K form, 16 otherwise):
 //   warp 0     TMA producer of the bf16 activation boxes (SWIZZLE_128B,
 //              straight into the UMMA operand layout) on full[s], after
 //              griddepcontrol.wait.  Owns the TMEM allocation.
@@ -22,7 +23,7 @@
 //              per 16-wide K slice and commits each step to empty[s].
 //   warp 2     TMA producer of the packed W quant and scale boxes (no
 //              swizzle) on p_full[s].
-//   warps 3-10 dequantise the staged packed W into the bf16 B operand
+//   warps 3.. dequantise the staged packed W into the bf16 B operand
 //              (K-major, SWIZZLE_128B written by hand), fence the async proxy
 //              and arrive on full[s] and p_empty[s] (on narrow tiles as 2 or 4
 //              groups that take K steps in turn); after the last stage they
@@ -32,6 +33,8 @@
 //              registers, or, when every rank's y receives the tile (fused
 //              all-gather over NVLink), through shared memory in whole row
 //              segments.
+// Up to 128 activation rows, a call may split K over 2, 4 or 8 CTAs per tile
+// (blockIdx.z), each writing an f32 partial plane that splitk_sum_kernel adds.
 // Every CTA loads its own tiles from this GPU's HBM (no cluster-shared loads).
 // Every wait is bounded; on expiry the kernel records ERR_WAIT_TIMEOUT, skips
 // the remaining work, waits (bounded) for its own copies and MMAs, frees TMEM
