@@ -15,7 +15,8 @@
 // programmatic dependent: everything but the activation loads (TMEM, barriers,
 // the weight stream, dequantisation) overlaps the previous kernel on the
 // stream.  Warp roles, 96 + 32 * DQW threads (DQW dequantising warps: 8 for
-// 256-row tiles and for the two-CTAs-per-SM split-K form, 16 otherwise):
+// 256-row tiles, 16 for 128-row tiles, whose stages of up to 128 columns hold
+// two 64-value K atoms):
 //   warp 0     TMA producer of the bf16 activation boxes (SWIZZLE_128B,
 //              straight into the UMMA operand layout) on full[s], after
 //              griddepcontrol.wait.  Owns the TMEM allocation.
@@ -53,9 +54,9 @@ namespace {
 constexpr int KSTEP = 64;                    // bf16 values per 128-byte row of a stage
 // warps 3 .. 3 + DQW - 1 dequantise, then run the epilogue: DQW = 8 for
 // 256-row tiles (there the dequantisation competes with the MMAs for shared
-// memory) and for the two-CTAs-per-SM split-K kernel, 16 for other 128-row
-// tiles (up to 128 activation rows: the weight stream is the work)
-constexpr int dq_warps_for(int subs, bool dual) { return subs == 2 || dual ? 8 : 16; }
+// memory), 16 for 128-row tiles (up to 128 activation rows: the weight stream
+// is the work)
+constexpr int dq_warps_for(int subs) { return subs == 2 ? 8 : 16; }
 constexpr int EPI_SQUARE_BYTES = 4352;  // a warp's 32 x 33 f32 square, rounded up
 constexpr int EPI_TMA_BYTES = 8192;     // a warp's two 4 KB TMA-store buffers
 
@@ -68,7 +69,9 @@ struct GemmParams {
   int qbytes;           // packed quant bytes per weight row per K step (32, 48 or 64)
   int wsw;              // scale-plane bytes per weight row per 256 values (16, 32 or 48)
   int dq_groups;        // dequant warp groups taking K steps in turn (1, 2 or 4)
-  int ksplit;           // K halves computed by separate CTAs (blockIdx.z), summed after
+  int ksplit;           // K parts computed by separate CTAs (blockIdx.z), summed after
+  int atoms;            // 64-value K atoms per pipeline stage (the kernel's AT)
+  uint32_t b_atom;      // bytes of one atom's bf16 W tile
   uint32_t a_bytes;     // per activation stage
   uint32_t b_bytes;     // per W-tile stage
   uint32_t wq_bytes;    // per packed stage
@@ -502,10 +505,9 @@ __device__ __forceinline__ void grid_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// MINB = 2: two CTAs share an SM (half the shared memory, 256 TMEM columns
-// each), so two K pipelines run side by side.
-template <int FMT, int SUBS, int DQW, int MINB>
-__global__ void __launch_bounds__(96 + 32 * DQW, MINB)
+// AT: 64-value K atoms per pipeline stage (1 or 2).
+template <int FMT, int SUBS, int DQW, int AT>
+__global__ void __launch_bounds__(96 + 32 * DQW, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_wq,
                 const __grid_constant__ CUtensorMap map_ws, const __grid_constant__ CUtensorMap map_y,
                 const GemmParams p) {
@@ -533,12 +535,12 @@ __global__ void __launch_bounds__(96 + 32 * DQW, MINB)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * p.bn;
   const int m0 = blockIdx.y * (128 * SUBS);
-  const int KT = p.k / KSTEP / p.ksplit;   // this CTA's K steps
-  const int kt0 = (int)blockIdx.z * KT;    // its first K step
+  const int KT = p.k / (KSTEP * AT) / p.ksplit;   // this CTA's stages
+  const int kt0 = (int)blockIdx.z * KT;                // its first stage
   // 128-row tiles alternate two accumulators over the K slices (columns 0 and
   // 256): consecutive MMAs into one accumulator wait on each other
-  constexpr int ACCS = SUBS == 1 && MINB == 1 ? 2 : 1;
-  constexpr uint32_t TMEM_COLS = MINB == 2 ? 256 : 512;
+  constexpr int ACCS = SUBS == 1 ? 2 : 1;
+  constexpr uint32_t TMEM_COLS = 512;
 
   if (threadIdx.x == 0) {
     // each K step is dequantised by one group of DQW / dq_groups warps
@@ -584,8 +586,11 @@ __global__ void __launch_bounds__(96 + 32 * DQW, MINB)
         if (*(volatile int *)abort_flag) break;
         uint8_t *st = a0 + (size_t)s * p.a_bytes;
         mbar_arrive_expect_tx(&full[s], p.a_bytes);
-        for (int sub = 0; sub < SUBS; ++sub)
-          tma_load_2d(st + sub * 16384, &map_a, (kt0 + kt) * KSTEP, m0 + sub * 128, &full[s]);
+#pragma unroll
+        for (int a = 0; a < AT; ++a)
+          for (int sub = 0; sub < SUBS; ++sub)
+            tma_load_2d(st + (a * SUBS + sub) * 16384, &map_a, ((kt0 + kt) * AT + a) * KSTEP,
+                        m0 + sub * 128, &full[s]);
       }
       // (every activation copy has landed before the MMAs that read it, and
       // the epilogue waits for those)
@@ -604,8 +609,9 @@ __global__ void __launch_bounds__(96 + 32 * DQW, MINB)
         if (*(volatile int *)abort_flag) break;
         uint8_t *st = pk0 + (size_t)s * p.pstage_bytes;
         mbar_arrive_expect_tx(&p_full[s], p.ptx_bytes);
-        tma_load_2d(st, &map_wq, (kt0 + kt) * p.qbytes, n0, &p_full[s]);
-        tma_load_2d(st + p.wq_bytes, &map_ws, ((kt0 + kt) / 4) * p.wsw, n0, &p_full[s]);
+        // (a stage's atoms lie in one 256-value block: one scale box)
+        tma_load_2d(st, &map_wq, (kt0 + kt) * p.qbytes * AT, n0, &p_full[s]);
+        tma_load_2d(st + p.wq_bytes, &map_ws, ((kt0 + kt) * AT / 4) * p.wsw, n0, &p_full[s]);
         issued = kt + 1;
       }
       for (int kt = (issued > SP ? issued - SP : 0); kt < issued; ++kt)
@@ -630,12 +636,15 @@ __global__ void __launch_bounds__(96 + 32 * DQW, MINB)
         const uint64_t ad = a_desc0 + (((uint64_t)s * p.a_bytes) >> 4);
         const uint64_t bd = b_desc0 + (((uint64_t)s * p.b_bytes) >> 4);
 #pragma unroll
-        for (int sub = 0; sub < SUBS; ++sub)
+        for (int a = 0; a < AT; ++a)
 #pragma unroll
-          for (int kk = 0; kk < KSTEP / 16; ++kk)
-            mma_bf16(tmem_base + (ACCS == 2 ? (kk & 1) : sub) * 256,
-                     ad + (uint64_t)((sub * 16384 + kk * 32) >> 4), bd + (uint64_t)((kk * 32) >> 4),
-                     idesc, (kt | (ACCS == 2 ? kk >> 1 : kk)) != 0);
+          for (int sub = 0; sub < SUBS; ++sub)
+#pragma unroll
+            for (int kk = 0; kk < KSTEP / 16; ++kk)
+              mma_bf16(tmem_base + (ACCS == 2 ? (kk & 1) : sub) * 256,
+                       ad + (uint64_t)(((a * SUBS + sub) * 16384 + kk * 32) >> 4),
+                       bd + (uint64_t)((a * p.b_atom + kk * 32) >> 4), idesc,
+                       (kt | a | (ACCS == 2 ? kk >> 1 : kk)) != 0);
         mma_commit(&empty[s]);
         if (++s == S) {
           s = 0;
@@ -657,7 +666,9 @@ __global__ void __launch_bounds__(96 + 32 * DQW, MINB)
         lut[i] = v;
       }
     }
-    const int items = p.bn * 2;  // (weight row, run) pairs per stage
+    const int items1 = p.bn * 2;              // (weight row, run) pairs per atom
+    const int items = items1 * AT;            // ... per stage
+    const int pk_row = p.qbytes * AT;         // a weight row's packed bytes per stage
     // Narrow tiles have little dequantisation per step, and one warp's pass
     // through a step (two barrier waits, the proxy fence, two arrivals) is
     // what bounds them: the warps split into groups that take K steps in
@@ -681,10 +692,13 @@ __global__ void __launch_bounds__(96 + 32 * DQW, MINB)
       const uint8_t *wq = pk0 + (size_t)sp * p.pstage_bytes;
       const uint8_t *ws = wq + p.wq_bytes;
       for (int it = gt; it < items; it += gw * 32) {
-        const int row = it >> 1, j = it & 1;
+        const int a = AT == 2 && it >= items1 ? 1 : 0;
+        const int r = it - a * items1;
+        const int row = r >> 1, j = r & 1;
         uint4 out[4];
-        dequant_run<FMT>(wq + row * p.qbytes, ws + row * p.wsw, kt0 + kt, j, lut, out);
-        uint8_t *dst_row = bt + row * 128;
+        dequant_run<FMT>(wq + row * pk_row + a * p.qbytes, ws + row * p.wsw,
+                         (kt0 + kt) * AT + a, j, lut, out);
+        uint8_t *dst_row = bt + a * p.b_atom + row * 128;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const int chunk = j * 4 + c;
@@ -827,37 +841,22 @@ uint64_t gemm_workspace_bytes(int, uint64_t m, uint64_t, uint64_t k) {
   return ceil_div(m * k * 2, 256) * 256;
 }
 
-// Split-K for up to 128 activation rows.  A 64-value K step of a tile up to
-// ~112 columns wide costs about the same, ~0.45 us (a copy of the kernel with
-// no loads, no dequantisation and no MMAs still takes ~0.3 us per step), so
-// fewer steps per CTA is what shortens such a call: s CTAs per tile each take
-// 1/s of K and a sum pass adds the s partial planes.  Two forms, measured:
-//  - two CTAs per SM (half the shared memory each), s = 4 or 8 parts of tiles
-//    at most 112 columns wide in one wave of 2 x SMs CTAs: best where the
-//    output is narrow (N = 1024 .. 4096);
-//  - otherwise one CTA per SM, s = 2 or 4, tiles at most 112 columns wide in
-//    one wave (wider tiles make each step dearer than the split saves).
-// Each part is whole 256-value blocks.
-struct SplitChoice {
-  int s;
-  bool dual;
-};
-
-static SplitChoice choose_split(uint64_t m, uint64_t n, uint64_t k, int sms) {
-  SplitChoice best = {1, false};
+// Split-K for up to 128 activation rows.  A pipeline stage of a tile up to
+// ~112 columns wide costs about the same whatever its width (a copy of the
+// kernel with no loads, no dequantisation and no MMAs keeps most of it), so
+// fewer stages per CTA is what shortens such a call: s CTAs per tile (s = 2,
+// 4 or 8) each take 1/s of K and a sum pass adds the s partial planes.  s is
+// the largest that keeps tiles at most 112 columns wide (wider tiles make
+// each stage dearer than the split saves), each part whole 256-value blocks,
+// and one wave of one CTA per SM.
+static int choose_split(uint64_t m, uint64_t n, uint64_t k, int sms) {
+  int best = 1;
   if (m > 128) return best;
-  for (int s = 4; s <= 8; s *= 2) {
-    if (k % (256ull * s) != 0) break;
-    const TileChoice t = choose_tiles(m, n, 2 * sms / s);
-    if (t.bn > 112 || (uint64_t)s * ceil_div(n, (uint64_t)t.bn) > 2ull * sms) break;
-    best = {s, true};
-  }
-  if (best.dual) return best;
-  for (int s = 2; s <= 4; s *= 2) {
+  for (int s = 2; s <= 8; s *= 2) {
     if (k % (256ull * s) != 0) break;
     const TileChoice t = choose_tiles(m, n, sms / s);
     if (t.bn > 112 || (uint64_t)s * ceil_div(n, (uint64_t)t.bn) > (uint64_t)sms) break;
-    best = {s, false};
+    best = s;
   }
   return best;
 }
@@ -868,7 +867,7 @@ constexpr int kB200Sms = 148;
 
 uint64_t gemm_workspace_bytes_preferred(int fmt, uint64_t m, uint64_t n, uint64_t k) {
   const uint64_t base = gemm_workspace_bytes(fmt, m, n, k);
-  const int s = choose_split(m, n, k, kB200Sms).s;
+  const int s = choose_split(m, n, k, kB200Sms);
   return s > 1 ? base + (uint64_t)s * m * n * 4 : base;
 }
 
@@ -879,7 +878,7 @@ bool gemm_supported(int fmt, uint64_t m, uint64_t n, uint64_t k) {
 
 cudaError_t launch_gemm_core(int fmt, const void *w, uint64_t n, uint64_t k, const void *xb,
                              uint64_t m, const OutSpec &out, const float *addend, int addend_mode,
-                             int *err, int sms, cudaStream_t stream, int ksplit, bool dual);
+                             int *err, int sms, cudaStream_t stream, int ksplit);
 
 cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const float *x, uint64_t m,
                         const OutSpec &out, const float *addend, int addend_mode, void *workspace,
@@ -901,13 +900,11 @@ cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const fl
   if (e != cudaSuccess) return e;
   // one output and room for the partial planes: split K
   const uint64_t base = gemm_workspace_bytes(fmt, m, n, k);
-  SplitChoice sc = out.world == 1 ? choose_split(m, n, k, sms) : SplitChoice{1, false};
-  while (sc.s > 1 && workspace_bytes < base + (uint64_t)sc.s * m * n * 4) sc.s /= 2;
-  const int s = sc.s;
+  int s = out.world == 1 ? choose_split(m, n, k, sms) : 1;
+  while (s > 1 && workspace_bytes < base + (uint64_t)s * m * n * 4) s /= 2;
   if (s > 1) {
     float *part = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + base);
-    e = launch_gemm_core(fmt, w, n, k, xb, m, plain_out(part, n), nullptr, 0, err, sms, stream, s,
-                         sc.dual);
+    e = launch_gemm_core(fmt, w, n, k, xb, m, plain_out(part, n), nullptr, 0, err, sms, stream, s);
     if (e == cudaSuccess) {
       uint64_t sblocks = ceil_div(m * n, 256);
       if (sblocks > (uint64_t)sms * 8) sblocks = (uint64_t)sms * 8;
@@ -916,31 +913,27 @@ cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const fl
     }
     return e;
   }
-  return launch_gemm_core(fmt, w, n, k, xb, m, out, addend, addend_mode, err, sms, stream, 1,
-                          false);
+  return launch_gemm_core(fmt, w, n, k, xb, m, out, addend, addend_mode, err, sms, stream, 1);
 }
 
 cudaError_t launch_gemm_bf16(int fmt, const void *w, uint64_t n, uint64_t k, const void *xb,
                              uint64_t m, const OutSpec &out, const float *addend, int addend_mode,
                              int *err, int sms, cudaStream_t stream) {
-  return launch_gemm_core(fmt, w, n, k, xb, m, out, addend, addend_mode, err, sms, stream, 1,
-                          false);
+  return launch_gemm_core(fmt, w, n, k, xb, m, out, addend, addend_mode, err, sms, stream, 1);
 }
 
 // The GEMM kernel launch; ksplit = 2, 4 or 8 writes the K parts' partial sums
-// into planes 0 .. ksplit-1 of out (one output, ldy = n, no addend).  dual:
-// the two-CTAs-per-SM kernel (up to 128 activation rows).
+// into planes 0 .. ksplit-1 of out (one output, ldy = n, no addend).
 cudaError_t launch_gemm_core(int fmt, const void *w, uint64_t n, uint64_t k, const void *xb,
                              uint64_t m, const OutSpec &out, const float *addend, int addend_mode,
-                             int *err, int sms, cudaStream_t stream, int ksplit, bool dual) {
+                             int *err, int sms, cudaStream_t stream, int ksplit) {
   if (!gemm_supported(fmt, m, n, k) || (reinterpret_cast<uintptr_t>(w) & 15) ||
       (reinterpret_cast<uintptr_t>(xb) & 15) ||
       (ksplit != 1 && ksplit != 2 && ksplit != 4 && ksplit != 8) ||
-      k % (256ull * ksplit) != 0 || (ksplit > 1 && (out.world != 1 || addend_mode != 0)) ||
-      (dual && m > 128))
+      k % (256ull * ksplit) != 0 || (ksplit > 1 && (out.world != 1 || addend_mode != 0)))
     return cudaErrorInvalidValue;
   const Layout L(fmt, n, k);
-  const TileChoice t = choose_tiles(m, n, (dual ? 2 * sms : sms) / ksplit);
+  const TileChoice t = choose_tiles(m, n, sms / ksplit);
   GemmParams p = {};
   p.m = (int)m;
   p.n = (int)n;
@@ -948,46 +941,60 @@ cudaError_t launch_gemm_core(int fmt, const void *w, uint64_t n, uint64_t k, con
   p.qbytes = fmt == Q8_0 ? 64 : fmt == Q6_K ? 48 : 32;
   p.wsw = fmt == Q6_K ? 32 : fmt == Q5_K ? 48 : 16;
   p.bn = t.bn;
-  p.a_bytes = 16384u * t.subs;
-  p.b_bytes = (uint32_t)ceil_div((uint64_t)t.bn * 128u, 1024) * 1024;
-  p.wq_bytes = (uint32_t)ceil_div((uint64_t)t.bn * p.qbytes, 1024) * 1024;
-  p.ws_bytes = (uint32_t)ceil_div((uint64_t)t.bn * p.wsw, 1024) * 1024;
-  p.pstage_bytes = p.wq_bytes + p.ws_bytes;
-  p.ptx_bytes = (uint32_t)t.bn * (uint32_t)(p.qbytes + p.wsw);
   const dim3 grid((unsigned)ceil_div(n, (uint64_t)t.bn), (unsigned)ceil_div(m, 128ull * t.subs),
                   (unsigned)ksplit);
   p.ksplit = ksplit;
+  const uint32_t budget = 225 * 1024 - 1024 /*align slack*/ - 512 /*barriers*/;
+  const int dqw = dq_warps_for(t.subs);
+  // Stage geometry and ring depths for `atoms` K atoms per stage; false when
+  // not even the shallowest rings fit.
+  //
   // Narrow tiles (few weight rows per CTA) run their K loop faster with more
   // operand stages in flight: as many as fit (up to 6), then packed stages (up
-  // to 8).
-  // (two CTAs per SM: each within half of the SM's 228 KB, less the 1 KB the
-  // runtime reserves per CTA)
-  const uint32_t budget = (dual ? 112 * 1024 : 225 * 1024) - 1024 /*align slack*/ - 512 /*barriers*/;
-  const uint32_t ab = p.a_bytes + p.b_bytes;
-  // Dequant warp groups for narrow tiles (see the kernel).  A group waits on
-  // the slots of its own steps only, and an mbarrier parity wait cannot tell
-  // phase q from phase q - 2: so the previous use of every slot a group waits
-  // on must be a step that group waited on itself.  That holds for the packed
-  // ring when its depth is a multiple of the group count, and for the operand
-  // ring (released in K order by the MMA commits) when it is at least that deep.
-  auto fits = [&](int a, int q) { return (uint32_t)a * ab + (uint32_t)q * p.pstage_bytes <= budget; };
-  const int dqw = dq_warps_for(t.subs, dual);
-  int groups = dqw == 16 ? (t.bn <= 128 ? 4 : 2) : (t.bn <= 64 ? 4 : t.bn <= 128 ? 2 : 1);
-  int sa = 2, sp = 2 * groups;
-  while (groups > 1) {
+  // to 8).  Dequant warp groups for narrow tiles (see the kernel): a group
+  // waits on the slots of its own steps only, and an mbarrier parity wait
+  // cannot tell phase q from phase q - 2, so the previous use of every slot a
+  // group waits on must be a step that group waited on itself.  That holds for
+  // the packed ring when its depth is a multiple of the group count, and for
+  // the operand ring (released in K order by the MMA commits) when it is at
+  // least that deep.
+  int groups = 1, sa = 2, sp = 3;
+  uint32_t ab = 0;
+  auto size_rings = [&](int atoms) -> bool {
+    p.atoms = atoms;
+    p.a_bytes = 16384u * t.subs * atoms;
+    p.b_atom = (uint32_t)ceil_div((uint64_t)t.bn * 128u, 1024) * 1024;
+    p.b_bytes = p.b_atom * atoms;
+    p.wq_bytes = (uint32_t)ceil_div((uint64_t)t.bn * p.qbytes * atoms, 1024) * 1024;
+    p.ws_bytes = (uint32_t)ceil_div((uint64_t)t.bn * p.wsw, 1024) * 1024;
+    p.pstage_bytes = p.wq_bytes + p.ws_bytes;
+    p.ptx_bytes = (uint32_t)t.bn * (uint32_t)(p.qbytes * atoms + p.wsw);
+    ab = p.a_bytes + p.b_bytes;
+    auto fits = [&](int a, int q) { return (uint32_t)a * ab + (uint32_t)q * p.pstage_bytes <= budget; };
+    groups = dqw == 16 ? (t.bn <= 128 ? 4 : 2) : (t.bn <= 64 ? 4 : t.bn <= 128 ? 2 : 1);
+    sa = 2;
     sp = 2 * groups;
-    sa = 2;
-    while (sa < 6 && fits(sa + 1, sp)) ++sa;
-    if (fits(sa, sp) && sa >= groups) break;
-    groups /= 2;
-  }
-  if (groups == 1) {
-    sa = 2;
-    sp = 3;
-    if (!fits(sa, sp)) return cudaErrorInvalidValue;
-    while (sa < 6 && fits(sa + 1, sp)) ++sa;
-    while (sp < 8 && fits(sa, sp + 1)) ++sp;
-  }
+    while (groups > 1) {
+      sp = 2 * groups;
+      sa = 2;
+      while (sa < 6 && fits(sa + 1, sp)) ++sa;
+      if (fits(sa, sp) && sa >= groups) break;
+      groups /= 2;
+    }
+    if (groups == 1) {
+      sa = 2;
+      sp = 3;
+      if (!fits(sa, sp)) return false;
+      while (sa < 6 && fits(sa + 1, sp)) ++sa;
+      while (sp < 8 && fits(sa, sp + 1)) ++sp;
+    }
+    return true;
+  };
+  // 128-row tiles up to 128 columns wide take two K atoms per pipeline stage:
+  // half the barrier rounds per K (wider tiles would be left with too shallow
+  // rings)
+  const bool two = t.subs == 1 && t.bn <= 128 && size_rings(2);
+  if (!two && !size_rings(1)) return cudaErrorInvalidValue;
   p.dq_groups = groups;
   p.astages = sa;
   p.bstages = sa;
@@ -1004,7 +1011,7 @@ cudaError_t launch_gemm_core(int fmt, const void *w, uint64_t n, uint64_t k, con
   if (!make_map_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xb, k, m, k * 2, KSTEP, 128,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map_2d(&map_wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, L.qs_row, n, L.qs_row,
-                   (uint32_t)p.qbytes, (uint32_t)t.bn, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+                   (uint32_t)(p.qbytes * p.atoms), (uint32_t)t.bn, CU_TENSOR_MAP_SWIZZLE_NONE) ||
       !make_map_2d(&map_ws, CU_TENSOR_MAP_DATA_TYPE_UINT8,
                    static_cast<const uint8_t *>(w) + L.qs_bytes, L.sc_row, n, L.sc_row,
                    (uint32_t)p.wsw, (uint32_t)t.bn, CU_TENSOR_MAP_SWIZZLE_NONE))
@@ -1037,7 +1044,7 @@ cudaError_t launch_gemm_core(int fmt, const void *w, uint64_t n, uint64_t k, con
 #define MGB_GEMM_FMT(F)                                     \
   case F:                                                   \
     if (t.subs == 2) MGB_GEMM_LAUNCH((gemm_kernel<F, 2, 8, 1>));       \
-    else if (dual) MGB_GEMM_LAUNCH((gemm_kernel<F, 1, 8, 2>));         \
+    else if (two) MGB_GEMM_LAUNCH((gemm_kernel<F, 1, 16, 2>));         \
     else MGB_GEMM_LAUNCH((gemm_kernel<F, 1, 16, 1>));                  \
     break;
   switch (fmt) {

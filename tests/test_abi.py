@@ -47,8 +47,8 @@ def test_status_names_and_packed_sizes():
     assert mgb.qmatmul_workspace_bytes(mgb.Q8_0, 3, 5, 96) == 0  # ragged k: GEMV pairs
     assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 512, 14336, 4096) == 512 * 4096 * 2
     # m <= 128: room for the split-K partial planes too (K parts per tile)
-    assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 64, 4096, 4096) == 64 * 4096 * 2 + 8 * 64 * 4096 * 4
-    assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 64, 8192, 4096) == 64 * 4096 * 2 + 4 * 64 * 8192 * 4
+    assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 64, 4096, 4096) == 64 * 4096 * 2 + 4 * 64 * 4096 * 4
+    assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 64, 8192, 4096) == 64 * 4096 * 2 + 2 * 64 * 8192 * 4
     assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 64, 14336, 4096) == 64 * 4096 * 2  # wide tiles
     assert mgb.qmatmul_min_workspace_bytes(mgb.Q4_K, 64, 4096, 4096) == 64 * 4096 * 2
     assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 130, 4096, 4096) == 130 * 4096 * 2  # m > 128

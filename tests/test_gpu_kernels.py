@@ -173,16 +173,15 @@ def test_gemm_config1_sampled_columns(torch_cuda, oracle):
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
-@pytest.mark.parametrize("m,n,k,parts", [(3, 300, 1024, 4), (64, 8192, 4096, 4),
+@pytest.mark.parametrize("m,n,k,parts", [(3, 300, 1024, 4), (64, 8192, 4096, 2),
                                          (128, 1001, 2048, 8), (17, 64, 14336, 8),
                                          (8, 512, 1536, 2), (64, 14336, 4096, 1),
-                                         (200, 1000, 1024, 1)])
+                                         (16, 4096, 4096, 4), (200, 1000, 1024, 1)])
 def test_gemm_split_k(torch_cuda, oracle, fmt, m, n, k, parts):
     """With the preferred workspace a call of m <= 128 rows with narrow tiles
-    splits K over 2, 4 or 8 CTAs per tile (4 and 8: two CTAs per SM) and sums
-    the parts in a fixed order: the result is deterministic and matches the
-    oracle, and the one-pass call (minimum workspace) to within the same
-    tolerance."""
+    splits K over 2, 4 or 8 CTAs per tile and sums the parts in a fixed
+    order: the result is deterministic and matches the oracle, and the
+    one-pass call (minimum workspace) to within the same tolerance."""
     torch = torch_cuda
     planes = 0 if parts == 1 else parts
     assert mgb.qmatmul_workspace_bytes(fmt, m, n, k) == \
@@ -257,7 +256,8 @@ def test_nan_activation_reaches_its_row_only(torch_cuda, oracle, fmt, m):
     assert np.isfinite(y[1:]).all()
 
 
-@pytest.mark.parametrize("m,n,k", [(40, 28672, 256), (300, 14344, 256), (300, 14342, 256)])
+@pytest.mark.parametrize("m,n,k", [(40, 28672, 256), (300, 14344, 256), (300, 14342, 256),
+                                   (16, 65536, 256)])
 def test_gemm_wide_tile_epilogue_edges(torch_cuda, oracle, m, n, k):
     """Wide tiles (bn >= 192) store 32x32 output blocks by TMA: rows past m and
     columns past n are clipped by the tensor map, a tile's partial last block
