@@ -790,7 +790,12 @@ static size_t staged_config(int n, int k, int sms, GemvStaged &p, int &grid, int
   p.chunk = chunk;
   const size_t fixed = red_stage * chunk;
   const size_t per_stage = (size_t)p.stage_bytes + p.dec_stage_bytes + 16;
-  const size_t budget = CORESIDENT_SMEM > fixed ? CORESIDENT_SMEM - fixed : 0;
+  // The 288-thread form stays within half an SM so the next GEMV's CTA can
+  // stream its weights beside it; the 1024-thread form (k > 8192) takes the
+  // whole SM's shared memory instead: its deeper ring is worth more than the
+  // overlap (K = 28,672, N = 8,192: 47.6 -> 34.4 us).
+  const size_t cap = MAXT > 288 ? MAX_SMEM - 1024 : CORESIDENT_SMEM;
+  const size_t budget = cap > fixed ? cap - fixed : 0;
   int stages = (int)(budget / per_stage);
   if (stages > 8) stages = 8;
   if (stages > nst) stages = nst;
