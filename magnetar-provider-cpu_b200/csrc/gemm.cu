@@ -14,9 +14,8 @@
 // boxes from HBM, 3+ deep, released by the dequantising warps).  Launched as a
 // programmatic dependent: everything but the activation loads (TMEM, barriers,
 // the weight stream, dequantisation) overlaps the previous kernel on the
-// stream.  Warp roles, 96 + 32 * DQW threads (DQW dequantising warps: 8 for
-// 256-row tiles, 16 for 128-row tiles, whose stages of up to 128 columns hold
-// two 64-value K atoms):
+// stream.  Warp roles, 96 + 32 * DQW threads (DQW = 16 dequantising warps;
+// 128-row tiles up to 128 columns wide hold two 64-value K atoms per stage):
 //   warp 0     TMA producer of the bf16 activation boxes (SWIZZLE_128B,
 //              straight into the UMMA operand layout) on full[s], after
 //              griddepcontrol.wait.  Owns the TMEM allocation.
@@ -52,11 +51,11 @@ namespace mgb {
 namespace {
 
 constexpr int KSTEP = 64;                    // bf16 values per 128-byte row of a stage
-// warps 3 .. 3 + DQW - 1 dequantise, then run the epilogue: DQW = 8 for
-// 256-row tiles (there the dequantisation competes with the MMAs for shared
-// memory), 16 for 128-row tiles (up to 128 activation rows: the weight stream
-// is the work)
-constexpr int dq_warps_for(int subs) { return subs == 2 ? 8 : 16; }
+// warps 3 .. 3 + DQW - 1 dequantise, then run the epilogue: 16 warps, as many
+// as the registers allow (608 threads x <= 104 registers); against 8 they took
+// config 1's 256-row tiles from 70.2 to 58.4 us and a 128-row M = 16 tile from
+// 37.4 to 35.8 us
+constexpr int dq_warps_for(int) { return 16; }
 constexpr int EPI_SQUARE_BYTES = 4352;  // a warp's 32 x 33 f32 square, rounded up
 constexpr int EPI_TMA_BYTES = 8192;     // a warp's two 4 KB TMA-store buffers
 
@@ -1043,7 +1042,7 @@ cudaError_t launch_gemm_core(int fmt, const void *w, uint64_t n, uint64_t k, con
   } while (0)
 #define MGB_GEMM_FMT(F)                                     \
   case F:                                                   \
-    if (t.subs == 2) MGB_GEMM_LAUNCH((gemm_kernel<F, 2, 8, 1>));       \
+    if (t.subs == 2) MGB_GEMM_LAUNCH((gemm_kernel<F, 2, 16, 1>));       \
     else if (two) MGB_GEMM_LAUNCH((gemm_kernel<F, 1, 16, 2>));         \
     else MGB_GEMM_LAUNCH((gemm_kernel<F, 1, 16, 1>));                  \
     break;
