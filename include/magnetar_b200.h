@@ -265,12 +265,15 @@ uint64_t mgb_packed_bytes(int32_t format, uint64_t stored_rows, uint64_t stored_
 mgb_status mgb_repack(int32_t format, const void *ggml_blocks, uint64_t stored_rows,
                       uint64_t stored_cols, void *out, void *stream);
 /* Scratch bytes `mgb_qmatmul` wants for this shape (0 when none): the bf16
- * copy of x and, for m <= 128 rows with k % 512 == 0, two f32 [m, n] planes
- * with which the tensor-core path splits K across twice as many CTAs and then
- * sums the two halves (a different f32 summation order, same tolerance).
+ * copy of x and, for m <= 128 rows whose output is narrow enough (one wave of
+ * tiles at most 112 columns wide with K split s ways, s = 2, 4 or 8, k a
+ * multiple of 256 s), s f32 [m, n] planes: each of s CTAs per tile computes
+ * 1/s of K into its plane and a sum pass adds them in plane order (a
+ * different f32 summation order than one pass, same tolerance, deterministic).
  * Any workspace of at least mgb_qmatmul_min_workspace_bytes (the bf16 copy
- * alone) also takes the tensor-core path, in one K pass; the tensor-parallel
- * call (mgb_qmatmul_tp) always runs one K pass. */
+ * alone) also takes the tensor-core path, in one K pass (a workspace in
+ * between splits fewer ways); the tensor-parallel call (mgb_qmatmul_tp)
+ * always runs one K pass. */
 uint64_t mgb_qmatmul_workspace_bytes(int32_t format, uint64_t m, uint64_t n, uint64_t k);
 uint64_t mgb_qmatmul_min_workspace_bytes(int32_t format, uint64_t m, uint64_t n, uint64_t k);
 /* y[m, n] = x[m, k] * W^T on `stream`, W (device layout, 16-byte aligned)
