@@ -364,17 +364,28 @@ mgb_status mgb_quantize_rows(const float *x, uint64_t len, int8_t *values, float
  * with CUDA IPC).  No counterpart in the reference, which runs on one host. */
 #define MGB_MAX_TP 8
 /* Bytes of a rank's synchronisation words: done[MGB_MAX_TP] (u32 at offset 0,
- * word r written by rank r) and the call's CTA counter (u32 at offset 128). */
+ * word r written by rank r), the call's CTA counter (u32 at offset 128) and,
+ * for device epochs, the rank's epoch word (u32 at offset 132, the word after
+ * the counter). */
 #define MGB_TP_SYNC_BYTES 256u
 #define MGB_TP_COUNTER_OFFSET 128u
+#define MGB_TP_EPOCH_OFFSET 132u
 
 /* Where one rank's tensor-parallel call writes.  All pointers are valid on the
  * calling GPU (this rank's own buffers or IPC mappings of the peers').  Output
  * element (row, col) of the call goes to y[r] + row * ldy + col0 + col for
- * every r < world.  When every CTA has stored, the call stores `epoch` with
+ * every r < world.  When every CTA has stored, the call stores its epoch with
  * release semantics (system scope) into done[r][rank] for every r;
  * `cta_counter` is this rank's counter word, zero before its first call (each
- * call leaves it zero). */
+ * call leaves it zero).  The epoch is `epoch` (host epochs, counting from 1),
+ * or, when `epoch` is 0 (device epochs), the value of this rank's epoch word
+ * (the word after `cta_counter`) plus one, which mgb_tp_wait with epoch 0
+ * advances after each call: a sequence of calls and waits captured in a CUDA
+ * graph then publishes fresh epochs on every replay.  One synchronisation
+ * buffer uses one mode; with device epochs every rank's epoch word starts at
+ * zero, and an op alternating between two y buffers per call captures an even
+ * number of its calls in a graph, so that consecutive calls (across replays
+ * too) alternate buffers. */
 typedef struct mgb_tp_out {
     float *y[MGB_MAX_TP];
     uint32_t *done[MGB_MAX_TP];
@@ -409,8 +420,10 @@ mgb_status mgb_qmatmul_tp(int32_t format, const void *w, uint64_t n, uint64_t k,
                           void *stream);
 /* Stream-ordered wait until done[r] has reached `epoch` for every r < world
  * (`done` = this rank's synchronisation words).  Work queued after it on
- * `stream` sees every rank's columns.  A wait longer than timeout_ms (0: 2000)
- * gives up and records device error 1 (see mgb_take_device_error). */
+ * `stream` sees every rank's columns.  `epoch` 0: device epochs, the rank's
+ * epoch word + 1, and the word is advanced to it once every rank has reached
+ * it.  A wait longer than timeout_ms (0: 2000) gives up and records device
+ * error 1 (see mgb_take_device_error). */
 mgb_status mgb_tp_wait(const uint32_t *done, int32_t world, uint32_t epoch, uint32_t timeout_ms,
                        void *stream);
 

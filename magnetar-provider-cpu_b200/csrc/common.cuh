@@ -236,9 +236,10 @@ __device__ __forceinline__ void out_complete(const OutSpec &o, uint32_t total_ct
   const uint32_t before = atomicAdd(o.cta_counter, 1u);
   if (before != total_ctas - 1) return;
   *o.cta_counter = 0;  // every CTA of this call has counted: ready for the next call
+  const uint32_t epoch = o.epoch_src ? *(volatile const uint32_t *)o.epoch_src + 1u : o.epoch;
   __threadfence_system();
   for (int r = 0; r < o.world; ++r)
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(o.done_ranks[r] + o.rank), "r"(o.epoch)
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(o.done_ranks[r] + o.rank), "r"(epoch)
                  : "memory");
 }
 

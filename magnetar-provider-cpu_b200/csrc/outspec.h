@@ -12,12 +12,17 @@ constexpr int MAX_TP = 8;
 // col for every r < world (plain call: world 1, y_ranks[0] = y, ldy = n,
 // col0 = 0).  With cta_counter set, the call publishes its completion: every
 // CTA fences its stores at system scope and counts itself on cta_counter
-// (zero before the call); the last one resets it and stores `epoch` with
-// system-scope release into done_ranks[r][rank] for every r.
+// (zero before the call); the last one resets it and stores the call's epoch
+// with system-scope release into done_ranks[r][rank] for every r.  The epoch
+// is `epoch`, or, with epoch_src set (device epochs), *epoch_src + 1 read by
+// that last CTA: the rank's epoch word, which its stream-ordered wait advances
+// after every call, so a captured sequence of calls publishes fresh epochs on
+// every replay.
 struct OutSpec {
   float *y_ranks[MAX_TP];
   uint32_t *done_ranks[MAX_TP];
   uint32_t *cta_counter;
+  const uint32_t *epoch_src;
   uint64_t ldy, col0;
   uint32_t epoch;
   int world, rank;
@@ -31,6 +36,7 @@ inline OutSpec plain_out(float *y, uint64_t n) {
   o.world = 1;
   o.rank = 0;
   o.cta_counter = nullptr;
+  o.epoch_src = nullptr;
   o.epoch = 0;
   return o;
 }

@@ -21,27 +21,39 @@ namespace mgb {
 static_assert(MGB_MAX_TP == MAX_TP, "C ABI and kernel rank limits differ");
 static_assert(sizeof(cudaIpcMemHandle_t) == MGB_IPC_HANDLE_BYTES, "IPC handle size");
 
-// One warp: lane r polls rank r's done word until it reaches `epoch` (serial
+// One warp: lane r polls rank r's done word until it reaches the epoch (serial
 // number arithmetic, so the epoch may wrap).  Bounded by `timeout_ns` of the
-// global timer and an iteration cap; giving up records ERR_WAIT_TIMEOUT.
+// global timer and an iteration cap; giving up records ERR_WAIT_TIMEOUT.  With
+// epoch_word set (device epochs) the epoch is *epoch_word + 1, and once every
+// rank has reached it lane 0 advances *epoch_word to it (a wait that gives up
+// leaves it, and the error recorded).
 __global__ void tp_wait_kernel(const uint32_t *done, int world, uint32_t epoch,
-                               uint64_t timeout_ns, int *err) {
+                               uint32_t *epoch_word, uint64_t timeout_ns, int *err) {
   const int lane = threadIdx.x;
   if (lane >= world) return;
+  if (epoch_word) epoch = *(volatile uint32_t *)epoch_word + 1u;
   uint64_t t0;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
   uint32_t ns = 32;
+  bool reached = false;
   for (uint32_t i = 0; i < (1u << 26); ++i) {
     uint32_t v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(done + lane) : "memory");
-    if ((int32_t)(v - epoch) >= 0) return;
+    if ((int32_t)(v - epoch) >= 0) {
+      reached = true;
+      break;
+    }
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     if (t - t0 > timeout_ns) break;
     __nanosleep(ns);
     if (ns < 1024) ns <<= 1;
   }
-  record_error(err, ERR_WAIT_TIMEOUT);
+  if (!reached) record_error(err, ERR_WAIT_TIMEOUT);
+  // lanes 0 .. world-1 are the ones still here
+  const unsigned lanes = world >= 32 ? 0xffffffffu : (1u << world) - 1u;
+  const bool all = __all_sync(lanes, reached);
+  if (epoch_word && lane == 0 && all) *(volatile uint32_t *)epoch_word = epoch;
 }
 
 static mgb_status to_outspec(const mgb_tp_out *o, uint64_t n, OutSpec &spec) {
@@ -62,6 +74,9 @@ static mgb_status to_outspec(const mgb_tp_out *o, uint64_t n, OutSpec &spec) {
     spec.done_ranks[r] = o->done[r];
   }
   spec.cta_counter = o->cta_counter;
+  // epoch 0: device epochs, from this rank's epoch word (the word after its
+  // CTA counter)
+  spec.epoch_src = o->epoch == 0 ? o->cta_counter + 1 : nullptr;
   spec.ldy = o->ldy;
   spec.col0 = o->col0;
   spec.epoch = o->epoch;
@@ -159,8 +174,11 @@ mgb_status mgb_tp_wait(const uint32_t *done, int32_t world, uint32_t epoch, uint
   int dev = 0;
   cudaGetDevice(&dev);
   const uint64_t ns = (uint64_t)(timeout_ms ? timeout_ms : 2000) * 1000000ull;
-  tp_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(done, world, epoch, ns,
-                                                                  device_error_flag(dev));
+  // epoch 0: device epochs (this rank's epoch word in its synchronisation words)
+  uint32_t *epoch_word =
+      epoch == 0 ? const_cast<uint32_t *>(done) + MGB_TP_EPOCH_OFFSET / 4 : nullptr;
+  tp_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(done, world, epoch, epoch_word,
+                                                                  ns, device_error_flag(dev));
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? MGB_OK : cuda_fail(e, "wait launch");
 }

@@ -83,6 +83,7 @@ class Observation(ctypes.Structure):
 MAX_TP = 8
 TP_SYNC_BYTES = 256
 TP_COUNTER_OFFSET = 128
+TP_EPOCH_OFFSET = 132  # device epochs: the rank's epoch word
 IPC_HANDLE_BYTES = 64
 
 

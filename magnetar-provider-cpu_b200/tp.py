@@ -133,7 +133,8 @@ class FusedShardedPackedMatmul(ShardedPackedMatmul):
     work queued before that call, including its reads of call e's result."""
 
     def __init__(self, fmt: int, ggml_shard: np.ndarray, n: int, k: int, world: int, rank: int,
-                 max_m: int, group=None, device=None, timeout_ms: int = 2000):
+                 max_m: int, group=None, device=None, timeout_ms: int = 2000,
+                 device_epochs: bool = False):
         import torch.distributed as dist
 
         import magnetar_b200 as mgb
@@ -142,6 +143,10 @@ class FusedShardedPackedMatmul(ShardedPackedMatmul):
         if world > mgb.MAX_TP:
             raise ValueError(f"at most {mgb.MAX_TP} ranks")
         self.max_m, self.group, self.timeout_ms = max_m, group, timeout_ms
+        # device epochs: the kernels and the wait take the epoch from this
+        # rank's epoch word, so calls captured in a CUDA graph (an even number
+        # of them, for the buffer alternation) replay with fresh epochs
+        self.device_epochs = device_epochs
         self._own: list[int] = []
         self._mapped: list[int] = []
         try:
@@ -190,8 +195,9 @@ class FusedShardedPackedMatmul(ShardedPackedMatmul):
             raise ValueError(f"{m} activation rows (1..{self.max_m})")
         self.epoch += 1
         slot = self.epoch & 1
+        epoch = 0 if self.device_epochs else self.epoch
         out = mgb.tp_out(self.y_slots[slot], self.done, self.sync + mgb.TP_COUNTER_OFFSET,
-                         ldy=self.n, col0=self.rank * self.n_loc, epoch=self.epoch, rank=self.rank)
+                         ldy=self.n, col0=self.rank * self.n_loc, epoch=epoch, rank=self.rank)
         ws_bytes = mgb.qmatmul_workspace_bytes(self.fmt, m, self.n_loc, self.k)
         if ws_bytes and (self._ws is None or self._ws.numel() < ws_bytes):
             self._ws = torch.empty(ws_bytes, dtype=torch.uint8, device=self.device)
@@ -199,7 +205,7 @@ class FusedShardedPackedMatmul(ShardedPackedMatmul):
         mgb.qmatmul_tp(self.fmt, self.weight.data_ptr(), self.n_loc, self.k, x.data_ptr(), m, out,
                        workspace_ptr=self._ws.data_ptr() if ws_bytes else 0,
                        workspace_bytes=ws_bytes, stream=stream)
-        mgb.tp_wait(self.sync, self.world, self.epoch, self.timeout_ms, stream)
+        mgb.tp_wait(self.sync, self.world, epoch, self.timeout_ms, stream)
         return torch.as_tensor(_DeviceArray(self.slots[slot], (m, self.n)), device=self.device)
 
     def close(self) -> None:

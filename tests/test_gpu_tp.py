@@ -125,6 +125,74 @@ def test_emulated_two_ranks_gather_every_column(torch_cuda, oracle, fmt, n, k, m
                         GEMV_TOL if m <= 2 else GEMM_TOL, f"tp fmt {fmt} m {m}")
 
 
+@pytest.mark.parametrize("fmt,n,k,m", [(synthetic.Q4_K, 512, 1024, 64),
+                                       (synthetic.Q4_K, 512, 1024, 1),
+                                       (synthetic.Q6_K, 256, 16384, 2)])
+def test_emulated_two_ranks_device_epochs_replay_in_a_graph(torch_cuda, fmt, n, k, m):
+    """Device epochs (epoch 0): each rank's kernels publish its epoch word + 1
+    and its wait advances the word, so the two ranks' calls and waits captured
+    in one CUDA graph publish fresh epochs on every replay.  Ranks are emulated
+    one after the other on one GPU, as above; every replay's gathered y equals
+    the unsharded call on that replay's activations."""
+    torch = torch_cuda
+    world = 2
+    w = synthetic.packed_weights(fmt, n, k, seed=23)
+    shards = [_device_layout(torch, fmt, tp.shard_packed(fmt, w, n, k, world, r), n // world, k)
+              for r in range(world)]
+    x = torch.zeros((m, k), dtype=torch.float32, device="cuda")
+    ys = [torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda") for _ in range(world)]
+    sync = [mgb.device_alloc(mgb.TP_SYNC_BYTES) for _ in range(world)]
+    ws_bytes = mgb.qmatmul_workspace_bytes(fmt, m, n // world, k)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+
+    def one_pass(sp):
+        for r in range(world):
+            out = mgb.tp_out([y.data_ptr() for y in ys], sync, sync[r] + mgb.TP_COUNTER_OFFSET,
+                             ldy=n, col0=r * (n // world), epoch=0, rank=r)
+            mgb.qmatmul_tp(fmt, shards[r].data_ptr(), n // world, k, x.data_ptr(), m, out,
+                           workspace_ptr=ws.data_ptr(), workspace_bytes=ws_bytes, stream=sp)
+        for r in range(world):
+            mgb.tp_wait(sync[r], world, 0, 2000, sp)
+
+    def epoch_words():
+        return [int(torch.as_tensor(tp._DeviceArray(s, (mgb.TP_SYNC_BYTES // 4,)), device="cuda")
+                    .view(torch.int32).cpu().numpy()[mgb.TP_EPOCH_OFFSET // 4]) for s in sync]
+
+    graph = None
+    try:
+        stream = torch.cuda.current_stream()
+        x.copy_(torch.from_numpy(synthetic.activations(m, k, seed=50)))
+        one_pass(stream.cuda_stream)  # eager: epoch 1
+        torch.cuda.synchronize()
+        assert epoch_words() == [1, 1]
+        cap = torch.cuda.Stream()
+        cap.wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(graph, stream=cap):
+                one_pass(torch.cuda.current_stream().cuda_stream)
+        stream.wait_stream(cap)
+        torch.cuda.synchronize()
+        assert epoch_words() == [1, 1]  # capturing runs nothing
+        for replay in range(3):
+            xh = synthetic.activations(m, k, seed=60 + replay)
+            x.copy_(torch.from_numpy(xh))
+            for y in ys:
+                y.fill_(float("nan"))
+            graph.replay()
+            torch.cuda.synchronize()
+            assert mgb.take_device_error(torch.cuda.current_device()) == 0
+            assert epoch_words() == [2 + replay] * world
+            got = [y.cpu().numpy() for y in ys]
+            np.testing.assert_array_equal(got[0], got[1])
+            np.testing.assert_array_equal(got[0], _unsharded(torch, fmt, w, n, k, x))
+    finally:
+        del graph
+        torch.cuda.synchronize()
+        for p in sync:
+            mgb.device_free(p)
+
+
 def test_wait_for_an_epoch_nobody_publishes_times_out(torch_cuda):
     """The bounded wait gives up, records device error 1 and the context stays usable."""
     torch = torch_cuda
