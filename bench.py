@@ -26,6 +26,8 @@ over one batch.  Metric: TFLOP/s (2*M*N*K per step), whole job.
   Wq/Wk/Wv/Wo/gate/up/down, Q4_K) at M = 1, 16, 64, and config 4, the
   Llama-3-70B layers (80 layers) at M = 1 and 2048: one CUDA graph per pass
   over every layer's own weights; weight GB/s and TFLOP/s (--no-stacks skips).
+  --tp-stacks adds the same passes under tensor parallelism (config 3 at M = 1, 16;
+  config 4 at M = 1, 2048): fused calls with device epochs, one CUDA graph per pass.
 - cpu_baseline: the reference's own CPU path (int8 activations, AVX2 kernels,
   persistent pool), restated in C (oracle/cpu_baseline.c), on a sample of
   the same workload, on every host core.
@@ -522,6 +524,75 @@ def run_b200(args) -> None:
             "timing": "CUDA events around replays of one CUDA graph holding one pass "
                       "(every projection of every layer once; weights far above L2)"}
 
+    def tp_stack(shapes: list[tuple[int, int]], layers: int, m: int) -> dict:
+        """A stack pass under tensor parallelism: every projection one fused
+        call on this rank's N/G stored rows (columns stored into every rank's
+        y, a stream-ordered wait for all ranks), with device epochs, the whole
+        pass captured as one CUDA graph.  One fused op per distinct shape, its
+        weight swapped for each layer's own copy (every shape is called an
+        even number of times per pass, so its two y buffers keep alternating
+        across replays)."""
+        ops = {}
+        graph = None
+        try:
+            for (n, k) in sorted(set(shapes)):
+                full = synthetic.packed_weights(fmt, n, k, seed=n + k)
+                ops[(n, k)] = tp.FusedShardedPackedMatmul(
+                    fmt, tp.shard_packed(fmt, full, n, k, world, rank), n, k, world, rank,
+                    max_m=m, device=dev, device_epochs=True)
+                del full
+            layer_w = [[ops[s].weight.clone() for s in shapes] for _ in range(layers)]
+            xs = {k: torch.from_numpy(synthetic.activations(m, k, seed=k)).to(dev)
+                  for k in sorted({k for _, k in shapes})}
+
+            def one_pass() -> None:
+                for lw in layer_w:
+                    for s, w in zip(shapes, lw):
+                        ops[s].weight = w
+                        ops[s](xs[s[1]])
+
+            one_pass()  # eager: workspaces allocated, kernels configured
+            torch.cuda.synchronize()
+            cap = torch.cuda.Stream(device=dev)
+            cap.wait_stream(stream)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(cap):
+                with torch.cuda.graph(graph, stream=cap):
+                    one_pass()
+            stream.wait_stream(cap)
+            probe = timed(lambda _i: graph.replay(), 1, 1)
+            reps = int(max(2, min(50, 1000.0 / max(probe, 1e-3))))
+            pass_ms = timed(lambda _i: graph.replay(), reps, 2) / reps
+            assert mgb.take_device_error(local) == 0, "a tensor-parallel wait gave up"
+            wbytes = layers * sum(mgb.packed_bytes(fmt, n, k) for n, k in shapes)
+            flops = 2.0 * m * layers * sum(n * k for n, k in shapes)
+            gbs = wbytes / (pass_ms * 1e-3) / 1e9
+            tfl = flops / (pass_ms * 1e-3) / 1e12
+            return {"m": m, "ms_per_pass": pass_ms, "tokens_per_s": m / (pass_ms * 1e-3),
+                    "weight_gbs": gbs, "weight_gbs_per_gpu": gbs / world,
+                    "frac_hbm_per_gpu": gbs / world / pk["hbm_gbs"], "tflops": tfl,
+                    "frac_bf16_per_gpu": tfl / world / pk["bf16_tflops_sustained"],
+                    "launches_per_pass": 3 * layers * len(shapes), "replays": reps}
+        finally:
+            del graph
+            for op in ops.values():
+                op.close()
+            torch.cuda.empty_cache()
+
+    tp_stacks = None
+    if args.tp_stacks:
+        l8 = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096),
+              (14336, 4096), (4096, 14336)]
+        l70 = [(8192, 8192), (1024, 8192), (1024, 8192), (8192, 8192), (28672, 8192),
+               (28672, 8192), (8192, 28672)]
+        tp_stacks = {
+            "config3": {"workload": f"Llama-3-8B decode stack, tp{world}",
+                        "passes": [tp_stack(l8, 32, mm) for mm in (1, 16)]},
+            "config4": {"workload": f"Llama-3-70B layers, tp{world}",
+                        "passes": [tp_stack(l70, 80, mm) for mm in (1, 2048)]},
+            "timing": "CUDA events around replays of one CUDA graph per pass (fused calls "
+                      "with device epochs), max over ranks"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(steps=10, warmup=1)
@@ -541,7 +612,8 @@ def run_b200(args) -> None:
                                       "mgb_tp_wait)" if world > 1 else "")},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": (3 if world > 1 else 2) * args.steps, "clocks": clocks,
-                "gemv": gemv, "formats": formats, "stacks": stacks, "tp_baseline_nccl": nccl}
+                "gemv": gemv, "formats": formats, "stacks": stacks, "tp_stacks": tp_stacks,
+                "tp_baseline_nccl": nccl}
         print(json.dumps(line), flush=True)
     if op is not None:
         op.close()
@@ -558,6 +630,9 @@ def main() -> None:
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-formats", action="store_true", help="skip the per-format table")
+    ap.add_argument("--tp-stacks", action="store_true",
+                    help="also time the config-3/4 stacks under tensor parallelism (CUDA graphs "
+                         "of fused calls; any N)")
     ap.add_argument("--no-stacks", action="store_true",
                     help="skip the config-3/4 projection stacks (one GPU)")
     args = ap.parse_args()

@@ -897,9 +897,11 @@ cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const fl
   e = launch_dependent(f32_to_bf16_kernel, dim3((unsigned)blocks), dim3(256), 0,
                                    stream, x, xb, m * k);
   if (e != cudaSuccess) return e;
-  // one output and room for the partial planes: split K
+  // one plain output and room for the partial planes: split K (a
+  // tensor-parallel call, even of one rank, publishes its completion from the
+  // GEMM's CTAs, which the sum pass would not do)
   const uint64_t base = gemm_workspace_bytes(fmt, m, n, k);
-  int s = out.world == 1 ? choose_split(m, n, k, sms) : 1;
+  int s = out.world == 1 && !out.cta_counter ? choose_split(m, n, k, sms) : 1;
   while (s > 1 && workspace_bytes < base + (uint64_t)s * m * n * 4) s /= 2;
   if (s > 1) {
     float *part = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + base);
@@ -929,7 +931,8 @@ cudaError_t launch_gemm_core(int fmt, const void *w, uint64_t n, uint64_t k, con
   if (!gemm_supported(fmt, m, n, k) || (reinterpret_cast<uintptr_t>(w) & 15) ||
       (reinterpret_cast<uintptr_t>(xb) & 15) ||
       (ksplit != 1 && ksplit != 2 && ksplit != 4 && ksplit != 8) ||
-      k % (256ull * ksplit) != 0 || (ksplit > 1 && (out.world != 1 || addend_mode != 0)))
+      k % (256ull * ksplit) != 0 ||
+      (ksplit > 1 && (out.world != 1 || out.cta_counter || addend_mode != 0)))
     return cudaErrorInvalidValue;
   const Layout L(fmt, n, k);
   const TileChoice t = choose_tiles(m, n, sms / ksplit);

@@ -193,6 +193,36 @@ def test_emulated_two_ranks_device_epochs_replay_in_a_graph(torch_cuda, fmt, n, 
             mgb.device_free(p)
 
 
+@pytest.mark.parametrize("m", [64, 1])
+@pytest.mark.parametrize("epoch", [1, 0])
+def test_one_rank_call_publishes_its_completion(torch_cuda, m, epoch):
+    """A tensor-parallel call of one rank runs one K pass (the split-K sum pass
+    publishes nothing) and publishes its epoch, host (1) or device (0), so its
+    wait returns at once and y equals the unsharded call."""
+    torch = torch_cuda
+    fmt, n, k = synthetic.Q4_K, 512, 1024
+    w = synthetic.packed_weights(fmt, n, k, seed=29)
+    wd = _device_layout(torch, fmt, w, n, k)
+    xd = torch.from_numpy(synthetic.activations(m, k, seed=30)).cuda()
+    y = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    sync = mgb.device_alloc(mgb.TP_SYNC_BYTES)
+    ws_bytes = mgb.qmatmul_workspace_bytes(fmt, m, n, k)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+    sp = torch.cuda.current_stream().cuda_stream
+    try:
+        out = mgb.tp_out([y.data_ptr()], [sync], sync + mgb.TP_COUNTER_OFFSET, ldy=n, col0=0,
+                         epoch=epoch, rank=0)
+        mgb.qmatmul_tp(fmt, wd.data_ptr(), n, k, xd.data_ptr(), m, out,
+                       workspace_ptr=ws.data_ptr(), workspace_bytes=ws_bytes, stream=sp)
+        mgb.tp_wait(sync, 1, epoch, 2000, sp)
+        torch.cuda.synchronize()
+        assert mgb.take_device_error(torch.cuda.current_device()) == 0
+        got = y.cpu().numpy()
+    finally:
+        mgb.device_free(sync)
+    np.testing.assert_array_equal(got, _unsharded(torch, fmt, w, n, k, xd))
+
+
 def test_wait_for_an_epoch_nobody_publishes_times_out(torch_cuda):
     """The bounded wait gives up, records device error 1 and the context stays usable."""
     torch = torch_cuda
