@@ -65,6 +65,8 @@ L2_BYTES = 126 * 1024 * 1024
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 METRIC = "Q4_K prefill GEMM TFLOP/s (X[512,4096] f32 x Q4_K W[14336x4096] -> f32)"
 WORKLOAD = "config1: Q4_K prefill GEMM M=512 K=4096 N=14336 (Llama-3-8B FFN gate/up)"
+GEMV_WORKLOAD = "config0: Q4_K decode GEMV x[1,4096] f32 x W[4096x4096] -> f32"
+GEMV_METRIC = "Q4_K decode GEMV weight GB/s (config0: x[1,4096] x W[4096x4096])"
 
 
 def peaks() -> tuple[dict, str]:
@@ -77,14 +79,25 @@ def peaks() -> tuple[dict, str]:
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def profile_traffic(name: str) -> float | None:
-    """DRAM bytes per launch from a committed ncu summary (profiles/<name>.md:
-    a line `dram_bytes_per_launch: <int>`), or None."""
-    path = ROOT / "profiles" / f"{name}.md"
-    if not path.exists():
-        return None
-    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", path.read_text())
-    return float(m.group(1)) if m else None
+# DRAM traffic measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum of one launch)
+# beside the algorithmic bytes of the same launch: the config-1 GEMM alone (bf16 x read,
+# packed W read; its f32 y stayed in L2 under the capture) and the config-0 GEMV (packed W,
+# f32 x and y).  The summaries and their commands are profiles/gemm_q4k_config1.md and
+# profiles/gemv_q4k_config0.md.  A launch of another size (a tensor-parallel shard)
+# reports the measured bytes scaled by its own algorithmic bytes: the traffic of these
+# kernels grows in proportion to the weight rows they stream.
+NCU_TRAFFIC = {
+    "gemm_q4k_config1": {"dram_bytes": 39_234_560, "algorithmic_bytes": 33_030_144 + 4_194_304},
+    "gemv_q4k_config0": {"dram_bytes": 9_489_920, "algorithmic_bytes": 9_469_952},
+}
+
+
+def scaled_traffic(name: str, algorithmic_bytes: float) -> dict:
+    ref = NCU_TRAFFIC[name]
+    return {"bytes_per_launch": ref["dram_bytes"] * algorithmic_bytes / ref["algorithmic_bytes"],
+            "basis": f"ncu dram bytes of {name} ({ref['dram_bytes']} B per launch) scaled by "
+                     f"this launch's algorithmic bytes ({algorithmic_bytes:.0f} / "
+                     f"{ref['algorithmic_bytes']})"}
 
 
 class ClockSampler:
@@ -143,7 +156,8 @@ class ClockSampler:
 
 def cpu_baseline(steps: int, warmup: int, budget_s: float = 20.0) -> dict:
     """Times the CPU port of the reference's default path (int8 activations,
-    AVX2 Q4_K kernel, pool over all host threads) on a column sample of config 1."""
+    AVX2 Q4_K kernel, pool over all host threads) on a column sample of config 1,
+    each call sized so that steps + warmup calls take about `budget_s`."""
     import numpy as np
 
     import synthetic
@@ -158,8 +172,7 @@ def cpu_baseline(steps: int, warmup: int, budget_s: float = 20.0) -> dict:
     t0 = time.perf_counter()
     oracle.baseline_packed_matmul(synthetic.Q4_K, w, ncols, K, x, int8=True, threads=threads)
     one = time.perf_counter() - t0
-    # size the sample so each timed call takes about budget / (steps + warmup) seconds
-    target = max(0.05, budget_s / max(1, steps + warmup))
+    target = max(0.02, budget_s / max(1, steps + warmup))
     ncols = int(min(N, max(64, ncols * target / max(one, 1e-6))) // 64 * 64) or 64
     w = synthetic.row_slice(synthetic.Q4_K, full, K, np.arange(ncols))
     for _ in range(warmup):
@@ -171,26 +184,64 @@ def cpu_baseline(steps: int, warmup: int, budget_s: float = 20.0) -> dict:
     flops = 2.0 * M * ncols * K
     return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
             "sample": f"M={M} K={K}, first {ncols} of {N} output columns per call, "
-                      f"{steps} timed calls of {dt * 1e3:.1f} ms after {warmup} warm-up",
+                      f"{steps} timed calls of {dt * 1e3:.2f} ms after {warmup} warm-up",
             "ms_per_call": dt * 1e3}
+
+
+def cpu_gemv_baseline(repeats: int = 10) -> dict:
+    """Config 0 on the CPU port of the reference's default path (M = 1, Q4_K
+    4096 x 4096, int8 activations, AVX2 kernel, pool over all host threads),
+    timed as the reference's own decode diagnostic times it
+    (`packed_matmul_bandwidth`, src/native/tests.rs:333-376: one warm-up call,
+    then the mean of `repeats` calls on the same weight; weight GB/s)."""
+    from oracle import oracle
+
+    import synthetic
+
+    threads = os.cpu_count() or 1
+    w = synthetic.packed_weights(synthetic.Q4_K, GEMV_N, GEMV_K)
+    x = synthetic.activations(1, GEMV_K)
+    oracle.baseline_packed_matmul(synthetic.Q4_K, w, GEMV_N, GEMV_K, x, int8=True, threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(repeats):
+        oracle.baseline_packed_matmul(synthetic.Q4_K, w, GEMV_N, GEMV_K, x, int8=True,
+                                      threads=threads)
+    dt = (time.perf_counter() - t0) / repeats
+    algo = w.size + GEMV_K * 4 + GEMV_N * 4
+    return {"value": algo / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"config 0 in full (x[1,{GEMV_K}] x Q4_K W[{GEMV_N}x{GEMV_K}]), one warm-up "
+                      f"then the mean of {repeats} calls on the same weight "
+                      "(the reference's packed_matmul_bandwidth method)",
+            "us_per_call": dt * 1e6}
+
+
+def config_dict() -> dict:
+    """The workload, identical in both arms (how each arm runs it is in `details`)."""
+    return {"workload": WORKLOAD, "m": M, "k": K, "n": N, "format": "Q4_K",
+            "gemv_workload": GEMV_WORKLOAD}
 
 
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return  # under torchrun only rank 0 runs the CPU arm
-    steps = max(1, min(args.steps, 20))
-    warmup = max(1, min(args.warmup, 3))
-    cb = cpu_baseline(steps, warmup)
+    steps, warmup = args.steps, args.warmup
+    cb = cpu_baseline(steps, warmup, budget_s=60.0)
+    gv = cpu_gemv_baseline()
     line = {"metric": METRIC, "value": cb["value"], "unit": "TFLOP/s", "n_gpus": args.gpus,
             "steps": steps, "warmup": warmup, "ms_per_step": cb["ms_per_call"],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int8 x u4 dots, f32 accumulate", "data": "synthetic", "impl": "reference",
-            "config": {"workload": WORKLOAD, "m": M, "k": K, "n": N, "format": "Q4_K",
-                       "parallelism": "cpu-threads"},
+            "config": config_dict(),
+            "details": {"parallelism": f"{cb['cores']} host threads (the reference's pool)",
+                        "step": "C port of the reference's packed_matmul: quantize_rows + "
+                                "columns_q4k_avx2 over the pool partition of "
+                                "src/native/mod.rs:135-150"},
             "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+                    "d2h_bytes_per_step": 0},
+            "gemv": {"metric": GEMV_METRIC, "value": gv["value"], "unit": "GB/s",
+                     "cpu_baseline": gv}}
     print(json.dumps(line), flush=True)
 
 
@@ -248,7 +299,8 @@ def run_b200(args) -> None:
 
     op = None
     if world > 1:
-        op = tp.FusedShardedPackedMatmul(fmt, w_loc, N, K, world, rank, max_m=M, device=dev)
+        op = tp.FusedShardedPackedMatmul(fmt, w_loc, N, K, world, rank, max_m=M, device=dev,
+                                         device_epochs=True)
 
     def step(i: int) -> None:
         s = i % R
@@ -259,14 +311,39 @@ def run_b200(args) -> None:
         mgb.qmatmul(fmt, W[s].data_ptr(), n_loc, K, X[s].data_ptr(), M, Y[s].data_ptr(),
                     workspace_ptr=WS.data_ptr(), workspace_bytes=ws_bytes, stream=sp)
 
+    # Under tensor parallelism the steps run as CUDA graphs of fused calls (device
+    # epochs), so the host's per-call work (ctypes, the output description) is out of
+    # the device's way: one graph of the W warm-up steps, one of the K timed steps,
+    # captured in that order and each replayed once, so the calls' y buffers keep
+    # alternating from one graph into the next.
+    graphs = {}
+    if op is not None:
+        step(0)  # eager: workspace allocated, kernels configured
+        torch.cuda.synchronize()
+        cap = torch.cuda.Stream(device=dev)
+        cap.wait_stream(stream)
+        for name, count in (("warm", args.warmup), ("timed", args.steps)):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(cap):
+                with torch.cuda.graph(g, stream=cap):
+                    for i in range(count):
+                        step(i)
+            graphs[name] = g
+        stream.wait_stream(cap)
+        torch.cuda.synchronize()
+
     def step_nccl(i: int) -> None:
         s = i % R
         mgb.qmatmul(fmt, W[s].data_ptr(), n_loc, K, X[s].data_ptr(), M, Y[s].data_ptr(),
                     workspace_ptr=WS.data_ptr(), workspace_bytes=ws_bytes, stream=sp)
         tp.gather_columns(Y[s])  # [M, N] on every rank
 
-    def timed(fn, steps: int, warmup: int) -> float:
-        for i in range(warmup):
+    def timed(fn, steps: int, warmup: int, whole=None) -> float:
+        """Device time of `steps` calls of fn after `warmup` untimed ones, max over
+        ranks; `whole` = (warm-up graph, timed graph) replaces the calls."""
+        if whole is not None:
+            whole[0].replay()
+        for i in range(warmup if whole is None else 0):
             fn(i)
         if world > 1:
             dist.barrier()
@@ -274,7 +351,9 @@ def run_b200(args) -> None:
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record(stream)
-        for i in range(steps):
+        if whole is not None:
+            whole[1].replay()
+        for i in range(steps if whole is None else 0):
             fn(i)
         t1.record(stream)
         torch.cuda.synchronize()
@@ -287,7 +366,11 @@ def run_b200(args) -> None:
 
     visible = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
     sampler = ClockSampler(visible[local] if local < len(visible) else str(local))
-    total_ms = timed(step, args.steps, args.warmup)
+    total_ms = timed(step, args.steps, args.warmup,
+                     (graphs["warm"], graphs["timed"]) if graphs else None)
+    if op is not None:
+        assert mgb.take_device_error(local) == 0, "a tensor-parallel wait gave up"
+        graphs.clear()
     ms_step = total_ms / args.steps
     flops = 2.0 * M * N * K
     value = flops / (ms_step * 1e-3) / 1e12
@@ -310,12 +393,12 @@ def run_b200(args) -> None:
     clocks = sampler.stop()
     pk, pk_kind = peaks()
     achieved = 2.0 * M * n_loc * K / (gemm_ms * 1e-3) / 1e12
-    traffic = profile_traffic("gemm_q4k_config1")
-    roofline = {"bound": "tensor", "kernel": "gemm_kernel<Q4_K> (tcgen05, bf16 x bf16 -> f32)",
+    tr = scaled_traffic("gemm_q4k_config1", w_bytes + M * K * 2)
+    roofline = {"bound": "tensor", "kernel": "mgb_gemm_kernel<Q4_K> (tcgen05, bf16 x bf16 -> f32)",
                 "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": achieved / pk["bf16_tflops"], "peak_kind": f"{pk_kind} burst bf16",
-                "traffic": traffic, "ms_per_launch": gemm_ms,
-                "flops_per_launch": 2.0 * M * n_loc * K}
+                "traffic": tr["bytes_per_launch"], "traffic_basis": tr["basis"],
+                "ms_per_launch": gemm_ms, "flops_per_launch": 2.0 * M * n_loc * K}
 
     # e2e with pinned host buffers: through the Provider's C ABI on one GPU,
     # through the fused tensor-parallel call on several
@@ -427,15 +510,17 @@ def run_b200(args) -> None:
         g_ms, gb, RV, reps = graph_ms(fmt, 1, GEMV_N, GEMV_K, max(args.steps, 200))
         algo = gb + GEMV_K * 4 + GEMV_N * 4
         gbs = algo / (g_ms * 1e-3) / 1e9
-        gemv = {"metric": "Q4_K decode GEMV weight GB/s (config0: x[1,4096] x W[4096x4096])",
-                "value": gbs, "unit": "GB/s", "us_per_launch": g_ms * 1e3,
-                "algorithmic_bytes": algo, "frac": gbs / pk["hbm_gbs"],
-                "peak": pk["hbm_gbs"], "peak_kind": f"{pk_kind} HBM copy",
+        tr = scaled_traffic("gemv_q4k_config0", algo)
+        gemv = {"metric": GEMV_METRIC, "value": gbs, "unit": "GB/s", "us_per_launch": g_ms * 1e3,
+                "algorithmic_bytes": algo,
+                "roofline": {"bound": "hbm", "kernel": "mgb_gemv_staged_kernel<Q4_K>",
+                             "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                             "frac": gbs / pk["hbm_gbs"], "peak_kind": f"{pk_kind} HBM copy",
+                             "traffic": tr["bytes_per_launch"], "traffic_basis": tr["basis"]},
                 "l2": f"{RV} rotating weight copies ({RV * gb / 1e6:.0f} MB > 3x L2)",
                 "timing": f"CUDA events around {reps} replays of a CUDA graph of {RV} "
-                          "back-to-back launches (activation pack + GEMV each, programmatic "
-                          "dependent launches)",
-                "traffic": profile_traffic("gemv_q4k_config0")}
+                          "back-to-back launches (programmatic dependent launches)",
+                "cpu_baseline": None}
 
         # every format the Provider executes, at config 2's shape (K = 4096,
         # N = 14336): decode GEMV (M = 1) weight GB/s and prefill step (M = 512,
@@ -580,7 +665,7 @@ def run_b200(args) -> None:
             torch.cuda.empty_cache()
 
     tp_stacks = None
-    if args.tp_stacks:
+    if args.tp_stacks or (world > 1 and not args.no_tp_stacks):
         l8 = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096),
               (14336, 4096), (4096, 14336)]
         l70 = [(8192, 8192), (1024, 8192), (1024, 8192), (8192, 8192), (28672, 8192),
@@ -596,20 +681,23 @@ def run_b200(args) -> None:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(steps=10, warmup=1)
+        if gemv is not None:
+            gemv["cpu_baseline"] = cpu_gemv_baseline()
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "bf16 operands, f32 accumulate", "data": "synthetic",
-                "config": {"workload": WORKLOAD, "m": M, "k": K, "n": N, "format": "Q4_K",
-                           "n_per_rank": n_loc, "parallelism": f"tp{world}",
-                           "l2": f"{R} rotating input sets of {set_bytes / 1e6:.0f} MB "
-                                 f"({R * set_bytes / 1e6:.0f} MB > 3x 126 MB L2)",
-                           "step": "mgb_qmatmul: f32->bf16 activation pass + tcgen05 GEMM"
-                                   + (" storing every column into every rank's y over NVLink "
-                                      "+ stream-ordered wait for all ranks (mgb_qmatmul_tp, "
-                                      "mgb_tp_wait)" if world > 1 else "")},
+                "config": config_dict(),
+                "details": {"n_per_rank": n_loc, "parallelism": f"tp{world}",
+                            "l2": f"{R} rotating input sets of {set_bytes / 1e6:.0f} MB "
+                                  f"({R * set_bytes / 1e6:.0f} MB > 3x 126 MB L2)",
+                            "step": "mgb_qmatmul: f32->bf16 activation pass + tcgen05 GEMM"
+                                    + (" storing every column into every rank's y over NVLink "
+                                       "+ stream-ordered wait for all ranks (mgb_qmatmul_tp, "
+                                       "mgb_tp_wait), device epochs; the warm-up and timed "
+                                       "steps each one CUDA graph" if world > 1 else "")},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": (3 if world > 1 else 2) * args.steps, "clocks": clocks,
                 "gemv": gemv, "formats": formats, "stacks": stacks, "tp_stacks": tp_stacks,
@@ -631,8 +719,10 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-formats", action="store_true", help="skip the per-format table")
     ap.add_argument("--tp-stacks", action="store_true",
-                    help="also time the config-3/4 stacks under tensor parallelism (CUDA graphs "
-                         "of fused calls; any N)")
+                    help="also time the config-3/4 stacks under tensor parallelism at N = 1 "
+                         "(CUDA graphs of fused calls; on by default at N > 1)")
+    ap.add_argument("--no-tp-stacks", action="store_true",
+                    help="skip the tensor-parallel config-3/4 stacks at N > 1")
     ap.add_argument("--no-stacks", action="store_true",
                     help="skip the config-3/4 projection stacks (one GPU)")
     args = ap.parse_args()

@@ -7,7 +7,8 @@
  * `ProviderExecutionApi` (defined in the crate `magnetar-provider-api`,
  * implemented by the reference at src/native/mod.rs:565-947) with plain
  * pointers and sizes, so a thin Rust `extern "C"` adapter can implement those
- * traits over this library (INTEGRATION.md shows the binding).
+ * traits over this library (the integration guide beside this header shows
+ * the binding).
  *
  * All entry points are thread-safe.  Tensors cross the boundary as host f32
  * buffers (copied in and out; the caller keeps ownership) or, for the
@@ -300,11 +301,16 @@ mgb_status mgb_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, co
  *  - the array is shared by every call on a device and keeps the last call's
  *    bytes: calls that may overlap on the GPU (different streams without
  *    ordering between them) race on it and corrupt each other's results;
- *  - the first call on a device resolves the array's device address (once,
- *    with that device current); make that first call before any stream
- *    capture;
- *  - nothing is allocated, and no device error word is attached: a bounded
- *    device wait that expires leaves y unspecified without a status. */
+ *  - the first call on a device resolves the device addresses of the array
+ *    and of its error word (once, with that device current); make that first
+ *    call before any stream capture.  The addresses belong to the device's
+ *    CUDA context: after cudaDeviceReset, or from another driver-API context
+ *    on the same device, they are stale, so do not call this entry point
+ *    there;
+ *  - nothing is allocated.  A bounded device wait that expires leaves y
+ *    unspecified and records 1 in a second fixed device word beside the
+ *    array, which mgb_take_device_error(device) reads and clears (that call
+ *    allocates nothing either). */
 #define MGB_STATIC_SCRATCH_BYTES (8u << 20)
 mgb_status mgb_qmatmul_static_scratch(int32_t format, const void *w, uint64_t n, uint64_t k,
                                       const float *x, uint64_t m, float *y, const float *addend,
@@ -332,9 +338,11 @@ mgb_status mgb_matmul_f32(const float *a, uint64_t a_rows, uint64_t a_cols, cons
                           uint64_t b_rows, uint64_t b_cols, int32_t transpose_a,
                           int32_t transpose_b, float *out, void *stream);
 /* Reads and clears the device error code the low-level kernels of `device`
- * record instead of trapping (1 = a bounded wait expired; 0 = none).
- * Synchronises with the device.  No counterpart in the reference (its kernels
- * run synchronously on the calling thread). */
+ * record instead of trapping (1 = a bounded wait expired; 0 = none), both the
+ * word of the calls that take a workspace and the word of
+ * mgb_qmatmul_static_scratch.  Synchronises with the device; allocates
+ * nothing.  No counterpart in the reference (its kernels run synchronously on
+ * the calling thread). */
 mgb_status mgb_take_device_error(int32_t device, int32_t *code);
 /* The `embedding` lookup in a packed table (`NativeState::embedding`,
  * src/native/mod.rs:389-417): out[count, dim] = the dequantised rows of the
@@ -423,7 +431,12 @@ mgb_status mgb_qmatmul_tp(int32_t format, const void *w, uint64_t n, uint64_t k,
  * `stream` sees every rank's columns.  `epoch` 0: device epochs, the rank's
  * epoch word + 1, and the word is advanced to it once every rank has reached
  * it.  A wait longer than timeout_ms (0: 2000) gives up and records device
- * error 1 (see mgb_take_device_error). */
+ * error 1 (see mgb_take_device_error).  After such an error the ranks' epochs
+ * disagree (the rank that gave up did not advance its epoch word, its peers
+ * may have), so every later wait would expire too: before the next call,
+ * every rank synchronises its stream, then all ranks zero their whole
+ * synchronisation area (MGB_TP_SYNC_BYTES: counter, epoch word and done
+ * words) and meet at a host barrier, and host epochs restart from 1. */
 mgb_status mgb_tp_wait(const uint32_t *done, int32_t world, uint32_t epoch, uint32_t timeout_ms,
                        void *stream);
 

@@ -74,7 +74,14 @@ mgb_status check_packed_shape(int32_t format, uint64_t rows, uint64_t cols) {
 namespace {
 std::mutex g_err_mu;
 int *g_err_flags[64] = {};
+
+// The flag of `device` if one was allocated (reading never allocates).
+int *existing_error_flag(int device) {
+  if (device < 0 || device >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(g_err_mu);
+  return g_err_flags[device];
 }
+}  // namespace
 
 int *device_error_flag(int device) {
   if (device < 0 || device >= 64) return nullptr;
@@ -313,13 +320,18 @@ mgb_status mgb_quantize_rows(const float *x, uint64_t len, int8_t *values, float
 mgb_status mgb_take_device_error(int32_t device, int32_t *code) {
   if (!code) return fail(MGB_INVALID_ARGUMENT, "null code pointer");
   *code = 0;
-  int *flag = device_error_flag(device);
-  if (!flag) return fail(MGB_CUDA_ERROR, "no error flag on device %d", device);
+  if (device < 0 || device >= 64) return fail(MGB_INVALID_ARGUMENT, "device %d out of range", device);
   int prev = 0;
-  cudaSetDevice(device);
-  cudaError_t e = cudaMemcpy(&prev, flag, sizeof(int), cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) return cuda_fail(e, "reading the device error flag");
-  if (prev) cudaMemset(flag, 0, sizeof(int));
+  mgb_status s = take_static_scratch_error(device, &prev);
+  if (s != MGB_OK) return s;
+  if (int *flag = existing_error_flag(device)) {
+    int word = 0;
+    cudaError_t e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaMemcpy(&word, flag, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "reading the device error flag");
+    if (word) cudaMemset(flag, 0, sizeof(int));
+    if (!prev) prev = word;
+  }
   *code = prev;
   return MGB_OK;
 }

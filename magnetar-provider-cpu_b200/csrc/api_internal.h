@@ -21,6 +21,8 @@ uint64_t ggml_bytes(int32_t format, uint64_t rows, uint64_t cols);
 uint64_t device_bytes(int32_t format, uint64_t rows, uint64_t cols);
 mgb_status check_packed_shape(int32_t format, uint64_t rows, uint64_t cols);
 int *device_error_flag(int device);
+// the error word of mgb_qmatmul_static_scratch on `device` (read and cleared)
+mgb_status take_static_scratch_error(int device, int *code);
 
 mgb_status validate_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, const float *x,
                             uint64_t m, float *y);

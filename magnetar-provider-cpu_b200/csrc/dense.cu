@@ -9,7 +9,7 @@ namespace mgb {
 
 // out[m, n] = op(a)[m, k] * op(b)[k, n], strides as src/lib.rs:291-302.
 // 64x64 output tile per 256-thread CTA, 4x4 per thread, k in steps of 16.
-__global__ void __launch_bounds__(256) matmul_f32_kernel(
+__global__ void __launch_bounds__(256) mgb_matmul_f32_kernel(
     const float *__restrict__ a, const float *__restrict__ b, uint64_t m, uint64_t n, uint64_t k,
     uint64_t a_row_stride, uint64_t a_inner_stride, uint64_t b_inner_stride,
     uint64_t b_col_stride, float *__restrict__ out) {
@@ -59,12 +59,12 @@ cudaError_t launch_matmul_f32(const float *a, uint64_t a_rows, uint64_t a_cols, 
   const uint64_t b_inner = transpose_b ? 1 : b_cols, b_col = transpose_b ? b_cols : 1;
   if (!m || !n) return cudaSuccess;
   dim3 grid((unsigned)ceil_div(n, 64), (unsigned)ceil_div(m, 64));
-  matmul_f32_kernel<<<grid, 256, 0, stream>>>(a, b, m, n, k, a_row_stride, a_inner, b_inner,
+  mgb_matmul_f32_kernel<<<grid, 256, 0, stream>>>(a, b, m, n, k, a_row_stride, a_inner, b_inner,
                                               b_col, out);
   return cudaGetLastError();
 }
 
-__global__ void transpose_kernel(const float *__restrict__ in, uint64_t rows, uint64_t cols,
+__global__ void mgb_transpose_kernel(const float *__restrict__ in, uint64_t rows, uint64_t cols,
                                  float *__restrict__ out) {
   __shared__ float tile[32][33];
   const uint64_t c0 = (uint64_t)blockIdx.x * 32, r0 = (uint64_t)blockIdx.y * 32;
@@ -83,12 +83,12 @@ cudaError_t launch_transpose(const float *in, uint64_t rows, uint64_t cols, floa
                              cudaStream_t stream) {
   if (!rows || !cols) return cudaSuccess;
   dim3 grid((unsigned)ceil_div(cols, 32), (unsigned)ceil_div(rows, 32));
-  transpose_kernel<<<grid, dim3(32, 8), 0, stream>>>(in, rows, cols, out);
+  mgb_transpose_kernel<<<grid, dim3(32, 8), 0, stream>>>(in, rows, cols, out);
   return cudaGetLastError();
 }
 
 // y = y + addend, addend of y's length or one row of `cols` broadcast.
-__global__ void add_kernel(float *__restrict__ y, uint64_t len, const float *__restrict__ addend,
+__global__ void mgb_add_kernel(float *__restrict__ y, uint64_t len, const float *__restrict__ addend,
                            uint64_t addend_len, uint64_t cols) {
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < len;
        i += (uint64_t)gridDim.x * blockDim.x)
@@ -99,14 +99,14 @@ cudaError_t launch_add(float *y, uint64_t len, const float *addend, uint64_t add
                        uint64_t cols, cudaStream_t stream) {
   if (!len) return cudaSuccess;
   const uint64_t blocks = ceil_div(len, 256);
-  add_kernel<<<(unsigned)(blocks > 4096 ? 4096 : blocks), 256, 0, stream>>>(y, len, addend,
+  mgb_add_kernel<<<(unsigned)(blocks > 4096 ? 4096 : blocks), 256, 0, stream>>>(y, len, addend,
                                                                            addend_len, cols);
   return cudaGetLastError();
 }
 
 // One warp per 32-value block: amax, d = amax / 127 (a division, as the
 // reference), q = round-half-even(x / d), per-16 sums.
-__global__ void quantize_rows_kernel(const float *__restrict__ x, uint64_t blocks,
+__global__ void mgb_quantize_rows_kernel(const float *__restrict__ x, uint64_t blocks,
                                      int8_t *__restrict__ values, float *__restrict__ scales,
                                      int32_t *__restrict__ sums, float *__restrict__ rounded) {
   const int lane = threadIdx.x & 31;
@@ -138,7 +138,7 @@ cudaError_t launch_quantize_rows(const float *x, uint64_t len, int8_t *values, f
   const uint64_t blocks = len / 32;
   if (!blocks) return cudaSuccess;
   const uint64_t ctas = ceil_div(blocks, 8);
-  quantize_rows_kernel<<<(unsigned)(ctas > 8192 ? 8192 : ctas), 256, 0, stream>>>(
+  mgb_quantize_rows_kernel<<<(unsigned)(ctas > 8192 ? 8192 : ctas), 256, 0, stream>>>(
       x, blocks, values, scales, sums, nullptr);
   return cudaGetLastError();
 }
@@ -147,7 +147,7 @@ cudaError_t launch_int8_rounded(const float *x, uint64_t len, float *out, cudaSt
   const uint64_t blocks = len / 32;
   if (!blocks) return cudaSuccess;
   const uint64_t ctas = ceil_div(blocks, 8);
-  quantize_rows_kernel<<<(unsigned)(ctas > 8192 ? 8192 : ctas), 256, 0, stream>>>(
+  mgb_quantize_rows_kernel<<<(unsigned)(ctas > 8192 ? 8192 : ctas), 256, 0, stream>>>(
       x, blocks, nullptr, nullptr, nullptr, out);
   return cudaGetLastError();
 }

@@ -34,7 +34,7 @@
 //              all-gather over NVLink), through shared memory in whole row
 //              segments.
 // Up to 128 activation rows, a call may split K over 2, 4 or 8 CTAs per tile
-// (blockIdx.z), each writing an f32 partial plane that splitk_sum_kernel adds.
+// (blockIdx.z), each writing an f32 partial plane that mgb_splitk_sum_kernel adds.
 // Every CTA loads its own tiles from this GPU's HBM (no cluster-shared loads).
 // Every wait is bounded; on expiry the kernel records ERR_WAIT_TIMEOUT, skips
 // the remaining work, waits (bounded) for its own copies and MMAs, frees TMEM
@@ -507,7 +507,7 @@ __device__ __forceinline__ void grid_launch_dependents() {
 // AT: 64-value K atoms per pipeline stage (1 or 2).
 template <int FMT, int SUBS, int DQW, int AT>
 __global__ void __launch_bounds__(96 + 32 * DQW, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_wq,
+    mgb_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_wq,
                 const __grid_constant__ CUtensorMap map_ws, const __grid_constant__ CUtensorMap map_y,
                 const GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -741,7 +741,7 @@ __global__ void __launch_bounds__(96 + 32 * DQW, 1)
 
 // f32 -> bf16 activations; lets the dependent GEMM launch at once (its weight
 // stream and dequantisation overlap this pass; its activation loads wait).
-__global__ void f32_to_bf16_kernel(const float *__restrict__ x, __nv_bfloat16 *__restrict__ out,
+__global__ void mgb_f32_to_bf16_kernel(const float *__restrict__ x, __nv_bfloat16 *__restrict__ out,
                                    uint64_t n) {
   grid_launch_dependents();
   grid_dependency_wait();
@@ -758,7 +758,7 @@ __global__ void f32_to_bf16_kernel(const float *__restrict__ x, __nv_bfloat16 *_
 
 // Split-K: y = the partial planes summed in plane order (+ the addend); a
 // programmatic dependent of the GEMM that wrote them.
-__global__ void splitk_sum_kernel(const float *__restrict__ part, int planes, uint64_t m,
+__global__ void mgb_splitk_sum_kernel(const float *__restrict__ part, int planes, uint64_t m,
                                   uint64_t n, float *__restrict__ y,
                                   const float *__restrict__ addend, int addend_mode) {
   grid_launch_dependents();
@@ -890,11 +890,11 @@ cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const fl
   uint64_t blocks = ceil_div(n4, 256);
   if (blocks > (uint64_t)sms * 16) blocks = (uint64_t)sms * 16;
   // same shared-memory carveout as the GEMM: no SM reconfiguration between them
-  cudaError_t e = cudaFuncSetAttribute(f32_to_bf16_kernel,
+  cudaError_t e = cudaFuncSetAttribute(mgb_f32_to_bf16_kernel,
                                        cudaFuncAttributePreferredSharedMemoryCarveout,
                                        (int)cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) return e;
-  e = launch_dependent(f32_to_bf16_kernel, dim3((unsigned)blocks), dim3(256), 0,
+  e = launch_dependent(mgb_f32_to_bf16_kernel, dim3((unsigned)blocks), dim3(256), 0,
                                    stream, x, xb, m * k);
   if (e != cudaSuccess) return e;
   // one plain output and room for the partial planes: split K (a
@@ -909,7 +909,7 @@ cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const fl
     if (e == cudaSuccess) {
       uint64_t sblocks = ceil_div(m * n, 256);
       if (sblocks > (uint64_t)sms * 8) sblocks = (uint64_t)sms * 8;
-      e = launch_dependent(splitk_sum_kernel, dim3((unsigned)sblocks), dim3(256), 0, stream,
+      e = launch_dependent(mgb_splitk_sum_kernel, dim3((unsigned)sblocks), dim3(256), 0, stream,
                            (const float *)part, s, m, n, out.y_ranks[0], addend, addend_mode);
     }
     return e;
@@ -1045,9 +1045,9 @@ cudaError_t launch_gemm_core(int fmt, const void *w, uint64_t n, uint64_t k, con
   } while (0)
 #define MGB_GEMM_FMT(F)                                     \
   case F:                                                   \
-    if (t.subs == 2) MGB_GEMM_LAUNCH((gemm_kernel<F, 2, 16, 1>));       \
-    else if (two) MGB_GEMM_LAUNCH((gemm_kernel<F, 1, 16, 2>));         \
-    else MGB_GEMM_LAUNCH((gemm_kernel<F, 1, 16, 1>));                  \
+    if (t.subs == 2) MGB_GEMM_LAUNCH((mgb_gemm_kernel<F, 2, 16, 1>));       \
+    else if (two) MGB_GEMM_LAUNCH((mgb_gemm_kernel<F, 1, 16, 2>));         \
+    else MGB_GEMM_LAUNCH((mgb_gemm_kernel<F, 1, 16, 1>));                  \
     break;
   switch (fmt) {
     MGB_GEMM_FMT(Q4_K)

@@ -487,7 +487,7 @@ struct GemvStaged {
 
 template <int FMT, int MR, int MAXT, int MINB>
 __global__ void __launch_bounds__(MAXT, MINB)
-    gemv_staged_kernel(const uint8_t *__restrict__ w, const float *__restrict__ x,
+    mgb_gemv_staged_kernel(const uint8_t *__restrict__ w, const float *__restrict__ x,
                        const GemvStaged p) {
   constexpr int RPT = rows_per_team<FMT, MR, MAXT>();
   extern __shared__ __align__(128) uint8_t smem[];
@@ -655,7 +655,7 @@ __global__ void __launch_bounds__(MAXT, MINB)
 
 template <int FMT, int MR, int R, int MAXT>
 __global__ void __launch_bounds__(MAXT, 1)
-    gemv_simple_kernel(const uint8_t *__restrict__ w, int n, int k, const float *__restrict__ x,
+    mgb_gemv_simple_kernel(const uint8_t *__restrict__ w, int n, int k, const float *__restrict__ x,
                        const OutSpec out, const float *__restrict__ addend, int addend_mode,
                        int rows_per_cta) {
   __shared__ float red[2][32][R * MR];
@@ -824,7 +824,7 @@ static cudaError_t launch_staged(const void *w, int n, int k, const float *x, co
   p.addend = addend;
   p.out = out;
   p.err = err;
-  auto kern = gemv_staged_kernel<FMT, MR, MAXT, MINB>;
+  auto kern = mgb_gemv_staged_kernel<FMT, MR, MAXT, MINB>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   return launch_dependent(kern, dim3((unsigned)grid), dim3((unsigned)threads), smem, stream,
@@ -844,7 +844,7 @@ static cudaError_t launch_simple(const void *w, int n, int k, const float *x, co
   int rows = (int)ceil_div((uint64_t)n, (uint64_t)target);
   if (rows < 1) rows = 1;
   const int grid = (int)ceil_div((uint64_t)n, (uint64_t)rows);
-  gemv_simple_kernel<FMT, MR, R, MAXT><<<grid, threads, 0, stream>>>(
+  mgb_gemv_simple_kernel<FMT, MR, R, MAXT><<<grid, threads, 0, stream>>>(
       static_cast<const uint8_t *>(w), n, k, x, out, addend, addend_mode, rows);
   return cudaGetLastError();
 }

@@ -34,7 +34,7 @@ __device__ void write_k_header(const uint8_t *blk, uint8_t *out) {
 
 // One thread per 32-value run: gathers the run's quants from its ggml block and
 // writes them as 16 (or 32) bytes holding values (2i, 2i+1) in byte i.
-__global__ void repack_kernel(int fmt, const uint8_t *__restrict__ src, uint64_t n, uint64_t k,
+__global__ void mgb_repack_kernel(int fmt, const uint8_t *__restrict__ src, uint64_t n, uint64_t k,
                               uint8_t *__restrict__ dst) {
   const uint64_t runs_per_row = k / RUN;
   const uint64_t total = n * runs_per_row;
@@ -218,7 +218,7 @@ __device__ __forceinline__ void decode_run(int fmt, const uint8_t *__restrict__ 
   }
 }
 
-__global__ void dequantize_kernel(int fmt, const uint8_t *__restrict__ w, uint64_t n, uint64_t k,
+__global__ void mgb_dequantize_kernel(int fmt, const uint8_t *__restrict__ w, uint64_t n, uint64_t k,
                                   float *__restrict__ out) {
   const Layout L(fmt, n, k);
   const uint64_t runs_per_row = k / RUN, total = n * runs_per_row;
@@ -242,7 +242,7 @@ __global__ void dequantize_kernel(int fmt, const uint8_t *__restrict__ w, uint64
 // stored rows are the k input rows, y[m, n_cols].  One thread per (output row
 // r, output column c); sums x[r, j] * value(j, c) over j in order, skipping
 // x == 0 like the reference.
-__global__ void input_major_kernel(int fmt, const uint8_t *__restrict__ w, uint64_t k_rows,
+__global__ void mgb_input_major_kernel(int fmt, const uint8_t *__restrict__ w, uint64_t k_rows,
                                    uint64_t n_cols, const float *__restrict__ x, uint64_t m,
                                    float *__restrict__ y) {
   const Layout L(fmt, k_rows, n_cols);
@@ -279,7 +279,7 @@ __device__ __forceinline__ bool valid_token(float raw, uint64_t vocab) {
 // or stored row j, column token_t of a transposed [dim, vocab] one.  One
 // thread per output element.  An invalid id writes zeros for its row and
 // records its position (the smallest one wins) in *bad.
-__global__ void embedding_kernel(int fmt, const uint8_t *__restrict__ w, uint64_t stored_rows,
+__global__ void mgb_embedding_kernel(int fmt, const uint8_t *__restrict__ w, uint64_t stored_rows,
                                  uint64_t stored_cols, int transposed, const float *__restrict__ ids,
                                  uint64_t count, int has_scale, float scale, float *__restrict__ out,
                                  uint32_t *bad) {
@@ -310,7 +310,7 @@ __global__ void embedding_kernel(int fmt, const uint8_t *__restrict__ w, uint64_
 
 // The same lookup in an f32 table [vocab, dim] (`f32_embedding`,
 // src/native/mod.rs:238-263), with the optional scale.
-__global__ void embedding_f32_kernel(const float *__restrict__ table, uint64_t vocab, uint64_t dim,
+__global__ void mgb_embedding_f32_kernel(const float *__restrict__ table, uint64_t vocab, uint64_t dim,
                                      const float *__restrict__ ids, uint64_t count, int has_scale,
                                      float scale, float *__restrict__ out, uint32_t *bad) {
   const uint64_t total = count * dim;
@@ -335,14 +335,14 @@ static int grid_for(uint64_t work, int threads) {
 
 cudaError_t launch_repack(int fmt, const void *src, uint64_t n, uint64_t k, void *dst,
                           cudaStream_t stream) {
-  repack_kernel<<<grid_for(n * (k / RUN), 256), 256, 0, stream>>>(
+  mgb_repack_kernel<<<grid_for(n * (k / RUN), 256), 256, 0, stream>>>(
       fmt, static_cast<const uint8_t *>(src), n, k, static_cast<uint8_t *>(dst));
   return cudaGetLastError();
 }
 
 cudaError_t launch_dequantize(int fmt, const void *w, uint64_t n, uint64_t k, float *out,
                               cudaStream_t stream) {
-  dequantize_kernel<<<grid_for(n * (k / RUN), 256), 256, 0, stream>>>(
+  mgb_dequantize_kernel<<<grid_for(n * (k / RUN), 256), 256, 0, stream>>>(
       fmt, static_cast<const uint8_t *>(w), n, k, out);
   return cudaGetLastError();
 }
@@ -356,7 +356,7 @@ cudaError_t launch_embedding(int fmt, const void *w, uint64_t stored_rows, uint6
   }
   const uint64_t dim = transposed ? stored_rows : stored_cols;
   if (count * dim == 0) return cudaSuccess;
-  embedding_kernel<<<grid_for(count * dim, 256), 256, 0, stream>>>(
+  mgb_embedding_kernel<<<grid_for(count * dim, 256), 256, 0, stream>>>(
       fmt, static_cast<const uint8_t *>(w), stored_rows, stored_cols, transposed, ids, count,
       has_scale, scale, out, bad);
   return cudaGetLastError();
@@ -370,14 +370,14 @@ cudaError_t launch_embedding_f32(const float *table, uint64_t vocab, uint64_t di
     if (e != cudaSuccess) return e;
   }
   if (count * dim == 0) return cudaSuccess;
-  embedding_f32_kernel<<<grid_for(count * dim, 256), 256, 0, stream>>>(table, vocab, dim, ids, count,
+  mgb_embedding_f32_kernel<<<grid_for(count * dim, 256), 256, 0, stream>>>(table, vocab, dim, ids, count,
                                                                       has_scale, scale, out, bad);
   return cudaGetLastError();
 }
 
 cudaError_t launch_input_major(int fmt, const void *w, uint64_t k_rows, uint64_t n_cols,
                                const float *x, uint64_t m, float *y, cudaStream_t stream) {
-  input_major_kernel<<<grid_for(m * n_cols, 256), 256, 0, stream>>>(
+  mgb_input_major_kernel<<<grid_for(m * n_cols, 256), 256, 0, stream>>>(
       fmt, static_cast<const uint8_t *>(w), k_rows, n_cols, x, m, y);
   return cudaGetLastError();
 }

@@ -18,25 +18,55 @@ namespace {
 // with m * k <= 4,194,304 (e.g. 512 x 8192 or 1024 x 4096).
 __device__ __align__(256) static unsigned char g_static_scratch[MGB_STATIC_SCRATCH_BYTES];
 
+// The device error word of the calls above (1 = a bounded device wait gave
+// up), beside the array: read and cleared by mgb_take_device_error.
+__device__ static int g_static_error;
+
 std::mutex g_mu;
 void *g_scratch_ptr[64] = {};
+int *g_error_ptr[64] = {};
 
-// The array's device address for `device` (the current device), resolved once
-// per device; host code may not use the symbol itself as a device address.
-mgb_status scratch_address(int device, void **out) {
+// The device addresses of the array and of the error word for `device` (the
+// current device), resolved once per device; host code may not use the
+// symbols themselves as device addresses.
+mgb_status scratch_address(int device, void **out, int **err) {
   if (device < 0 || device >= 64) return fail(MGB_INVALID_ARGUMENT, "device %d out of range", device);
   std::lock_guard<std::mutex> lock(g_mu);
   if (!g_scratch_ptr[device]) {
-    void *p = nullptr;
+    void *p = nullptr, *q = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
+    e = cudaGetSymbolAddress(&q, g_static_error);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static error word)");
+    g_error_ptr[device] = static_cast<int *>(q);
     g_scratch_ptr[device] = p;
   }
   *out = g_scratch_ptr[device];
+  *err = g_error_ptr[device];
   return MGB_OK;
 }
 
 }  // namespace
+
+// Reads and clears the error word of the static-scratch calls on `device`
+// (0 when that device has made none).  Allocates nothing.
+mgb_status take_static_scratch_error(int device, int *code) {
+  *code = 0;
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (device < 0 || device >= 64 || !g_error_ptr[device]) return MGB_OK;
+  }
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(code, g_static_error, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "reading the static scratch error word");
+  if (*code) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_static_error, &zero, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "clearing the static scratch error word");
+  }
+  return MGB_OK;
+}
+
 }  // namespace mgb
 
 using namespace mgb;
@@ -67,12 +97,13 @@ extern "C" mgb_status mgb_qmatmul_static_scratch(int32_t format, const void *w, 
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   void *scratch = nullptr;
-  s = scratch_address(dev, &scratch);
+  int *err = nullptr;
+  s = scratch_address(dev, &scratch, &err);
   if (s != MGB_OK) return s;
   // The scratch is fully rewritten by each call before it is read (nothing in
-  // it has to start at zero).  No error word is passed: a bounded device wait
-  // that expires leaves y unspecified and is not reported through this call.
+  // it has to start at zero).  A bounded device wait that expires records 1 in
+  // the static error word (mgb_take_device_error reads it).
   return run_qmatmul(format, w, n, k, x, m, plain_out(y, n), addend, mode, scratch,
-                     MGB_STATIC_SCRATCH_BYTES, nullptr, MGB_KERNEL_AUTO,
+                     MGB_STATIC_SCRATCH_BYTES, err, MGB_KERNEL_AUTO,
                      static_cast<cudaStream_t>(stream));
 }

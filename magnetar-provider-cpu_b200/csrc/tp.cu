@@ -27,7 +27,7 @@ static_assert(sizeof(cudaIpcMemHandle_t) == MGB_IPC_HANDLE_BYTES, "IPC handle si
 // epoch_word set (device epochs) the epoch is *epoch_word + 1, and once every
 // rank has reached it lane 0 advances *epoch_word to it (a wait that gives up
 // leaves it, and the error recorded).
-__global__ void tp_wait_kernel(const uint32_t *done, int world, uint32_t epoch,
+__global__ void mgb_tp_wait_kernel(const uint32_t *done, int world, uint32_t epoch,
                                uint32_t *epoch_word, uint64_t timeout_ns, int *err) {
   const int lane = threadIdx.x;
   if (lane >= world) return;
@@ -177,7 +177,7 @@ mgb_status mgb_tp_wait(const uint32_t *done, int32_t world, uint32_t epoch, uint
   // epoch 0: device epochs (this rank's epoch word in its synchronisation words)
   uint32_t *epoch_word =
       epoch == 0 ? const_cast<uint32_t *>(done) + MGB_TP_EPOCH_OFFSET / 4 : nullptr;
-  tp_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(done, world, epoch, epoch_word,
+  mgb_tp_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(done, world, epoch, epoch_word,
                                                                   ns, device_error_flag(dev));
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? MGB_OK : cuda_fail(e, "wait launch");

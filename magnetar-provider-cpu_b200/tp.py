@@ -208,6 +208,28 @@ class FusedShardedPackedMatmul(ShardedPackedMatmul):
         mgb.tp_wait(self.sync, self.world, epoch, self.timeout_ms, stream)
         return torch.as_tensor(_DeviceArray(self.slots[slot], (m, self.n)), device=self.device)
 
+    def reset(self) -> None:
+        """Recovery after a wait gave up (device error 1, a peer that never
+        published): the ranks' epochs then disagree and every later wait would
+        expire too.  Collective: every rank drains its stream, all ranks zero
+        their synchronisation words (counter, epoch word, done words) between
+        two barriers, and epochs restart from 1."""
+        import torch
+        import torch.distributed as dist
+
+        import magnetar_b200 as mgb
+
+        multi = self.world > 1 and dist.is_initialized()
+        torch.cuda.synchronize(self.device)
+        if multi:
+            dist.barrier(group=self.group)
+        torch.as_tensor(_DeviceArray(self.sync, (mgb.TP_SYNC_BYTES // 4,)),
+                        device=self.device).zero_()
+        torch.cuda.synchronize(self.device)
+        if multi:
+            dist.barrier(group=self.group)
+        self.epoch = 0
+
     def close(self) -> None:
         """Unmaps the peers' buffers and frees this rank's.  Collective: every
         rank calls it (no peer may still be writing into this rank's buffers)."""

@@ -253,7 +253,8 @@ void orc_quantize_rows(const float *rows, uint64_t len, int8_t *values, float *s
             int8_t q = 0;
             if (amax != 0.0f) {
                 float r = nearbyintf(x[i] / d); /* default rounding: ties to even */
-                q = (int8_t)(r > 127.0f ? 127 : (r < -128.0f ? -128 : r));
+                /* Rust's `as i8` saturates and maps NaN to 0 */
+                q = isnan(r) ? 0 : (int8_t)(r > 127.0f ? 127 : (r < -128.0f ? -128 : r));
             }
             values[b * ORC_RUN + i] = q;
             s[i / 16] += q;

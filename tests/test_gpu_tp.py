@@ -237,6 +237,37 @@ def test_wait_for_an_epoch_nobody_publishes_times_out(torch_cuda):
         mgb.device_free(sync)
 
 
+@pytest.mark.parametrize("device_epochs", [False, True])
+def test_reset_after_an_expired_wait(torch_cuda, device_epochs):
+    """A wait that gave up leaves the epochs disagreeing; `reset` (every rank
+    zeroes its synchronisation words between barriers) makes the next call
+    publish and complete again, with the unsharded result."""
+    torch = torch_cuda
+    fmt, n, k, m = synthetic.Q4_K, 512, 1024, 2
+    w = synthetic.packed_weights(fmt, n, k, seed=41)
+    xd = torch.from_numpy(synthetic.activations(m, k, seed=42)).cuda()
+    op = tp.FusedShardedPackedMatmul(fmt, w, n, k, 1, 0, max_m=m, device_epochs=device_epochs)
+    dev = torch.cuda.current_device()
+    try:
+        ref = _unsharded(torch, fmt, w, n, k, xd)
+        assert np.array_equal(op(xd).cpu().numpy(), ref)
+        assert mgb.take_device_error(dev) == 0
+        # a peer that never publishes: wait for an epoch nobody reaches
+        mgb.tp_wait(op.sync, 1, op.epoch + 5, timeout_ms=20,
+                    stream=torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert mgb.take_device_error(dev) == 1
+        op.reset()
+        words = torch.as_tensor(tp._DeviceArray(op.sync, (mgb.TP_SYNC_BYTES // 4,)),
+                                device="cuda").view(torch.int32).cpu().numpy()
+        assert not words.any() and op.epoch == 0
+        for _ in range(3):
+            assert np.array_equal(op(xd).cpu().numpy(), ref)
+        assert mgb.take_device_error(dev) == 0
+    finally:
+        op.close()
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))

@@ -244,3 +244,43 @@ def test_cpu_baseline_port_matches_the_oracle(oracle, fmt, threads):
         a = oracle.test_activations(2, 96, 7)
         oracle.assert_close(oracle.baseline_packed_matmul(fmt, w, 5, 96, a, threads=threads),
                             oracle.packed_matmul(fmt, w, 5, 96, a, int8=True), 2e-5)
+
+
+def quantize_edge_rows() -> np.ndarray:
+    """Activation blocks that probe `quantize_rows` (src/native/quant.rs:350-378):
+    N(0, 1) rows, an all-zero block, exact ties at .5 (amax 127 makes d = 1),
+    +-amax at both ends, a NaN and an infinity (amax then ignores the NaN, and
+    inf / inf is NaN, which `as i8` maps to 0)."""
+    rng = np.random.default_rng(0x5EED)
+    blocks = [rng.standard_normal(32 * 64, dtype=np.float32).reshape(-1, 32)]
+    blocks.append(np.zeros((1, 32), np.float32))
+    ties = np.array([127.0, -127.0, 2.5, 3.5, -2.5, -3.5, 0.5, -0.5, 1.5, -1.5, 126.5, -126.5]
+                    + [4.5] * 20, np.float32)
+    blocks.append(ties[None])
+    amax = rng.standard_normal(32).astype(np.float32)
+    amax[0], amax[31] = 7.25, -7.25
+    blocks.append(amax[None])
+    nan = rng.standard_normal(32).astype(np.float32)
+    nan[5] = np.nan
+    blocks.append(nan[None])
+    inf = rng.standard_normal(32).astype(np.float32)
+    inf[9] = np.inf
+    blocks.append(inf[None])
+    tiny = np.full((1, 32), 1e-30, np.float32)
+    tiny[0, 3] = -3e-38
+    blocks.append(tiny)
+    return np.concatenate(blocks).reshape(-1)
+
+
+def test_quantize_rows_known_answers(oracle):
+    values, scales, sums = oracle.quantize_rows(quantize_edge_rows())
+    v = values.reshape(-1, 32)
+    z, t, nan, inf = 64, 65, 67, 68
+    assert not v[z].any() and scales[z] == 0.0 and not sums[z].any()
+    assert scales[t] == 1.0
+    # round half to even, division (not a reciprocal) by d = amax / 127
+    assert list(v[t, :12]) == [127, -127, 2, 4, -2, -4, 0, 0, 2, -2, 126, -126]
+    assert list(sums[t]) == [int(v[t, :16].sum()), int(v[t, 16:].sum())]
+    assert v[66, 0] == 127 and v[66, 31] == -127
+    assert v[nan, 5] == 0 and np.isfinite(scales[nan])
+    assert scales[inf] == np.inf and v[inf, 9] == 0 and not v[inf].any()

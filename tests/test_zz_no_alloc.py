@@ -60,6 +60,48 @@ def test_static_scratch_matches_allocating_entry(cuda_device, fmt, m, n, k):
         assert _norm_err(a, b) <= tol, f"call {call}: {_norm_err(a, b)} > {tol}"
 
 
+def test_static_scratch_back_to_back_calls_allocate_nothing(cuda_device):
+    """Two calls queued on one stream with nothing between them (split K active:
+    the shared array holds the bf16 activations and the partial planes), with
+    different activations: each output equals the allocating entry point's, and
+    neither torch's allocator nor the device's free memory moves."""
+    import torch
+
+    torch.cuda.set_device(cuda_device)
+    stream = torch.cuda.current_stream().cuda_stream
+    fmt, m, n, k = mgb.Q4_K, 16, 4096, 4096
+    assert mgb.qmatmul_workspace_bytes(fmt, m, n, k) > mgb.qmatmul_min_workspace_bytes(fmt, m, n, k)
+    w = synthetic.packed_weights(fmt, n, k, seed=19)
+    src = torch.from_numpy(w).cuda()
+    wdev = torch.empty(mgb.packed_bytes(fmt, n, k), dtype=torch.uint8, device="cuda")
+    mgb.repack(fmt, src.data_ptr(), n, k, wdev.data_ptr(), stream)
+    ws_bytes = mgb.qmatmul_workspace_bytes(fmt, m, n, k)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    xs = [torch.from_numpy(synthetic.activations(m, k, seed=200 + i)).cuda() for i in range(2)]
+    refs = [torch.full((m, n), float("nan"), device="cuda") for _ in range(2)]
+    ys = [torch.full((m, n), float("nan"), device="cuda") for _ in range(2)]
+    for x, r in zip(xs, refs):
+        mgb.qmatmul(fmt, wdev.data_ptr(), n, k, x.data_ptr(), m, r.data_ptr(),
+                    workspace_ptr=ws.data_ptr(), workspace_bytes=ws_bytes, stream=stream)
+    # one call first, so that lazy module loading is not counted below
+    mgb.check(mgb.lib().mgb_qmatmul_static_scratch(fmt, wdev.data_ptr(), n, k, xs[0].data_ptr(),
+                                                   m, ys[0].data_ptr(), None, 0, stream))
+    torch.cuda.synchronize()
+    allocated, free = torch.cuda.memory_allocated(), torch.cuda.mem_get_info()[0]
+    for x, y in zip(xs, ys):
+        mgb.check(mgb.lib().mgb_qmatmul_static_scratch(fmt, wdev.data_ptr(), n, k, x.data_ptr(),
+                                                       m, y.data_ptr(), None, 0, stream))
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_allocated() == allocated
+    assert torch.cuda.mem_get_info()[0] == free
+    assert mgb.take_device_error(cuda_device) == 0
+    for call, (y, r) in enumerate(zip(ys, refs)):
+        a, b = y.cpu().numpy(), r.cpu().numpy()
+        assert np.isfinite(a).all(), f"call {call}: non-finite output"
+        assert _norm_err(a, b) <= GEMM_TOL, f"call {call}: {_norm_err(a, b)} > {GEMM_TOL}"
+    assert not np.array_equal(ys[0].cpu().numpy(), ys[1].cpu().numpy())
+
+
 def test_static_scratch_rejects_oversized_shapes(cuda_device):
     import torch
 
