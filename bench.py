@@ -612,8 +612,9 @@ def run_b200(args) -> None:
     def tp_stack(shapes: list[tuple[int, int]], layers: int, m: int) -> dict:
         """A stack pass under tensor parallelism: every projection one fused
         call on this rank's N/G stored rows (columns stored into every rank's
-        y, a stream-ordered wait for all ranks), with device epochs, the whole
-        pass captured as one CUDA graph.  One fused op per distinct shape, its
+        y; each call waits, inside its first kernel, for the call before it on
+        every rank), with device epochs, the whole pass captured as one CUDA
+        graph.  One fused op per distinct shape, its
         weight swapped for each layer's own copy (every shape is called an
         even number of times per pass, so its two y buffers keep alternating
         across replays)."""
@@ -631,10 +632,17 @@ def run_b200(args) -> None:
                   for k in sorted({k for _, k in shapes})}
 
             def one_pass() -> None:
-                for lw in layer_w:
-                    for s, w in zip(shapes, lw):
+                # each call waits for the call before it (the previous pass's
+                # last, for the first) inside its own first kernel, as a model
+                # whose next projection reads the gathered y would; only the
+                # pass's last call is followed by a wait of its own
+                prev = ops[shapes[-1]]
+                for li, lw in enumerate(layer_w):
+                    for si, (s, w) in enumerate(zip(shapes, lw)):
+                        last = li == len(layer_w) - 1 and si == len(shapes) - 1
                         ops[s].weight = w
-                        ops[s](xs[s[1]])
+                        ops[s](xs[s[1]], after=prev, wait=last)
+                        prev = ops[s]
 
             one_pass()  # eager: workspaces allocated, kernels configured
             torch.cuda.synchronize()
@@ -657,7 +665,8 @@ def run_b200(args) -> None:
                     "weight_gbs": gbs, "weight_gbs_per_gpu": gbs / world,
                     "frac_hbm_per_gpu": gbs / world / pk["hbm_gbs"], "tflops": tfl,
                     "frac_bf16_per_gpu": tfl / world / pk["bf16_tflops_sustained"],
-                    "launches_per_pass": 3 * layers * len(shapes), "replays": reps}
+                    "launches_per_pass": (2 if m > 2 else 1) * layers * len(shapes) + 1,
+                    "replays": reps}
         finally:
             del graph
             for op in ops.values():

@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define MGB_ABI_VERSION 2
+#define MGB_ABI_VERSION 3
 #define MGB_MAX_RANK 8
 
 /* Status codes.  The kernel errors follow `KernelError` (src/lib.rs:2193-2230,
@@ -387,13 +387,22 @@ mgb_status mgb_quantize_rows(const float *x, uint64_t len, int8_t *values, float
  * `cta_counter` is this rank's counter word, zero before its first call (each
  * call leaves it zero).  The epoch is `epoch` (host epochs, counting from 1),
  * or, when `epoch` is 0 (device epochs), the value of this rank's epoch word
- * (the word after `cta_counter`) plus one, which mgb_tp_wait with epoch 0
- * advances after each call: a sequence of calls and waits captured in a CUDA
- * graph then publishes fresh epochs on every replay.  One synchronisation
- * buffer uses one mode; with device epochs every rank's epoch word starts at
- * zero, and an op alternating between two y buffers per call captures an even
+ * (the word after `cta_counter`) plus one, and the call advances the word to
+ * it as it publishes: a sequence of calls and waits captured in a CUDA graph
+ * then publishes fresh epochs on every replay.  One synchronisation buffer
+ * uses one mode; with device epochs every rank's epoch word starts at zero,
+ * and an op alternating between two y buffers per call captures an even
  * number of its calls in a graph, so that consecutive calls (across replays
- * too) alternate buffers. */
+ * too) alternate buffers.
+ *
+ * Input wait (optional; `wait_done` NULL: none).  Before the call reads x, its
+ * first kernel waits, bounded by wait_timeout_ms (0: 2000; giving up records
+ * device error 1), until every one of `wait_world` ranks has published
+ * `wait_epoch` (0: device epochs, the current value of that buffer's epoch
+ * word) into `wait_done`: this rank's synchronisation words of an earlier
+ * fused call on this stream, normally the one whose gathered y is this call's
+ * x.  It does what an mgb_tp_wait for that call would do, inside the next
+ * call instead of as a kernel of its own between the two. */
 typedef struct mgb_tp_out {
     float *y[MGB_MAX_TP];
     uint32_t *done[MGB_MAX_TP];
@@ -403,6 +412,10 @@ typedef struct mgb_tp_out {
     uint32_t epoch;
     int32_t world;
     int32_t rank;
+    const uint32_t *wait_done;
+    uint32_t wait_epoch;
+    int32_t wait_world;
+    uint32_t wait_timeout_ms;
 } mgb_tp_out;
 
 /* cudaMalloc'd, zero-filled device memory on the current device, whole
@@ -428,12 +441,13 @@ mgb_status mgb_qmatmul_tp(int32_t format, const void *w, uint64_t n, uint64_t k,
                           void *stream);
 /* Stream-ordered wait until done[r] has reached `epoch` for every r < world
  * (`done` = this rank's synchronisation words).  Work queued after it on
- * `stream` sees every rank's columns.  `epoch` 0: device epochs, the rank's
- * epoch word + 1, and the word is advanced to it once every rank has reached
- * it.  A wait longer than timeout_ms (0: 2000) gives up and records device
- * error 1 (see mgb_take_device_error).  After such an error the ranks' epochs
- * disagree (the rank that gave up did not advance its epoch word, its peers
- * may have), so every later wait would expire too: before the next call,
+ * `stream` sees every rank's columns.  `epoch` 0: device epochs, the current
+ * value of the rank's epoch word (which the last call on that buffer advanced
+ * as it published).  A wait longer than timeout_ms (0: 2000) gives up and
+ * records device error 1 (see mgb_take_device_error).  After such an error the
+ * ranks' epochs disagree (the rank that gave up may be behind its peers, or
+ * ahead of one that never published), so every later wait may expire too:
+ * before the next call,
  * every rank synchronises its stream, then all ranks zero their whole
  * synchronisation area (MGB_TP_SYNC_BYTES: counter, epoch word and done
  * words) and meet at a host barrier, and host epochs restart from 1. */

@@ -221,8 +221,11 @@ __device__ __forceinline__ void out_store(const OutSpec &o, int m, uint64_t col,
 }
 
 // Every thread that stored output calls this before the CTA barrier that
-// precedes out_complete: its stores (to peer GPUs too) become visible
-// system-wide.  A plain call (one rank) needs no fence.
+// precedes out_complete: its stores (to peer GPUs too) become visible at
+// system scope.  (A fence executes per warp; on B200 a system fence drains
+// only the executing warp's stores, and one fence per CTA after the barrier
+// let a peer read stale columns of a chained call on two GPUs, so every
+// storing warp fences.)  A plain call (one rank) needs no fence.
 __device__ __forceinline__ void out_fence(const OutSpec &o) {
   if (o.world > 1 || o.cta_counter) __threadfence_system();
 }
@@ -236,11 +239,55 @@ __device__ __forceinline__ void out_complete(const OutSpec &o, uint32_t total_ct
   const uint32_t before = atomicAdd(o.cta_counter, 1u);
   if (before != total_ctas - 1) return;
   *o.cta_counter = 0;  // every CTA of this call has counted: ready for the next call
-  const uint32_t epoch = o.epoch_src ? *(volatile const uint32_t *)o.epoch_src + 1u : o.epoch;
+  const uint32_t epoch = o.epoch_word ? *(volatile const uint32_t *)o.epoch_word + 1u : o.epoch;
+  if (o.epoch_word) *(volatile uint32_t *)o.epoch_word = epoch;  // the next call publishes epoch + 1
   __threadfence_system();
   for (int r = 0; r < o.world; ++r)
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(o.done_ranks[r] + o.rank), "r"(epoch)
                  : "memory");
 }
 
+
+// ---- waits on the ranks of a tensor-parallel group ------------------------------------
+
+// Word index of the epoch word in a rank's synchronisation buffer
+// (MGB_TP_EPOCH_OFFSET / 4: after the done words and the CTA counter).
+constexpr int TP_EPOCH_WORD = 33;
+
+// Lane r (< world) of one warp polls done[r] until it reaches `epoch` (serial
+// number arithmetic, so epochs may wrap), sleeping 32 to 128 ns between polls,
+// giving up after `timeout_ns` of the global timer or an iteration cap.  The
+// load is an acquire at system scope: what the publishing rank released
+// before its epoch is visible after.  Returns whether this lane's rank got
+// there; lanes >= world return true.
+__device__ __forceinline__ bool poll_epoch(const uint32_t *done, int world, uint32_t epoch,
+                                           uint64_t timeout_ns, int lane) {
+  if (lane >= world) return true;
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  uint32_t ns = 32;
+  for (uint32_t i = 0; i < (1u << 26); ++i) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(done + lane) : "memory");
+    if ((int32_t)(v - epoch) >= 0) return true;
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > timeout_ns) break;
+    __nanosleep(ns);
+    if (ns < 128) ns <<= 1;
+  }
+  return false;
+}
+
+// The input wait of a call (OutSpec::wait_done): one whole warp, after the
+// kernel's griddepcontrol.wait (so the earlier call on this stream, which
+// advanced the epoch word, has finished), before a barrier that precedes every
+// read of x in the CTA.  A wait that gives up records ERR_WAIT_TIMEOUT.
+__device__ __forceinline__ void out_wait_input(const OutSpec &o, int lane, int *err) {
+  if (!o.wait_done) return;
+  const uint32_t epoch =
+      o.wait_epoch ? o.wait_epoch : *(volatile const uint32_t *)(o.wait_done + TP_EPOCH_WORD);
+  const bool reached = poll_epoch(o.wait_done, o.wait_world, epoch, o.wait_timeout_ns, lane);
+  if (!__all_sync(0xffffffffu, reached) && lane == 0) record_error(err, ERR_WAIT_TIMEOUT);
+}
 }  // namespace mgb

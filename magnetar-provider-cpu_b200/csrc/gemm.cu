@@ -443,8 +443,8 @@ __device__ __forceinline__ void drain_accumulators(const GemmParams &p, const CU
           for (int e = 0; e < 8; ++e) {
             if (col + e < p.n) {
               float o = v[e];
-              if (p.addend_mode == 1) o = o + p.addend[col + e];
-              else if (p.addend_mode == 2) o = o + p.addend[(size_t)row * p.n + col + e];
+              if (p.addend_mode == 1) o = o + __ldcg(p.addend + col + e);
+              else if (p.addend_mode == 2) o = o + __ldcg(p.addend + (size_t)row * p.n + col + e);
               yr[col + e] = o;
             }
           }
@@ -475,11 +475,11 @@ __device__ __forceinline__ void drain_accumulators(const GemmParams &p, const CU
         if (p.addend_mode == 1) {
 #pragma unroll
           for (int e = 0; e < 4; ++e)
-            if (col + e < p.n) o[e] = o[e] + p.addend[col + e];
+            if (col + e < p.n) o[e] = o[e] + __ldcg(p.addend + col + e);
         } else if (p.addend_mode == 2) {
 #pragma unroll
           for (int e = 0; e < 4; ++e)
-            if (col + e < p.n) o[e] = o[e] + p.addend[(size_t)row * p.n + col + e];
+            if (col + e < p.n) o[e] = o[e] + __ldcg(p.addend + (size_t)row * p.n + col + e);
         }
         // this call's column col lands at col0 + col of every output rank's y
         const size_t off = (size_t)row * p.out.ldy + p.out.col0 + col;
@@ -741,14 +741,21 @@ __global__ void __launch_bounds__(96 + 32 * DQW, 1)
 
 // f32 -> bf16 activations; lets the dependent GEMM launch at once (its weight
 // stream and dequantisation overlap this pass; its activation loads wait).
+// A tensor-parallel call with an input wait (OutSpec::wait_done) waits here,
+// warp 0 of every CTA, before any thread of the CTA reads x.
 __global__ void mgb_f32_to_bf16_kernel(const float *__restrict__ x, __nv_bfloat16 *__restrict__ out,
-                                   uint64_t n) {
+                                   uint64_t n, const OutSpec spec, int *err) {
   grid_launch_dependents();
   grid_dependency_wait();
+  if (spec.wait_done) {
+    if (threadIdx.x < 32) out_wait_input(spec, threadIdx.x, err);
+    __syncthreads();
+  }
   const uint64_t n4 = n / 4;
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n4;
        i += (uint64_t)gridDim.x * blockDim.x) {
-    const float4 v = reinterpret_cast<const float4 *>(x)[i];
+    // coherent loads: x may have been written by the kernel this one overlaps
+    const float4 v = __ldcg(reinterpret_cast<const float4 *>(x) + i);
     uint2 o;
     o.x = pack_bf16(v.x, v.y);
     o.y = pack_bf16(v.z, v.w);
@@ -766,10 +773,11 @@ __global__ void mgb_splitk_sum_kernel(const float *__restrict__ part, int planes
   const uint64_t total = m * n;
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total;
        i += (uint64_t)gridDim.x * blockDim.x) {
-    float v = part[i];
-    for (int z = 1; z < planes; ++z) v = v + part[z * total + i];
-    if (addend_mode == 1) v = v + addend[i % n];
-    else if (addend_mode == 2) v = v + addend[i];
+    // coherent loads: the planes are the overlapped GEMM's output
+    float v = __ldcg(part + i);
+    for (int z = 1; z < planes; ++z) v = v + __ldcg(part + z * total + i);
+    if (addend_mode == 1) v = v + __ldcg(addend + i % n);
+    else if (addend_mode == 2) v = v + __ldcg(addend + i);
     y[i] = v;
   }
 }
@@ -895,7 +903,7 @@ cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const fl
                                        (int)cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) return e;
   e = launch_dependent(mgb_f32_to_bf16_kernel, dim3((unsigned)blocks), dim3(256), 0,
-                                   stream, x, xb, m * k);
+                                   stream, x, xb, m * k, out, err);
   if (e != cudaSuccess) return e;
   // one plain output and room for the partial planes: split K (a
   // tensor-parallel call, even of one rank, publishes its completion from the

@@ -428,7 +428,11 @@ __device__ __forceinline__ void load_x(const float *__restrict__ x, int k, int u
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (active) f = __ldg(reinterpret_cast<const float4 *>(x + (size_t)m * k + (size_t)u * 32) + i);
+      // coherent loads (L2): under programmatic dependent launch the kernel
+      // starts while the previous one may still write x, which the
+      // non-coherent read-only path (ld.global.nc) does not allow; only the
+      // warp that executed griddepcontrol.wait was seen to read fresh values
+      if (active) f = __ldcg(reinterpret_cast<const float4 *>(x + (size_t)m * k + (size_t)u * 32) + i);
       v[4 * i] = f.x;
       v[4 * i + 1] = f.y;
       v[4 * i + 2] = f.z;
@@ -584,7 +588,10 @@ __global__ void __launch_bounds__(MAXT, MINB)
   // computes on the SM.  The barrier orders every thread's x loads and y
   // stores after that wait.  Each thread then loads and quantises its own run
   // of x.
-  if (cw == 0) grid_dependency_wait();
+  if (cw == 0) {
+    grid_dependency_wait();
+    out_wait_input(p.out, lane, p.err);  // a tensor-parallel call's wait on the call before
+  }
   named_barrier(14, consumer_warps * 32);
   XRun xr[MR];
   load_x<FMT, MR>(x, p.k, u, active, xr);
@@ -642,12 +649,10 @@ __global__ void __launch_bounds__(MAXT, MINB)
   }
   // a tensor-parallel call: every consumer's stores are fenced, then one
   // thread (past the grid dependency wait) counts the CTA
+  out_fence(p.out);
   if (p.out.cta_counter) {
-    out_fence(p.out);
     named_barrier(13, consumer_warps * 32);
     if (threadIdx.x == 32) out_complete(p.out, gridDim.x);
-  } else {
-    out_fence(p.out);
   }
 }
 
@@ -657,7 +662,7 @@ template <int FMT, int MR, int R, int MAXT>
 __global__ void __launch_bounds__(MAXT, 1)
     mgb_gemv_simple_kernel(const uint8_t *__restrict__ w, int n, int k, const float *__restrict__ x,
                        const OutSpec out, const float *__restrict__ addend, int addend_mode,
-                       int rows_per_cta) {
+                       int rows_per_cta, int *err) {
   __shared__ float red[2][32][R * MR];
   const Layout L(FMT, (uint64_t)n, (uint64_t)k);
   const int runs = k / RUN;
@@ -665,6 +670,10 @@ __global__ void __launch_bounds__(MAXT, 1)
   const bool active = u < runs;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
+  if (out.wait_done) {  // a tensor-parallel call's wait on the call before
+    if (warp == 0) out_wait_input(out, lane, err);
+    __syncthreads();
+  }
   XRun xr[MR];
   load_x<FMT, MR>(x, k, u, active, xr);
   uint32_t lut[4] = {0, 0, 0, 0};
@@ -833,7 +842,7 @@ static cudaError_t launch_staged(const void *w, int n, int k, const float *x, co
 
 template <int FMT, int MR, int R, int MAXT>
 static cudaError_t launch_simple(const void *w, int n, int k, const float *x, const OutSpec &out,
-                                 const float *addend, int addend_mode, int sms,
+                                 const float *addend, int addend_mode, int *err, int sms,
                                  cudaStream_t stream) {
   const int runs = k / RUN;
   const int threads = ((runs + 31) / 32) * 32;
@@ -845,7 +854,7 @@ static cudaError_t launch_simple(const void *w, int n, int k, const float *x, co
   if (rows < 1) rows = 1;
   const int grid = (int)ceil_div((uint64_t)n, (uint64_t)rows);
   mgb_gemv_simple_kernel<FMT, MR, R, MAXT><<<grid, threads, 0, stream>>>(
-      static_cast<const uint8_t *>(w), n, k, x, out, addend, addend_mode, rows);
+      static_cast<const uint8_t *>(w), n, k, x, out, addend, addend_mode, rows, err);
   return cudaGetLastError();
 }
 
@@ -869,18 +878,20 @@ static cudaError_t launch_fmt(const void *w, int n, int k, const float *x, const
       cudaError_t e = launch_staged<FMT, 1, 1024, 1>(w, n, k, x, without_completion(out), addend,
                                                      addend_mode, err, sms, stream);
       if (e == cudaSuccess)
-        e = launch_staged<FMT, 1, 1024, 1>(w, n, k, x + k, rows_from(out, 1), addend1, addend_mode,
-                                           err, sms, stream);
+        e = launch_staged<FMT, 1, 1024, 1>(w, n, k, x + k, without_input_wait(rows_from(out, 1)),
+                                           addend1, addend_mode, err, sms, stream);
       return e;
     }
   }
-  if (k <= 256 * 32) return launch_simple<FMT, MR, 4, 256>(w, n, k, x, out, addend, addend_mode, sms, stream);
-  if (MR == 1) return launch_simple<FMT, 1, 2, 1024>(w, n, k, x, out, addend, addend_mode, sms, stream);
+  if (k <= 256 * 32)
+    return launch_simple<FMT, MR, 4, 256>(w, n, k, x, out, addend, addend_mode, err, sms, stream);
+  if (MR == 1)
+    return launch_simple<FMT, 1, 2, 1024>(w, n, k, x, out, addend, addend_mode, err, sms, stream);
   cudaError_t e = launch_simple<FMT, 1, 2, 1024>(w, n, k, x, without_completion(out), addend,
-                                                 addend_mode, sms, stream);
+                                                 addend_mode, err, sms, stream);
   if (e == cudaSuccess)
-    e = launch_simple<FMT, 1, 2, 1024>(w, n, k, x + k, rows_from(out, 1), addend1, addend_mode, sms,
-                                       stream);
+    e = launch_simple<FMT, 1, 2, 1024>(w, n, k, x + k, without_input_wait(rows_from(out, 1)),
+                                       addend1, addend_mode, err, sms, stream);
   return e;
 }
 

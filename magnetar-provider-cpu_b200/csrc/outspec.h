@@ -11,21 +11,25 @@ constexpr int MAX_TP = 8;
 // Output element (row, col) of a call goes to y_ranks[r] + row * ldy + col0 +
 // col for every r < world (plain call: world 1, y_ranks[0] = y, ldy = n,
 // col0 = 0).  With cta_counter set, the call publishes its completion: every
-// CTA fences its stores at system scope and counts itself on cta_counter
-// (zero before the call); the last one resets it and stores the call's epoch
-// with system-scope release into done_ranks[r][rank] for every r.  The epoch
-// is `epoch`, or, with epoch_src set (device epochs), *epoch_src + 1 read by
-// that last CTA: the rank's epoch word, which its stream-ordered wait advances
-// after every call, so a captured sequence of calls publishes fresh epochs on
-// every replay.
+// CTA counts itself on cta_counter (zero before the call) once its stores are
+// done; the last one resets it and stores the call's epoch with system-scope
+// release into done_ranks[r][rank] for every r.  The epoch is `epoch`, or,
+// with epoch_word set (device epochs), *epoch_word + 1 read by that last CTA,
+// which also advances *epoch_word to it: a captured sequence of calls then
+// publishes fresh epochs on every replay.  With wait_done set, the kernel that
+// reads x first waits (after its griddepcontrol.wait) until every one of
+// wait_world ranks has published wait_epoch (0: the value of the epoch word of
+// that synchronisation buffer) into wait_done.
 struct OutSpec {
   float *y_ranks[MAX_TP];
   uint32_t *done_ranks[MAX_TP];
   uint32_t *cta_counter;
-  const uint32_t *epoch_src;
+  uint32_t *epoch_word;
+  const uint32_t *wait_done;
   uint64_t ldy, col0;
-  uint32_t epoch;
-  int world, rank;
+  uint64_t wait_timeout_ns;
+  uint32_t epoch, wait_epoch;
+  int world, rank, wait_world;
 };
 
 inline OutSpec plain_out(float *y, uint64_t n) {
@@ -36,7 +40,8 @@ inline OutSpec plain_out(float *y, uint64_t n) {
   o.world = 1;
   o.rank = 0;
   o.cta_counter = nullptr;
-  o.epoch_src = nullptr;
+  o.epoch_word = nullptr;
+  o.wait_done = nullptr;
   o.epoch = 0;
   return o;
 }
@@ -44,6 +49,13 @@ inline OutSpec plain_out(float *y, uint64_t n) {
 // The same destination with its completion left to a later launch.
 inline OutSpec without_completion(OutSpec o) {
   o.cta_counter = nullptr;
+  return o;
+}
+
+// The same call without its input wait (a later launch of a call whose first
+// launch waited).
+inline OutSpec without_input_wait(OutSpec o) {
+  o.wait_done = nullptr;
   return o;
 }
 

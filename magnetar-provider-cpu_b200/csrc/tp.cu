@@ -20,40 +20,22 @@ namespace mgb {
 
 static_assert(MGB_MAX_TP == MAX_TP, "C ABI and kernel rank limits differ");
 static_assert(sizeof(cudaIpcMemHandle_t) == MGB_IPC_HANDLE_BYTES, "IPC handle size");
+static_assert(MGB_TP_EPOCH_OFFSET == 4 * TP_EPOCH_WORD, "epoch word offset");
 
-// One warp: lane r polls rank r's done word until it reaches the epoch (serial
-// number arithmetic, so the epoch may wrap).  Bounded by `timeout_ns` of the
-// global timer and an iteration cap; giving up records ERR_WAIT_TIMEOUT.  With
-// epoch_word set (device epochs) the epoch is *epoch_word + 1, and once every
-// rank has reached it lane 0 advances *epoch_word to it (a wait that gives up
-// leaves it, and the error recorded).
+// One warp waits until every rank's done word has reached the epoch
+// (poll_epoch); with epoch_word set (device epochs) the epoch is the word's
+// current value, which the call it waits for advanced as it published.
 __global__ void mgb_tp_wait_kernel(const uint32_t *done, int world, uint32_t epoch,
-                               uint32_t *epoch_word, uint64_t timeout_ns, int *err) {
+                               const uint32_t *epoch_word, uint64_t timeout_ns, int *err) {
+  // The next kernel on the stream (a programmatic dependent, e.g. the next
+  // projection's GEMV) may launch now and stream its weights while this wait
+  // polls; its griddepcontrol.wait still holds its reads of x until this grid
+  // has completed.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int lane = threadIdx.x;
-  if (lane >= world) return;
-  if (epoch_word) epoch = *(volatile uint32_t *)epoch_word + 1u;
-  uint64_t t0;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-  uint32_t ns = 32;
-  bool reached = false;
-  for (uint32_t i = 0; i < (1u << 26); ++i) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(done + lane) : "memory");
-    if ((int32_t)(v - epoch) >= 0) {
-      reached = true;
-      break;
-    }
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    if (t - t0 > timeout_ns) break;
-    __nanosleep(ns);
-    if (ns < 1024) ns <<= 1;
-  }
-  if (!reached) record_error(err, ERR_WAIT_TIMEOUT);
-  // lanes 0 .. world-1 are the ones still here
-  const unsigned lanes = world >= 32 ? 0xffffffffu : (1u << world) - 1u;
-  const bool all = __all_sync(lanes, reached);
-  if (epoch_word && lane == 0 && all) *(volatile uint32_t *)epoch_word = epoch;
+  if (epoch_word) epoch = *(volatile const uint32_t *)epoch_word;
+  const bool reached = poll_epoch(done, world, epoch, timeout_ns, lane);
+  if (!__all_sync(0xffffffffu, reached) && lane == 0) record_error(err, ERR_WAIT_TIMEOUT);
 }
 
 static mgb_status to_outspec(const mgb_tp_out *o, uint64_t n, OutSpec &spec) {
@@ -76,7 +58,16 @@ static mgb_status to_outspec(const mgb_tp_out *o, uint64_t n, OutSpec &spec) {
   spec.cta_counter = o->cta_counter;
   // epoch 0: device epochs, from this rank's epoch word (the word after its
   // CTA counter)
-  spec.epoch_src = o->epoch == 0 ? o->cta_counter + 1 : nullptr;
+  spec.epoch_word = o->epoch == 0 ? o->cta_counter + 1 : nullptr;
+  if (o->wait_done) {
+    if (o->wait_world < 1 || o->wait_world > MGB_MAX_TP)
+      return fail(MGB_INVALID_ARGUMENT, "input wait over %d ranks (1..%d)", o->wait_world,
+                  MGB_MAX_TP);
+    spec.wait_done = o->wait_done;
+    spec.wait_epoch = o->wait_epoch;
+    spec.wait_world = o->wait_world;
+    spec.wait_timeout_ns = (uint64_t)(o->wait_timeout_ms ? o->wait_timeout_ms : 2000) * 1000000ull;
+  }
   spec.ldy = o->ldy;
   spec.col0 = o->col0;
   spec.epoch = o->epoch;
@@ -175,8 +166,7 @@ mgb_status mgb_tp_wait(const uint32_t *done, int32_t world, uint32_t epoch, uint
   cudaGetDevice(&dev);
   const uint64_t ns = (uint64_t)(timeout_ms ? timeout_ms : 2000) * 1000000ull;
   // epoch 0: device epochs (this rank's epoch word in its synchronisation words)
-  uint32_t *epoch_word =
-      epoch == 0 ? const_cast<uint32_t *>(done) + MGB_TP_EPOCH_OFFSET / 4 : nullptr;
+  const uint32_t *epoch_word = epoch == 0 ? done + TP_EPOCH_WORD : nullptr;
   mgb_tp_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(done, world, epoch, epoch_word,
                                                                   ns, device_error_flag(dev));
   cudaError_t e = cudaGetLastError();

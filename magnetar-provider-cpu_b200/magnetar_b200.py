@@ -92,7 +92,9 @@ class TpOut(ctypes.Structure):
     _fields_ = [("y", ctypes.c_void_p * MAX_TP), ("done", ctypes.c_void_p * MAX_TP),
                 ("cta_counter", ctypes.c_void_p), ("ldy", ctypes.c_uint64),
                 ("col0", ctypes.c_uint64), ("epoch", ctypes.c_uint32), ("world", ctypes.c_int32),
-                ("rank", ctypes.c_int32)]
+                ("rank", ctypes.c_int32), ("wait_done", ctypes.c_void_p),
+                ("wait_epoch", ctypes.c_uint32), ("wait_world", ctypes.c_int32),
+                ("wait_timeout_ms", ctypes.c_uint32)]
 
 
 _lib = None
@@ -283,7 +285,10 @@ def ipc_close(ptr: int) -> None:
 
 
 def tp_out(y: list[int], done: list[int], cta_counter: int, ldy: int, col0: int, epoch: int,
-           rank: int) -> TpOut:
+           rank: int, wait_done: int = 0, wait_epoch: int = 0, wait_world: int = 0,
+           wait_timeout_ms: int = 0) -> TpOut:
+    """`mgb_tp_out`; wait_done (this rank's synchronisation words of an earlier
+    fused call) makes the call wait for that call's epoch before reading x."""
     world = len(y)
     if len(done) != world:
         raise ValueError("one done pointer per rank")
@@ -293,6 +298,8 @@ def tp_out(y: list[int], done: list[int], cta_counter: int, ldy: int, col0: int,
         o.done[r] = done[r]
     o.cta_counter = cta_counter
     o.ldy, o.col0, o.epoch, o.world, o.rank = ldy, col0, epoch & 0xFFFFFFFF, world, rank
+    o.wait_done = wait_done or None
+    o.wait_epoch, o.wait_world, o.wait_timeout_ms = wait_epoch & 0xFFFFFFFF, wait_world, wait_timeout_ms
     return o
 
 

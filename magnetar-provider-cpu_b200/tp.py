@@ -184,8 +184,14 @@ class FusedShardedPackedMatmul(ShardedPackedMatmul):
         self._own.append(ptr)
         return ptr
 
-    def __call__(self, x, group=None):
-        """y [M, N] (every rank's columns) for device activations x [M, K] (f32)."""
+    def __call__(self, x, group=None, after=None, wait=True):
+        """y [M, N] (every rank's columns) for device activations x [M, K] (f32).
+
+        `after`: the fused op whose latest call on this stream produced x (or
+        must otherwise complete first); this call's first kernel waits for that
+        call's epoch on every rank before reading x, instead of a wait kernel
+        of its own between the two.  `wait=False` leaves this call's own wait
+        to whoever consumes y: a later call with after=self, or wait()."""
         import torch
 
         import magnetar_b200 as mgb
@@ -193,11 +199,19 @@ class FusedShardedPackedMatmul(ShardedPackedMatmul):
         m = x.shape[0]
         if not 0 < m <= self.max_m:
             raise ValueError(f"{m} activation rows (1..{self.max_m})")
+        if after is not None and after.device_epochs != self.device_epochs:
+            raise ValueError("chained fused calls use one epoch mode")
         self.epoch += 1
         slot = self.epoch & 1
         epoch = 0 if self.device_epochs else self.epoch
+        wait_kw = {}
+        if after is not None:
+            wait_kw = dict(wait_done=after.sync, wait_world=after.world,
+                           wait_epoch=0 if after.device_epochs else after.epoch,
+                           wait_timeout_ms=after.timeout_ms)
         out = mgb.tp_out(self.y_slots[slot], self.done, self.sync + mgb.TP_COUNTER_OFFSET,
-                         ldy=self.n, col0=self.rank * self.n_loc, epoch=epoch, rank=self.rank)
+                         ldy=self.n, col0=self.rank * self.n_loc, epoch=epoch, rank=self.rank,
+                         **wait_kw)
         ws_bytes = mgb.qmatmul_workspace_bytes(self.fmt, m, self.n_loc, self.k)
         if ws_bytes and (self._ws is None or self._ws.numel() < ws_bytes):
             self._ws = torch.empty(ws_bytes, dtype=torch.uint8, device=self.device)
@@ -205,8 +219,18 @@ class FusedShardedPackedMatmul(ShardedPackedMatmul):
         mgb.qmatmul_tp(self.fmt, self.weight.data_ptr(), self.n_loc, self.k, x.data_ptr(), m, out,
                        workspace_ptr=self._ws.data_ptr() if ws_bytes else 0,
                        workspace_bytes=ws_bytes, stream=stream)
-        mgb.tp_wait(self.sync, self.world, epoch, self.timeout_ms, stream)
+        if wait:
+            self.wait()
         return torch.as_tensor(_DeviceArray(self.slots[slot], (m, self.n)), device=self.device)
+
+    def wait(self) -> None:
+        """Stream-ordered wait for this op's latest call on every rank."""
+        import torch
+
+        import magnetar_b200 as mgb
+
+        mgb.tp_wait(self.sync, self.world, 0 if self.device_epochs else self.epoch,
+                    self.timeout_ms, torch.cuda.current_stream(self.device).cuda_stream)
 
     def reset(self) -> None:
         """Recovery after a wait gave up (device error 1, a peer that never

@@ -22,7 +22,7 @@ def test_library_exports_every_header_function():
 
 
 def test_identity_and_advertisements():
-    assert mgb.lib().mgb_abi_version() == 2
+    assert mgb.lib().mgb_abi_version() == 3
     md = mgb.metadata()
     assert md["name"] == "magnetar:provider/b200-native"
     assert md["name"] != "magnetar:provider/reference-cpu"

@@ -271,3 +271,34 @@ def test_gemm_wide_tile_epilogue_edges(torch_cuda, oracle, m, n, k):
     y = _qmatmul(torch, fmt, wdev, n, k, x)
     assert np.isfinite(y).all()
     oracle.assert_close(y, oracle.packed_matmul(fmt, w, n, k, x), GEMM_TOL, f"gemm m {m} n {n}")
+
+
+@pytest.mark.parametrize("m", [1, 2])
+def test_gemv_chain_reads_the_previous_output(torch_cuda, oracle, m):
+    """A decode chain: y1 = x W1^T then y2 = y1 W2^T on one stream, the second
+    GEMV a programmatic dependent that starts while the first still writes y1,
+    over three rounds with the same buffers (so earlier rounds have read y1's
+    lines).  Every round equals the oracle chain: x is loaded coherently after
+    the dependency wait, never through the read-only path."""
+    torch = torch_cuda
+    fmt, k, n1, n2 = mgb.Q4_K, 1024, 512, 256
+    w1 = synthetic.packed_weights(fmt, n1, k, seed=91)
+    w2 = synthetic.packed_weights(fmt, n2, n1, seed=92)
+    d1, d2 = _device_layout(torch, fmt, w1, n1, k), _device_layout(torch, fmt, w2, n2, n1)
+    xd = torch.empty((m, k), dtype=torch.float32, device="cuda")
+    y1 = torch.empty((m, n1), dtype=torch.float32, device="cuda")
+    y2 = torch.empty((m, n2), dtype=torch.float32, device="cuda")
+    sp = torch.cuda.current_stream().cuda_stream
+    for rnd in range(3):
+        x = synthetic.activations(m, k, seed=93 + rnd)
+        xd.copy_(torch.from_numpy(x))
+        mgb.qmatmul(fmt, d1.data_ptr(), n1, k, xd.data_ptr(), m, y1.data_ptr(), stream=sp)
+        mgb.qmatmul(fmt, d2.data_ptr(), n2, n1, y1.data_ptr(), m, y2.data_ptr(), stream=sp)
+        torch.cuda.synchronize()
+        assert mgb.take_device_error(torch.cuda.current_device()) == 0
+        ref1 = oracle.packed_matmul(fmt, w1, n1, k, x)
+        got1 = y1.cpu().numpy()
+        oracle.assert_close(got1, ref1, GEMV_TOL, f"round {rnd} first")
+        # the second GEMV against the oracle on the first's actual output
+        oracle.assert_close(y2.cpu().numpy(), oracle.packed_matmul(fmt, w2, n2, n1, got1),
+                            GEMV_TOL, f"round {rnd} second")

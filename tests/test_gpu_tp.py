@@ -130,7 +130,7 @@ def test_emulated_two_ranks_gather_every_column(torch_cuda, oracle, fmt, n, k, m
                                        (synthetic.Q6_K, 256, 16384, 2)])
 def test_emulated_two_ranks_device_epochs_replay_in_a_graph(torch_cuda, fmt, n, k, m):
     """Device epochs (epoch 0): each rank's kernels publish its epoch word + 1
-    and its wait advances the word, so the two ranks' calls and waits captured
+    and advance the word to it, so the two ranks' calls and waits captured
     in one CUDA graph publish fresh epochs on every replay.  Ranks are emulated
     one after the other on one GPU, as above; every replay's gathered y equals
     the unsharded call on that replay's activations."""
@@ -191,6 +191,95 @@ def test_emulated_two_ranks_device_epochs_replay_in_a_graph(torch_cuda, fmt, n, 
         torch.cuda.synchronize()
         for p in sync:
             mgb.device_free(p)
+
+
+@pytest.mark.parametrize("fmt_b,n1", [(synthetic.Q4_K, 512), (synthetic.Q8_0, 480)])
+@pytest.mark.parametrize("m", [1, 2, 5])
+@pytest.mark.parametrize("device_epochs", [False, True])
+def test_emulated_two_ranks_chained_call_waits_inside_its_first_kernel(torch_cuda, fmt_b, n1, m,
+                                                                        device_epochs):
+    """Call B reads call A's gathered y as its x and waits for A's epoch on
+    every rank inside its own first kernel (the input wait of mgb_tp_out)
+    instead of a wait kernel between the two; only B's own completion is waited
+    for.  Ranks emulated one after the other on one GPU; the GEMV (m = 1), the
+    tensor-core path (m = 5, the wait in the activation pass) and, for Q8_0 at
+    k = 480, the direct-load GEMV in row-pair launches (the first one waits).
+    Three rounds; B's gathered y equals the unsharded chain bit for bit."""
+    torch = torch_cuda
+    world, fmt_a, k, n2 = 2, synthetic.Q4_K, 1024, 256
+    wa = synthetic.packed_weights(fmt_a, n1, k, seed=51)
+    wb = synthetic.packed_weights(fmt_b, n2, n1, seed=52)
+    sa = [_device_layout(torch, fmt_a, tp.shard_packed(fmt_a, wa, n1, k, world, r), n1 // world, k)
+          for r in range(world)]
+    sb = [_device_layout(torch, fmt_b, tp.shard_packed(fmt_b, wb, n2, n1, world, r), n2 // world, n1)
+          for r in range(world)]
+    ya = [torch.full((m, n1), float("nan"), dtype=torch.float32, device="cuda") for _ in range(world)]
+    yb = [torch.full((m, n2), float("nan"), dtype=torch.float32, device="cuda") for _ in range(world)]
+    sync_a = [mgb.device_alloc(mgb.TP_SYNC_BYTES) for _ in range(world)]
+    sync_b = [mgb.device_alloc(mgb.TP_SYNC_BYTES) for _ in range(world)]
+    ws_bytes = max(mgb.qmatmul_workspace_bytes(fmt_a, m, n1 // world, k),
+                   mgb.qmatmul_workspace_bytes(fmt_b, m, n2 // world, n1), 16)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    sp = torch.cuda.current_stream().cuda_stream
+    dev = torch.cuda.current_device()
+    try:
+        for rnd in range(3):
+            e = 0 if device_epochs else rnd + 1
+            xd = torch.from_numpy(synthetic.activations(m, k, seed=70 + rnd)).cuda()
+            for r in range(world):
+                out = mgb.tp_out([y.data_ptr() for y in ya], sync_a, sync_a[r] + mgb.TP_COUNTER_OFFSET,
+                                 ldy=n1, col0=r * (n1 // world), epoch=e, rank=r)
+                mgb.qmatmul_tp(fmt_a, sa[r].data_ptr(), n1 // world, k, xd.data_ptr(), m, out,
+                               workspace_ptr=ws.data_ptr(), workspace_bytes=ws_bytes, stream=sp)
+            for r in range(world):
+                out = mgb.tp_out([y.data_ptr() for y in yb], sync_b, sync_b[r] + mgb.TP_COUNTER_OFFSET,
+                                 ldy=n2, col0=r * (n2 // world), epoch=e, rank=r,
+                                 wait_done=sync_a[r], wait_epoch=e, wait_world=world)
+                mgb.qmatmul_tp(fmt_b, sb[r].data_ptr(), n2 // world, n1, ya[r].data_ptr(), m, out,
+                               workspace_ptr=ws.data_ptr(), workspace_bytes=ws_bytes, stream=sp)
+            for r in range(world):
+                mgb.tp_wait(sync_b[r], world, e, 2000, sp)
+            torch.cuda.synchronize()
+            assert mgb.take_device_error(dev) == 0
+            ref_a = _unsharded(torch, fmt_a, wa, n1, k, xd)
+            ref_b = _unsharded(torch, fmt_b, wb, n2, n1, torch.from_numpy(ref_a).cuda())
+            for r in range(world):
+                np.testing.assert_array_equal(ya[r].cpu().numpy(), ref_a)
+                got = yb[r].cpu().numpy()
+                bad = np.argwhere(got != ref_b)
+                assert bad.size == 0, (rnd, r, sorted(set(bad[:, 0].tolist())),
+                                       int(bad[:, 1].min()), int(bad[:, 1].max()), len(bad))
+    finally:
+        torch.cuda.synchronize()
+        for p in sync_a + sync_b:
+            mgb.device_free(p)
+
+
+def test_input_wait_for_an_epoch_nobody_publishes_times_out(torch_cuda):
+    """The input wait of a call is bounded like mgb_tp_wait: waiting on an epoch
+    no rank publishes gives up, records device error 1, and the context stays
+    usable."""
+    torch = torch_cuda
+    fmt, n, k, m = synthetic.Q4_K, 256, 512, 1
+    w = synthetic.packed_weights(fmt, n, k, seed=53)
+    wd = _device_layout(torch, fmt, w, n, k)
+    xd = torch.from_numpy(synthetic.activations(m, k, seed=54)).cuda()
+    y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    sync, other = mgb.device_alloc(mgb.TP_SYNC_BYTES), mgb.device_alloc(mgb.TP_SYNC_BYTES)
+    dev = torch.cuda.current_device()
+    try:
+        assert mgb.take_device_error(dev) == 0
+        out = mgb.tp_out([y.data_ptr()], [sync], sync + mgb.TP_COUNTER_OFFSET, ldy=n, col0=0,
+                         epoch=1, rank=0, wait_done=other, wait_epoch=9, wait_world=2,
+                         wait_timeout_ms=20)
+        mgb.qmatmul_tp(fmt, wd.data_ptr(), n, k, xd.data_ptr(), m, out,
+                       stream=torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert mgb.take_device_error(dev) == 1
+        assert float(torch.ones(4, device="cuda").sum()) == 4.0
+    finally:
+        mgb.device_free(sync)
+        mgb.device_free(other)
 
 
 @pytest.mark.parametrize("m", [64, 1])
@@ -296,6 +385,24 @@ def _rank_main(rank: int, world: int, port: int, out) -> None:
             ref = _unsharded(torch, fmt, w, n, k, xd)
             if not np.array_equal(y, ref):
                 mismatches.append((call, m, float(np.nanmax(np.abs(y - ref)))))
+        # a chained pair: the second call reads the first's gathered y and
+        # waits for it inside its own first kernel; one wait at the end
+        n2 = 512
+        w2 = synthetic.packed_weights(fmt, n2, n, seed=32)
+        op2 = tp.FusedShardedPackedMatmul(fmt, tp.shard_packed(fmt, w2, n2, n, world, rank), n2, n,
+                                          world, rank, max_m=64)
+        try:
+            for call, m in enumerate([1, 64, 2]):
+                xd = torch.from_numpy(synthetic.activations(m, k, seed=80 + call)).to(dev)
+                y1 = op(xd, wait=False)
+                y2 = op2(y1, after=op).cpu().numpy()
+                ref1 = _unsharded(torch, fmt, w, n, k, xd)
+                ref2 = _unsharded(torch, fmt, w2, n2, n, torch.from_numpy(ref1).to(dev))
+                if not np.array_equal(y2, ref2):
+                    bad = np.argwhere(y2 != ref2)
+                    mismatches.append(("chained", call, m, sorted(set(bad[:, 0].tolist()))))
+        finally:
+            op2.close()
         torch.cuda.synchronize()
         err = mgb.take_device_error(rank)
         out.put((rank, mismatches, err))
