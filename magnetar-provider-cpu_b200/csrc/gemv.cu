@@ -428,11 +428,19 @@ __device__ __forceinline__ void load_x(const float *__restrict__ x, int k, int u
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-      // coherent loads (L2): under programmatic dependent launch the kernel
-      // starts while the previous one may still write x, which the
-      // non-coherent read-only path (ld.global.nc) does not allow; only the
-      // warp that executed griddepcontrol.wait was seen to read fresh values
-      if (active) f = __ldcg(reinterpret_cast<const float4 *>(x + (size_t)m * k + (size_t)u * 32) + i);
+      // Ordinary (L1-cacheable) loads, never the non-coherent read-only path
+      // (ld.global.nc): under programmatic dependent launch the kernel starts
+      // while the previous one may still write x, and with ld.global.nc only
+      // the warp that executed griddepcontrol.wait was seen to read fresh
+      // values.  Ordered after that wait by the acquire fence and the barrier
+      // that follow it; L2-only loads (ld.global.cg) were 3.5 us slower per
+      // config-0 link than these.
+      if (active) {
+        const float *src = x + (size_t)m * k + (size_t)u * 32 + 4 * i;
+        asm volatile("ld.global.ca.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(f.x), "=f"(f.y), "=f"(f.z), "=f"(f.w)
+                     : "l"(src));
+      }
       v[4 * i] = f.x;
       v[4 * i + 1] = f.y;
       v[4 * i + 2] = f.z;
@@ -590,6 +598,9 @@ __global__ void __launch_bounds__(MAXT, MINB)
   // of x.
   if (cw == 0) {
     grid_dependency_wait();
+    // acquire at GPU scope: the other warps' loads of x after the barrier
+    // below are ordered after the previous grid's writes
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
     out_wait_input(p.out, lane, p.err);  // a tensor-parallel call's wait on the call before
   }
   named_barrier(14, consumer_warps * 32);
