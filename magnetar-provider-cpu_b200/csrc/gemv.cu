@@ -511,6 +511,10 @@ __global__ void __launch_bounds__(MAXT, MINB)
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * (p.stage_bytes + p.dec_stage_bytes));
   uint64_t *empty = full + S;
   float *red = reinterpret_cast<float *>(empty + S);  // [teams][chunk][RPT][team_warps][MR]
+  // A tensor-parallel call stages the CTA's outputs here and one warp stores
+  // them to every rank: only that warp's stores then need a system fence.
+  float *ostage = red + (size_t)p.teams * p.chunk * RPT * p.team_warps * MR;  // [rows][MR]
+  const bool staged_out = p.out.world > 1 || p.out.cta_counter;
   const int consumer_warps = p.teams * p.team_warps;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = blockIdx.x * p.rows_per_cta;
@@ -652,18 +656,27 @@ __global__ void __launch_bounds__(MAXT, MINB)
             sum += red_team[((cc * RPT + i) * p.team_warps + wi) * MR + m];
           if (p.addend_mode == 1) sum = sum + __ldcg(p.addend + row);
           else if (p.addend_mode == 2) sum = sum + __ldcg(p.addend + (size_t)m * p.n + row);
-          out_store(p.out, m, row, sum);
+          if (staged_out) ostage[(size_t)(row - r0) * MR + m] = sum;
+          else out_store(p.out, m, row, sum);
         }
       }
       named_barrier(1 + team, team_threads);
     }
   }
-  // a tensor-parallel call: every consumer's stores are fenced, then one
-  // thread (past the grid dependency wait) counts the CTA
-  out_fence(p.out);
-  if (p.out.cta_counter) {
+  // a tensor-parallel call: consumer warp 0 (past the grid dependency wait)
+  // stores the CTA's outputs into every rank's y, fences its stores at system
+  // scope, and counts the CTA.  (A system fence drains only the executing
+  // warp's stores: nine storing warps per CTA each fencing cost ~4.6 us more
+  // per call than this.)
+  if (staged_out) {
     named_barrier(13, consumer_warps * 32);
-    if (threadIdx.x == 32) out_complete(p.out, gridDim.x);
+    if (cw == 0) {
+      const int total = (r1 - r0) * MR;
+      for (int i = lane; i < total; i += 32) out_store(p.out, i % MR, r0 + i / MR, ostage[i]);
+      out_fence(p.out);
+      __syncwarp();
+      if (lane == 0) out_complete(p.out, gridDim.x);
+    }
   }
 }
 
@@ -808,7 +821,8 @@ static size_t staged_config(int n, int k, int sms, GemvStaged &p, int &grid, int
   if (chunk > nst) chunk = nst;
   if (chunk < 1) chunk = 1;
   p.chunk = chunk;
-  const size_t fixed = red_stage * chunk;
+  // + the output staging of a tensor-parallel call: rows_per_cta x MR floats
+  const size_t fixed = red_stage * chunk + ceil_div((uint64_t)p.rows_per_cta * MR * 4, 16) * 16;
   const size_t per_stage = (size_t)p.stage_bytes + p.dec_stage_bytes + 16;
   // The 288-thread form stays within half an SM so the next GEMV's CTA can
   // stream its weights beside it; the 1024-thread form (k > 8192) takes the
