@@ -430,11 +430,10 @@ __device__ __forceinline__ void load_x(const float *__restrict__ x, int k, int u
       float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
       // Ordinary (L1-cacheable) loads, never the non-coherent read-only path
       // (ld.global.nc): under programmatic dependent launch the kernel starts
-      // while the previous one may still write x, and with ld.global.nc only
-      // the warp that executed griddepcontrol.wait was seen to read fresh
-      // values.  Ordered after that wait by the acquire fence and the barrier
-      // that follow it; L2-only loads (ld.global.cg) were 3.5 us slower per
-      // config-0 link than these.
+      // while the previous one may still write x, and with ld.global.nc, one
+      // warp waiting and the others released by a barrier, only the waiting
+      // warp was seen to read fresh values.  L2-only loads (ld.global.cg)
+      // were 3.5 us slower per config-0 link than these.
       if (active) {
         const float *src = x + (size_t)m * k + (size_t)u * 32 + 4 * i;
         asm volatile("ld.global.ca.v4.f32 {%0, %1, %2, %3}, [%4];"
@@ -600,12 +599,15 @@ __global__ void __launch_bounds__(MAXT, MINB)
   // computes on the SM.  The barrier orders every thread's x loads and y
   // stores after that wait.  Each thread then loads and quantises its own run
   // of x.
-  if (cw == 0) {
-    grid_dependency_wait();
-    // acquire at GPU scope: the other warps' loads of x after the barrier
-    // below are ordered after the previous grid's writes
+  // Every consumer warp waits for the previous grid itself (a hardware wait,
+  // nothing spins), so its own loads of x are ordered after that grid's writes.
+  grid_dependency_wait();
+  if (cw == 0 && p.out.wait_done) {
+    // a tensor-parallel call's wait on the call before (peers' writes, which
+    // the grid dependency does not cover): the acquire and the barrier below
+    // order the other warps' loads after it
+    out_wait_input(p.out, lane, p.err);
     asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    out_wait_input(p.out, lane, p.err);  // a tensor-parallel call's wait on the call before
   }
   named_barrier(14, consumer_warps * 32);
   XRun xr[MR];
