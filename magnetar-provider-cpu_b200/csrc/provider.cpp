@@ -10,7 +10,12 @@
 //   hands the result out exactly once (src/lib.rs:2301-2356).
 // - Observations are kept like the reference's bounded log (capacity 4096,
 //   trimmed at twice that, src/lib.rs:171, :1848-1868).
-// Every entry point takes the Provider's mutex, so they are thread-safe.
+// Every entry point takes the Provider's mutex, so they are thread-safe (the
+// reference's trait takes `&self` everywhere: calls may come from several
+// threads).  Tensor uploads and downloads run on copy streams of their own and
+// release the mutex while the host waits for them, so one thread's download
+// overlaps another thread's upload and kernels (PCIe carries both directions
+// at once); kernels stay on the one compute stream.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -81,8 +86,15 @@ struct ProfileEntry {
 struct mgb_provider {
   mgb_settings settings{};
   int sms = 148;
-  cudaStream_t stream = nullptr;
+  cudaStream_t stream = nullptr;  // kernels, allocations and frees
+  cudaStream_t h2d = nullptr;     // tensor uploads
+  cudaStream_t d2h = nullptr;     // tensor downloads
   std::mutex mu;
+  // Buffers that a download reads with the mutex released, with the number of
+  // such downloads; freeing one of them waits in `deferred` until the last
+  // download ends.
+  std::map<void *, int> reading;
+  std::vector<DevBuf> deferred;
   std::map<std::string, Tensor> storage;
   std::map<std::string, Packed> packed;
   std::map<uint64_t, Execution> executions;
@@ -117,9 +129,54 @@ void observe(mgb_provider *p, int32_t kind, const std::string &kernel, const std
 // host synchronisation), and the pool keeps freed memory for the next
 // allocation of the step (no cudaMalloc / cudaFree per tensor).
 void free_buf(mgb_provider *p, DevBuf &b) {
-  if (b.ptr) cudaFreeAsync(b.ptr, p->stream);
+  if (b.ptr && p->reading.count(b.ptr)) p->deferred.push_back(b);
+  else if (b.ptr) cudaFreeAsync(b.ptr, p->stream);
   b.ptr = nullptr;
   b.bytes = 0;
+}
+
+// Ends one download of `ptr` (mutex held): the last one frees the buffer if it
+// was released meanwhile.  The copy has completed (the host waited for it),
+// so the free needs no ordering against the download stream.
+void end_read(mgb_provider *p, void *ptr) {
+  auto r = p->reading.find(ptr);
+  if (r == p->reading.end() || --r->second > 0) return;
+  p->reading.erase(r);
+  for (size_t i = 0; i < p->deferred.size();) {
+    if (p->deferred[i].ptr == ptr) {
+      cudaFreeAsync(ptr, p->stream);
+      p->deferred.erase(p->deferred.begin() + i);
+    } else {
+      ++i;
+    }
+  }
+}
+
+// One host<->device copy on `copy_stream`, ordered after everything already
+// queued on the compute stream (the buffer's stream-ordered allocation, the
+// kernel that produced it, kernels that still read it).  The mutex is released
+// while the host waits for the copy and held again on return.
+cudaError_t copy_unlocked(mgb_provider *p, std::unique_lock<std::mutex> &lock,
+                          cudaStream_t copy_stream, void *dst, const void *src, uint64_t bytes,
+                          cudaMemcpyKind kind) {
+  cudaEvent_t ready = nullptr, done = nullptr;
+  cudaError_t e = cudaEventCreateWithFlags(&ready, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&done, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventRecord(ready, p->stream);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(copy_stream, ready, 0);
+  bool queued = false;
+  if (e == cudaSuccess) {
+    e = cudaMemcpyAsync(dst, src, bytes, kind, copy_stream);
+    queued = e == cudaSuccess;
+  }
+  if (e == cudaSuccess) e = cudaEventRecord(done, copy_stream);
+  lock.unlock();
+  if (e == cudaSuccess) e = cudaEventSynchronize(done);
+  else if (queued) cudaStreamSynchronize(copy_stream);  // nothing may outlive the call
+  lock.lock();
+  if (ready) cudaEventDestroy(ready);
+  if (done) cudaEventDestroy(done);
+  return e;
 }
 
 // Reuses `b` when it already holds `bytes`, else reallocates; fallible.  An
@@ -565,6 +622,8 @@ mgb_status mgb_provider_create(const mgb_settings *settings, mgb_provider **out)
   p->settings = st;
   p->sms = device_sms(st.device);
   e = cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->h2d, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->d2h, cudaStreamNonBlocking);
   if (e == cudaSuccess) {
     cudaMemPoolProps props = {};
     props.allocType = cudaMemAllocationTypePinned;
@@ -585,6 +644,8 @@ mgb_status mgb_provider_create(const mgb_settings *settings, mgb_provider **out)
     if (p->dev_bad) cudaFree(p->dev_bad);
     if (p->pool) cudaMemPoolDestroy(p->pool);
     if (p->stream) cudaStreamDestroy(p->stream);
+    if (p->h2d) cudaStreamDestroy(p->h2d);
+    if (p->d2h) cudaStreamDestroy(p->d2h);
     delete p;
     return cuda_fail(e, "provider set-up");
   }
@@ -614,11 +675,15 @@ void mgb_provider_destroy(mgb_provider *p) {
   for (auto &kv : p->storage) free_buf(p, kv.second.buf);
   for (auto &kv : p->packed) free_buf(p, kv.second.buf);
   free_buf(p, p->workspace);
+  p->reading.clear();  // no call may be in flight while the Provider is destroyed
+  for (auto &b : p->deferred) free_buf(p, b);
   if (p->stream) cudaStreamSynchronize(p->stream);
   if (p->pool) cudaMemPoolDestroy(p->pool);
   if (p->dev_err) cudaFree(p->dev_err);
   if (p->dev_bad) cudaFree(p->dev_bad);
   if (p->stream) cudaStreamDestroy(p->stream);
+  if (p->h2d) cudaStreamDestroy(p->h2d);
+  if (p->d2h) cudaStreamDestroy(p->d2h);
   delete p;
 }
 
@@ -676,36 +741,29 @@ mgb_status mgb_write_tensor(mgb_provider *p, const char *id, const uint64_t *sha
                             const float *data) {
   if (!p || !id || (rank > 0 && !shape) || rank < 0 || rank > MGB_MAX_RANK)
     return fail(MGB_INVALID_ARGUMENT, "invalid tensor arguments");
-  std::lock_guard<std::mutex> lock(p->mu);
+  std::unique_lock<std::mutex> lock(p->mu);
   cudaSetDevice(p->settings.device);
   std::vector<uint64_t> sh(shape, shape + rank);
   uint64_t elems = 1;
   for (uint64_t d : sh) elems *= d;
   if (elems && !data) return fail(MGB_INVALID_ARGUMENT, "null tensor data");
-  forget_packed(p, id);
+  // A new buffer (the pool hands back the memory of the previous one, in
+  // stream order): the resource keeps its old value until the upload is done,
+  // so a kernel submitted meanwhile from another thread reads old or new,
+  // never a half-written tensor.
   DevBuf buf;
-  auto it = p->storage.find(id);
-  if (it != p->storage.end() && it->second.buf.bytes == elems * 4) {
-    buf = it->second.buf;  // reuse the allocation
-    it->second.buf = DevBuf{};
-    p->storage.erase(it);
-  } else {
-    forget_tensor(p, id);
-    mgb_status s = ensure_buf(p, buf, elems * 4);
-    if (s != MGB_OK) return s;
-  }
+  mgb_status s = ensure_buf(p, buf, elems * 4);
+  if (s != MGB_OK) return s;
   if (elems) {
-    cudaError_t e = cudaMemcpyAsync(buf.ptr, data, elems * 4, cudaMemcpyHostToDevice, p->stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(p->stream);
+    cudaError_t e = copy_unlocked(p, lock, p->h2d, buf.ptr, data, elems * 4,
+                                  cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
       free_buf(p, buf);
       return cuda_fail(e, "tensor upload");
     }
   }
-  Tensor t;
-  t.shape = sh;
-  t.buf = buf;
-  p->storage[id] = t;
+  forget_packed(p, id);
+  put_tensor(p, id, sh, buf);
   return MGB_OK;
 }
 
@@ -756,7 +814,7 @@ mgb_status mgb_write_packed_weight(mgb_provider *p, const char *id, int32_t form
 mgb_status mgb_read_tensor(mgb_provider *p, const char *id, float *out, uint64_t capacity,
                            uint64_t *shape_out, int32_t *rank_out) {
   if (!p || !id) return fail(MGB_INVALID_ARGUMENT, "invalid arguments");
-  std::lock_guard<std::mutex> lock(p->mu);
+  std::unique_lock<std::mutex> lock(p->mu);
   cudaSetDevice(p->settings.device);
   const void *src = nullptr;
   std::vector<uint64_t> shape;
@@ -784,8 +842,12 @@ mgb_status mgb_read_tensor(mgb_provider *p, const char *id, float *out, uint64_t
       s = fail(MGB_INVALID_ARGUMENT, "output capacity %llu < %llu values",
                (unsigned long long)capacity, (unsigned long long)elems);
     } else if (elems) {
-      cudaError_t e = cudaMemcpyAsync(out, src, elems * 4, cudaMemcpyDeviceToHost, p->stream);
-      if (e == cudaSuccess) e = cudaStreamSynchronize(p->stream);
+      // the buffer stays allocated while the mutex is released: a release or
+      // overwrite of the resource meanwhile defers its free to `end_read`
+      void *key = const_cast<void *>(src);
+      if (!owned.ptr) p->reading[key]++;
+      cudaError_t e = copy_unlocked(p, lock, p->d2h, out, src, elems * 4, cudaMemcpyDeviceToHost);
+      if (!owned.ptr) end_read(p, key);
       if (e != cudaSuccess) s = cuda_fail(e, "tensor download");
     }
   }

@@ -204,3 +204,74 @@ def test_invalid_packed_bytes_are_rejected(provider):
     assert info.value.status == mgb.INVALID_ARGUMENT
     with pytest.raises(mgb.MgbError):
         provider.write_packed_weight_tensor("w", mgb.Q4_K, 4, 100, True, np.zeros(10, np.uint8))
+
+
+def test_calls_from_several_threads(provider, oracle):
+    """The reference's Provider methods take `&self` (src/native/mod.rs:565-700):
+    several threads may drive one Provider.  Uploads and downloads overlap
+    other threads' calls here; every thread must still get its own result."""
+    import threading
+
+    n, k, m = 512, 1024, 64
+    w = oracle.test_packed(mgb.Q4_K, n, k, 7)
+    provider.write_packed_weight_tensor("w", mgb.Q4_K, n, k, True, w)
+    rng = np.random.default_rng(3)
+    xs = [rng.standard_normal((m, k)).astype(np.float32) for _ in range(4)]
+    expect = []
+    for t, x in enumerate(xs):  # one thread first: the results to reproduce
+        provider.write_tensor(f"x{t}", x)
+        assert provider.complete_kernel(provider.submit_kernel("matmul", [f"x{t}", "w"], f"y{t}")).ok
+        expect.append(provider.read_tensor(f"y{t}"))
+    oracle.assert_close(expect[0], oracle.packed_matmul(mgb.Q4_K, w, n, k, xs[0]), _tol(m), "y0")
+    errors: list[str] = []
+
+    def lane(t: int) -> None:
+        for i in range(12):
+            provider.write_tensor(f"x{t}", xs[t])
+            r = provider.complete_kernel(provider.submit_kernel("matmul", [f"x{t}", "w"], f"y{t}"))
+            y = provider.read_tensor(f"y{t}")
+            if not r.ok or not np.array_equal(y, expect[t]):
+                errors.append(f"thread {t} step {i}: {r.reason or 'wrong values'}")
+
+    threads = [threading.Thread(target=lane, args=(t,)) for t in range(4)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    assert not errors, errors
+
+
+def test_release_and_overwrite_during_a_download(provider):
+    """A download reads its buffer with the Provider's mutex released: a
+    release or an overwrite of the same resource meanwhile must neither free
+    the buffer under the copy nor tear the values read."""
+    import threading
+
+    big = np.arange(16 << 20, dtype=np.float32).reshape(4096, 4096)  # 64 MiB
+    other = np.full_like(big, -1.0)
+    outcomes: list[str] = []
+    for trial in range(6):
+        provider.write_tensor("t", big)
+        got: list[object] = []
+
+        def reader() -> None:
+            try:
+                got.append(provider.read_tensor("t"))
+            except mgb.MgbError as e:
+                got.append(e.status)
+
+        th = threading.Thread(target=reader)
+        th.start()
+        if trial % 2:
+            provider.release_tensor("t")
+        else:
+            provider.write_tensor("t", other)
+        th.join()
+        v = got[0]
+        if isinstance(v, np.ndarray):
+            assert np.array_equal(v, big) or np.array_equal(v, other), f"trial {trial}: torn read"
+            outcomes.append("old" if np.array_equal(v, big) else "new")
+        else:
+            assert v == mgb.NOT_FOUND or v is None
+            outcomes.append("gone")
+    assert len(outcomes) == 6
