@@ -372,9 +372,9 @@ mgb_status mgb_quantize_rows(const float *x, uint64_t len, int8_t *values, float
  * with CUDA IPC).  No counterpart in the reference, which runs on one host. */
 #define MGB_MAX_TP 8
 /* Bytes of a rank's synchronisation words: done[MGB_MAX_TP] (u32 at offset 0,
- * word r written by rank r), the call's CTA counter (u32 at offset 128) and,
- * for device epochs, the rank's epoch word (u32 at offset 132, the word after
- * the counter). */
+ * word r written by rank r), a reserved word at offset 128 (`cta_counter`
+ * points at it) and, for device epochs, the rank's epoch word (u32 at offset
+ * 132, the word after it). */
 #define MGB_TP_SYNC_BYTES 256u
 #define MGB_TP_COUNTER_OFFSET 128u
 #define MGB_TP_EPOCH_OFFSET 132u
@@ -382,10 +382,12 @@ mgb_status mgb_quantize_rows(const float *x, uint64_t len, int8_t *values, float
 /* Where one rank's tensor-parallel call writes.  All pointers are valid on the
  * calling GPU (this rank's own buffers or IPC mappings of the peers').  Output
  * element (row, col) of the call goes to y[r] + row * ldy + col0 + col for
- * every r < world.  When every CTA has stored, the call stores its epoch with
- * release semantics (system scope) into done[r][rank] for every r;
- * `cta_counter` is this rank's counter word, zero before its first call (each
- * call leaves it zero).  The epoch is `epoch` (host epochs, counting from 1),
+ * every r < world, with plain stores.  After the call's last launch, a
+ * one-CTA kernel of the call waits for that launch's grid to complete (its
+ * stores performed) and stores the epoch with release semantics (system
+ * scope) into done[r][rank] for every r.  `cta_counter` locates this rank's
+ * synchronisation words: the word itself is reserved (zero; the call does not
+ * write it) and the epoch word follows it.  The epoch is `epoch` (host epochs, counting from 1),
  * or, when `epoch` is 0 (device epochs), the value of this rank's epoch word
  * (the word after `cta_counter`) plus one, and the call advances the word to
  * it as it publishes: a sequence of calls and waits captured in a CUDA graph

@@ -121,11 +121,11 @@ mgb_status run_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, co
     return MGB_OK;
   }
   if (k / 32 > 1024) return fail(MGB_UNSUPPORTED, "GEMV supports k <= 32768 (got %llu)", (unsigned long long)k);
-  // row pairs; a tensor-parallel call completes with its last launch
+  // row pairs
   for (uint64_t r = 0; r < m; r += 2) {
     const uint64_t rows = m - r < 2 ? m - r : 2;
     const float *add = addend_mode == 2 ? addend + r * n : addend;
-    OutSpec sub = r + rows < m ? without_completion(rows_from(out, r)) : rows_from(out, r);
+    OutSpec sub = rows_from(out, r);
     if (r > 0) sub = without_input_wait(sub);  // the first launch waited
     e = launch_gemv(format, w, n, k, x + r * k, rows, sub, add, addend_mode, err, sms, stream);
     if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");

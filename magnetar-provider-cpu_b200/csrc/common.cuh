@@ -220,34 +220,6 @@ __device__ __forceinline__ void out_store(const OutSpec &o, int m, uint64_t col,
   for (int r = 0; r < o.world; ++r) o.y_ranks[r][off] = v;
 }
 
-// Every thread that stored output calls this before the CTA barrier that
-// precedes out_complete: its stores (to peer GPUs too) become visible at
-// system scope.  (A fence executes per warp; on B200 a system fence drains
-// only the executing warp's stores, and one fence per CTA after the barrier
-// let a peer read stale columns of a chained call on two GPUs, so every
-// storing warp fences.)  A plain call (one rank) needs no fence.
-__device__ __forceinline__ void out_fence(const OutSpec &o) {
-  if (o.world > 1 || o.cta_counter) __threadfence_system();
-}
-
-// One thread per CTA, after a barrier that follows every out_fence of the CTA
-// and after this thread's griddepcontrol.wait (the previous call on the stream
-// has finished with the counter).  The CTA that counts last publishes the call.
-__device__ __forceinline__ void out_complete(const OutSpec &o, uint32_t total_ctas) {
-  if (!o.cta_counter) return;
-  __threadfence_system();
-  const uint32_t before = atomicAdd(o.cta_counter, 1u);
-  if (before != total_ctas - 1) return;
-  *o.cta_counter = 0;  // every CTA of this call has counted: ready for the next call
-  const uint32_t epoch = o.epoch_word ? *(volatile const uint32_t *)o.epoch_word + 1u : o.epoch;
-  if (o.epoch_word) *(volatile uint32_t *)o.epoch_word = epoch;  // the next call publishes epoch + 1
-  __threadfence_system();
-  for (int r = 0; r < o.world; ++r)
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(o.done_ranks[r] + o.rank), "r"(epoch)
-                 : "memory");
-}
-
-
 // ---- waits on the ranks of a tensor-parallel group ------------------------------------
 
 // Word index of the epoch word in a rank's synchronisation buffer

@@ -724,11 +724,8 @@ __global__ void __launch_bounds__(96 + 32 * DQW, 1)
                          reinterpret_cast<float *>(
                              smem + (size_t)(warp - 3) * (p.tma_out ? EPI_TMA_BYTES : EPI_SQUARE_BYTES)));
   }
-  out_fence(p.out);
   tc_fence_before();
   __syncthreads();
-  // (thread 0 is the activation producer: it has waited for the previous grid)
-  if (threadIdx.x == 0) out_complete(p.out, gridDim.x * gridDim.y);
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),

@@ -510,10 +510,6 @@ __global__ void __launch_bounds__(MAXT, MINB)
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * (p.stage_bytes + p.dec_stage_bytes));
   uint64_t *empty = full + S;
   float *red = reinterpret_cast<float *>(empty + S);  // [teams][chunk][RPT][team_warps][MR]
-  // A tensor-parallel call stages the CTA's outputs here and one warp stores
-  // them to every rank: only that warp's stores then need a system fence.
-  float *ostage = red + (size_t)p.teams * p.chunk * RPT * p.team_warps * MR;  // [rows][MR]
-  const bool staged_out = p.out.world > 1 || p.out.cta_counter;
   const int consumer_warps = p.teams * p.team_warps;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = blockIdx.x * p.rows_per_cta;
@@ -593,14 +589,10 @@ __global__ void __launch_bounds__(MAXT, MINB)
   }
 
   // x may be the previous kernel's output; the weight stream above never
-  // waits.  One warp waits for the previous grid (its completion, its memory
-  // made visible to this grid); the others block on a hardware barrier
-  // meanwhile, so no warp of this CTA spins while the previous kernel still
-  // computes on the SM.  The barrier orders every thread's x loads and y
-  // stores after that wait.  Each thread then loads and quantises its own run
-  // of x.
-  // Every consumer warp waits for the previous grid itself (a hardware wait,
-  // nothing spins), so its own loads of x are ordered after that grid's writes.
+  // waits.  Every consumer warp waits for the previous grid itself (its
+  // completion, its memory made visible to this grid; a hardware wait, nothing
+  // spins), so its own loads of x are ordered after that grid's writes.  Each
+  // thread then loads and quantises its own run of x.
   grid_dependency_wait();
   if (cw == 0 && p.out.wait_done) {
     // a tensor-parallel call's wait on the call before (peers' writes, which
@@ -658,26 +650,10 @@ __global__ void __launch_bounds__(MAXT, MINB)
             sum += red_team[((cc * RPT + i) * p.team_warps + wi) * MR + m];
           if (p.addend_mode == 1) sum = sum + __ldcg(p.addend + row);
           else if (p.addend_mode == 2) sum = sum + __ldcg(p.addend + (size_t)m * p.n + row);
-          if (staged_out) ostage[(size_t)(row - r0) * MR + m] = sum;
-          else out_store(p.out, m, row, sum);
+          out_store(p.out, m, row, sum);
         }
       }
       named_barrier(1 + team, team_threads);
-    }
-  }
-  // a tensor-parallel call: consumer warp 0 (past the grid dependency wait)
-  // stores the CTA's outputs into every rank's y, fences its stores at system
-  // scope, and counts the CTA.  (A system fence drains only the executing
-  // warp's stores: nine storing warps per CTA each fencing cost ~4.6 us more
-  // per call than this.)
-  if (staged_out) {
-    named_barrier(13, consumer_warps * 32);
-    if (cw == 0) {
-      const int total = (r1 - r0) * MR;
-      for (int i = lane; i < total; i += 32) out_store(p.out, i % MR, r0 + i / MR, ostage[i]);
-      out_fence(p.out);
-      __syncwarp();
-      if (lane == 0) out_complete(p.out, gridDim.x);
     }
   }
 }
@@ -763,9 +739,6 @@ __global__ void __launch_bounds__(MAXT, 1)
     }
     buf ^= 1;
   }
-  out_fence(out);
-  __syncthreads();
-  if (threadIdx.x == 0) out_complete(out, gridDim.x);
 }
 
 // ---- launch --------------------------------------------------------------------------
@@ -823,8 +796,7 @@ static size_t staged_config(int n, int k, int sms, GemvStaged &p, int &grid, int
   if (chunk > nst) chunk = nst;
   if (chunk < 1) chunk = 1;
   p.chunk = chunk;
-  // + the output staging of a tensor-parallel call: rows_per_cta x MR floats
-  const size_t fixed = red_stage * chunk + ceil_div((uint64_t)p.rows_per_cta * MR * 4, 16) * 16;
+  const size_t fixed = red_stage * chunk;
   const size_t per_stage = (size_t)p.stage_bytes + p.dec_stage_bytes + 16;
   // The 288-thread form stays within half an SM so the next GEMV's CTA can
   // stream its weights beside it; the 1024-thread form (k > 8192) takes the
@@ -891,8 +863,7 @@ template <int FMT, int MR>
 static cudaError_t launch_fmt(const void *w, int n, int k, const float *x, const OutSpec &out,
                               const float *addend, int addend_mode, int *err, int sms,
                               cudaStream_t stream) {
-  // Two activation rows in two launches: the first writes output row 0 and
-  // leaves the call's completion to the second, which writes row 1.
+  // (Two activation rows in the 1,024-thread forms: two launches, one per row.)
   const float *addend1 = addend_mode == 2 ? addend + n : addend;
   if (staged_ok((uint64_t)k)) {  // a team of at most 31 warps plus the producer
     // 288 threads with at most 112 registers each: two kernels' CTAs fit on an SM
@@ -902,8 +873,8 @@ static cudaError_t launch_fmt(const void *w, int n, int k, const float *x, const
       // 1024-thread CTAs have 64 registers per thread: one activation row per launch
       if (MR == 1)
         return launch_staged<FMT, 1, 1024, 1>(w, n, k, x, out, addend, addend_mode, err, sms, stream);
-      cudaError_t e = launch_staged<FMT, 1, 1024, 1>(w, n, k, x, without_completion(out), addend,
-                                                     addend_mode, err, sms, stream);
+      cudaError_t e = launch_staged<FMT, 1, 1024, 1>(w, n, k, x, out, addend, addend_mode, err,
+                                                     sms, stream);
       if (e == cudaSuccess)
         e = launch_staged<FMT, 1, 1024, 1>(w, n, k, x + k, without_input_wait(rows_from(out, 1)),
                                            addend1, addend_mode, err, sms, stream);
@@ -914,8 +885,8 @@ static cudaError_t launch_fmt(const void *w, int n, int k, const float *x, const
     return launch_simple<FMT, MR, 4, 256>(w, n, k, x, out, addend, addend_mode, err, sms, stream);
   if (MR == 1)
     return launch_simple<FMT, 1, 2, 1024>(w, n, k, x, out, addend, addend_mode, err, sms, stream);
-  cudaError_t e = launch_simple<FMT, 1, 2, 1024>(w, n, k, x, without_completion(out), addend,
-                                                 addend_mode, err, sms, stream);
+  cudaError_t e = launch_simple<FMT, 1, 2, 1024>(w, n, k, x, out, addend, addend_mode, err, sms,
+                                                 stream);
   if (e == cudaSuccess)
     e = launch_simple<FMT, 1, 2, 1024>(w, n, k, x + k, without_input_wait(rows_from(out, 1)),
                                        addend1, addend_mode, err, sms, stream);

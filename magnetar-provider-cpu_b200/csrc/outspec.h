@@ -10,13 +10,12 @@ constexpr int MAX_TP = 8;
 
 // Output element (row, col) of a call goes to y_ranks[r] + row * ldy + col0 +
 // col for every r < world (plain call: world 1, y_ranks[0] = y, ldy = n,
-// col0 = 0).  With cta_counter set, the call publishes its completion: every
-// CTA counts itself on cta_counter (zero before the call) once its stores are
-// done; the last one resets it and stores the call's epoch with system-scope
-// release into done_ranks[r][rank] for every r.  The epoch is `epoch`, or,
-// with epoch_word set (device epochs), *epoch_word + 1 read by that last CTA,
-// which also advances *epoch_word to it: a captured sequence of calls then
-// publishes fresh epochs on every replay.  With wait_done set, the kernel that
+// col0 = 0).  With cta_counter set (a tensor-parallel call), a one-CTA kernel
+// after the call's last launch publishes its completion (mgb_tp_publish_kernel):
+// it stores the call's epoch into done_ranks[r][rank] for every r.  The epoch
+// is `epoch`, or, with epoch_word set (device epochs), *epoch_word + 1, to
+// which that kernel also advances *epoch_word: a captured sequence of calls
+// then publishes fresh epochs on every replay.  With wait_done set, the kernel that
 // reads x first waits (after its griddepcontrol.wait) until every one of
 // wait_world ranks has published wait_epoch (0: the value of the epoch word of
 // that synchronisation buffer) into wait_done.
@@ -43,12 +42,6 @@ inline OutSpec plain_out(float *y, uint64_t n) {
   o.epoch_word = nullptr;
   o.wait_done = nullptr;
   o.epoch = 0;
-  return o;
-}
-
-// The same destination with its completion left to a later launch.
-inline OutSpec without_completion(OutSpec o) {
-  o.cta_counter = nullptr;
   return o;
 }
 
