@@ -384,7 +384,7 @@ mgb_status mgb_quantize_rows(const float *x, uint64_t len, int8_t *values, float
  * element (row, col) of the call goes to y[r] + row * ldy + col0 + col for
  * every r < world, with plain stores.  After the call's last launch, a
  * one-CTA kernel of the call waits for that launch's grid to complete (its
- * stores performed) and stores the epoch with release semantics (system
+ * stores performed at every rank's memory) and then stores the epoch (system
  * scope) into done[r][rank] for every r.  `cta_counter` locates this rank's
  * synchronisation words: the word itself is reserved (zero; the call does not
  * write it) and the epoch word follows it.  The epoch is `epoch` (host epochs, counting from 1),

@@ -223,15 +223,16 @@ __device__ __forceinline__ void out_store(const OutSpec &o, int m, uint64_t col,
 // ---- waits on the ranks of a tensor-parallel group ------------------------------------
 
 // Word index of the epoch word in a rank's synchronisation buffer
-// (MGB_TP_EPOCH_OFFSET / 4: after the done words and the CTA counter).
+// (MGB_TP_EPOCH_OFFSET / 4: after the done words and the reserved word).
 constexpr int TP_EPOCH_WORD = 33;
 
 // Lane r (< world) of one warp polls done[r] until it reaches `epoch` (serial
 // number arithmetic, so epochs may wrap), sleeping 32 to 128 ns between polls,
 // giving up after `timeout_ns` of the global timer or an iteration cap.  The
-// load is an acquire at system scope: what the publishing rank released
-// before its epoch is visible after.  Returns whether this lane's rank got
-// there; lanes >= world return true.
+// load is an acquire at system scope, so this thread's later loads are not
+// satisfied before it (the columns an epoch announces were performed before
+// the epoch was stored).  Returns whether this lane's rank got there; lanes
+// >= world return true.
 __device__ __forceinline__ bool poll_epoch(const uint32_t *done, int world, uint32_t epoch,
                                            uint64_t timeout_ns, int lane) {
   if (lane >= world) return true;

@@ -763,7 +763,7 @@ __global__ void mgb_f32_to_bf16_kernel(const float *__restrict__ x, __nv_bfloat1
 // Split-K: y = the partial planes summed in plane order (+ the addend); a
 // programmatic dependent of the GEMM that wrote them.
 __global__ void mgb_splitk_sum_kernel(const float *__restrict__ part, int planes, uint64_t m,
-                                  uint64_t n, float *__restrict__ y,
+                                  uint64_t n, const OutSpec out,
                                   const float *__restrict__ addend, int addend_mode) {
   grid_launch_dependents();
   grid_dependency_wait();
@@ -775,7 +775,7 @@ __global__ void mgb_splitk_sum_kernel(const float *__restrict__ part, int planes
     for (int z = 1; z < planes; ++z) v = v + __ldcg(part + z * total + i);
     if (addend_mode == 1) v = v + __ldcg(addend + i % n);
     else if (addend_mode == 2) v = v + __ldcg(addend + i);
-    y[i] = v;
+    out_store(out, (int)(i / n), i % n, v);  // every rank's y for a tensor-parallel call
   }
 }
 
@@ -902,11 +902,10 @@ cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const fl
   e = launch_dependent(mgb_f32_to_bf16_kernel, dim3((unsigned)blocks), dim3(256), 0,
                                    stream, x, xb, m * k, out, err);
   if (e != cudaSuccess) return e;
-  // one plain output and room for the partial planes: split K (a
-  // tensor-parallel call, even of one rank, publishes its completion from the
-  // GEMM's CTAs, which the sum pass would not do)
+  // room for the partial planes: split K (the sum pass writes every rank's y
+  // of a tensor-parallel call; the call publishes after it)
   const uint64_t base = gemm_workspace_bytes(fmt, m, n, k);
-  int s = out.world == 1 && !out.cta_counter ? choose_split(m, n, k, sms) : 1;
+  int s = choose_split(m, n, k, sms);
   while (s > 1 && workspace_bytes < base + (uint64_t)s * m * n * 4) s /= 2;
   if (s > 1) {
     float *part = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + base);
@@ -915,7 +914,7 @@ cudaError_t launch_gemm(int fmt, const void *w, uint64_t n, uint64_t k, const fl
       uint64_t sblocks = ceil_div(m * n, 256);
       if (sblocks > (uint64_t)sms * 8) sblocks = (uint64_t)sms * 8;
       e = launch_dependent(mgb_splitk_sum_kernel, dim3((unsigned)sblocks), dim3(256), 0, stream,
-                           (const float *)part, s, m, n, out.y_ranks[0], addend, addend_mode);
+                           (const float *)part, s, m, n, out, addend, addend_mode);
     }
     return e;
   }

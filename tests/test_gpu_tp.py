@@ -7,10 +7,12 @@ sets of synchronisation words, and the waits run after both calls have
 finished (no kernel waits on another kernel that may still be running on
 the same GPU).  With two GPUs, two processes run the real path over NVLink.
 
-Every output column is computed by the same kernel code as the unsharded
-call (the split is by whole stored rows, `packed_matmul`,
-src/native/mod.rs:135-150), so the gathered y must equal the unsharded
-`mgb_qmatmul` bit for bit, and the oracle within the kernels' tolerances.
+Every output column is computed by the same kernels as a plain call on the
+rank's shard (the split is by whole stored rows, `packed_matmul`,
+src/native/mod.rs:135-150), so the gathered y must equal the plain
+`mgb_qmatmul` of every shard side by side bit for bit (with the same
+workspace, so the same split-K choice), and the oracle within the kernels'
+tolerances.
 """
 
 from __future__ import annotations
@@ -48,18 +50,25 @@ def _device_layout(torch, fmt, ggml, rows, cols):
     return out
 
 
-def _unsharded(torch, fmt, w, n, k, xd):
-    # the minimum workspace: one K pass, as every tensor-parallel call runs
+def _plain_shards(torch, fmt, w, n, k, xd, world=1):
+    """The plain `mgb_qmatmul` of each of `world` shards, side by side, each
+    with its preferred workspace as the tensor-parallel calls get it (a split-K
+    choice depends on the shard's width, so the shard is the unit that matches
+    bit for bit)."""
     m = xd.shape[0]
-    wd = _device_layout(torch, fmt, w, n, k)
-    y = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
-    ws_bytes = mgb.qmatmul_min_workspace_bytes(fmt, m, n, k)
-    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
-    mgb.qmatmul(fmt, wd.data_ptr(), n, k, xd.data_ptr(), m, y.data_ptr(),
-                workspace_ptr=ws.data_ptr(), workspace_bytes=ws_bytes,
-                stream=torch.cuda.current_stream().cuda_stream)
-    torch.cuda.synchronize()
-    return y.cpu().numpy()
+    n_loc = n // world
+    cols = []
+    for r in range(world):
+        wd = _device_layout(torch, fmt, tp.shard_packed(fmt, w, n, k, world, r), n_loc, k)
+        y = torch.full((m, n_loc), float("nan"), dtype=torch.float32, device="cuda")
+        ws_bytes = mgb.qmatmul_workspace_bytes(fmt, m, n_loc, k)
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+        mgb.qmatmul(fmt, wd.data_ptr(), n_loc, k, xd.data_ptr(), m, y.data_ptr(),
+                    workspace_ptr=ws.data_ptr(), workspace_bytes=ws_bytes,
+                    stream=torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        cols.append(y.cpu().numpy())
+    return np.concatenate(cols, axis=1)
 
 
 CASES = [
@@ -120,7 +129,7 @@ def test_emulated_two_ranks_gather_every_column(torch_cuda, oracle, fmt, n, k, m
         for p in sync:
             mgb.device_free(p)
     np.testing.assert_array_equal(got[0], got[1])
-    np.testing.assert_array_equal(got[0], _unsharded(torch, fmt, w, n, k, xd))
+    np.testing.assert_array_equal(got[0], _plain_shards(torch, fmt, w, n, k, xd, world))
     oracle.assert_close(got[0], oracle.packed_matmul(fmt, w, n, k, x),
                         GEMV_TOL if m <= 2 else GEMM_TOL, f"tp fmt {fmt} m {m}")
 
@@ -185,7 +194,7 @@ def test_emulated_two_ranks_device_epochs_replay_in_a_graph(torch_cuda, fmt, n, 
             assert epoch_words() == [2 + replay] * world
             got = [y.cpu().numpy() for y in ys]
             np.testing.assert_array_equal(got[0], got[1])
-            np.testing.assert_array_equal(got[0], _unsharded(torch, fmt, w, n, k, x))
+            np.testing.assert_array_equal(got[0], _plain_shards(torch, fmt, w, n, k, x, world))
     finally:
         del graph
         torch.cuda.synchronize()
@@ -241,8 +250,8 @@ def test_emulated_two_ranks_chained_call_waits_inside_its_first_kernel(torch_cud
                 mgb.tp_wait(sync_b[r], world, e, 2000, sp)
             torch.cuda.synchronize()
             assert mgb.take_device_error(dev) == 0
-            ref_a = _unsharded(torch, fmt_a, wa, n1, k, xd)
-            ref_b = _unsharded(torch, fmt_b, wb, n2, n1, torch.from_numpy(ref_a).cuda())
+            ref_a = _plain_shards(torch, fmt_a, wa, n1, k, xd, world)
+            ref_b = _plain_shards(torch, fmt_b, wb, n2, n1, torch.from_numpy(ref_a).cuda(), world)
             for r in range(world):
                 np.testing.assert_array_equal(ya[r].cpu().numpy(), ref_a)
                 got = yb[r].cpu().numpy()
@@ -285,9 +294,9 @@ def test_input_wait_for_an_epoch_nobody_publishes_times_out(torch_cuda):
 @pytest.mark.parametrize("m", [64, 1])
 @pytest.mark.parametrize("epoch", [1, 0])
 def test_one_rank_call_publishes_its_completion(torch_cuda, m, epoch):
-    """A tensor-parallel call of one rank runs one K pass (the split-K sum pass
-    publishes nothing) and publishes its epoch, host (1) or device (0), so its
-    wait returns at once and y equals the unsharded call."""
+    """A tensor-parallel call of one rank (split K at m = 64, the sum pass
+    before the publish kernel) publishes its epoch, host (1) or device (0), so
+    its wait returns at once and y equals the plain call."""
     torch = torch_cuda
     fmt, n, k = synthetic.Q4_K, 512, 1024
     w = synthetic.packed_weights(fmt, n, k, seed=29)
@@ -309,7 +318,7 @@ def test_one_rank_call_publishes_its_completion(torch_cuda, m, epoch):
         got = y.cpu().numpy()
     finally:
         mgb.device_free(sync)
-    np.testing.assert_array_equal(got, _unsharded(torch, fmt, w, n, k, xd))
+    np.testing.assert_array_equal(got, _plain_shards(torch, fmt, w, n, k, xd))
 
 
 def test_wait_for_an_epoch_nobody_publishes_times_out(torch_cuda):
@@ -338,7 +347,7 @@ def test_reset_after_an_expired_wait(torch_cuda, device_epochs):
     op = tp.FusedShardedPackedMatmul(fmt, w, n, k, 1, 0, max_m=m, device_epochs=device_epochs)
     dev = torch.cuda.current_device()
     try:
-        ref = _unsharded(torch, fmt, w, n, k, xd)
+        ref = _plain_shards(torch, fmt, w, n, k, xd)
         assert np.array_equal(op(xd).cpu().numpy(), ref)
         assert mgb.take_device_error(dev) == 0
         # a peer that never publishes: wait for an epoch nobody reaches
@@ -382,7 +391,7 @@ def _rank_main(rank: int, world: int, port: int, out) -> None:
         for call, m in enumerate([1, 2, 64, 5, 1, 64]):
             xd = torch.from_numpy(synthetic.activations(m, k, seed=40 + call)).to(dev)
             y = op(xd).cpu().numpy()
-            ref = _unsharded(torch, fmt, w, n, k, xd)
+            ref = _plain_shards(torch, fmt, w, n, k, xd, world)
             if not np.array_equal(y, ref):
                 mismatches.append((call, m, float(np.nanmax(np.abs(y - ref)))))
         # a chained pair: the second call reads the first's gathered y and
@@ -396,8 +405,8 @@ def _rank_main(rank: int, world: int, port: int, out) -> None:
                 xd = torch.from_numpy(synthetic.activations(m, k, seed=80 + call)).to(dev)
                 y1 = op(xd, wait=False)
                 y2 = op2(y1, after=op).cpu().numpy()
-                ref1 = _unsharded(torch, fmt, w, n, k, xd)
-                ref2 = _unsharded(torch, fmt, w2, n2, n, torch.from_numpy(ref1).to(dev))
+                ref1 = _plain_shards(torch, fmt, w, n, k, xd, world)
+                ref2 = _plain_shards(torch, fmt, w2, n2, n, torch.from_numpy(ref1).to(dev), world)
                 if not np.array_equal(y2, ref2):
                     bad = np.argwhere(y2 != ref2)
                     mismatches.append(("chained", call, m, sorted(set(bad[:, 0].tolist()))))
@@ -414,7 +423,7 @@ def _rank_main(rank: int, world: int, port: int, out) -> None:
         dist.destroy_process_group()
 
 
-def test_two_gpus_fused_gather_matches_unsharded(torch_cuda):
+def test_two_gpus_fused_gather_matches_plain_shards(torch_cuda):
     torch = torch_cuda
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
