@@ -785,7 +785,12 @@ static size_t staged_config(int n, int k, int sms, GemvStaged &p, int &grid, int
   p.dec_stage_bytes = (uint32_t)(TR * runs * 8);
   threads = 32 * (1 + p.teams * p.team_warps);
   const int units = (int)ceil_div((uint64_t)n, (uint64_t)TR);
-  grid = sms;
+  // One CTA per SM, or two for long 288-thread launches (at least 16 stages
+  // of rows per SM): twice the warps to hide the dot products' latency, at the
+  // cost of the next kernel's CTAs finding no free slot until these finish
+  // (graph-replayed chains, one B200: N = 65,536, K = 4,096: 43.5 -> 39.4 us;
+  // N = 28,672, K = 8,192: 39.9 -> 38.4 us; shorter launches keep one).
+  grid = (MAXT == 288 && units >= 16 * sms) ? 2 * sms : sms;
   if (grid > units) grid = units;
   p.rows_per_cta = (int)ceil_div((uint64_t)n, (uint64_t)grid);
   grid = (int)ceil_div((uint64_t)n, (uint64_t)p.rows_per_cta);
