@@ -214,10 +214,15 @@ __host__ __device__ inline uint64_t ceil_div(uint64_t a, uint64_t b) { return (a
 
 // ---- output fan-out and completion of a tensor-parallel call ----------------------
 
-// Output element (m, col) of this call, written to every rank's y.
+// Output element (m, col) of this call, written to every rank's y.  The rank
+// loop is unrolled over MAX_TP so y_ranks is only indexed by constants: a
+// runtime index into the kernel parameter would make every thread copy the
+// whole OutSpec into local memory at entry.
 __device__ __forceinline__ void out_store(const OutSpec &o, int m, uint64_t col, float v) {
   const uint64_t off = (uint64_t)m * o.ldy + o.col0 + col;
-  for (int r = 0; r < o.world; ++r) o.y_ranks[r][off] = v;
+#pragma unroll
+  for (int r = 0; r < MAX_TP; ++r)
+    if (r < o.world) o.y_ranks[r][off] = v;
 }
 
 // ---- waits on the ranks of a tensor-parallel group ------------------------------------
