@@ -134,6 +134,56 @@ def test_emulated_two_ranks_gather_every_column(torch_cuda, oracle, fmt, n, k, m
                         GEMV_TOL if m <= 2 else GEMM_TOL, f"tp fmt {fmt} m {m}")
 
 
+@pytest.mark.parametrize("world", [4, 8])
+@pytest.mark.parametrize("fmt,n,k,m", [(synthetic.Q4_K, 512, 1024, 1),
+                                       (synthetic.Q4_K, 512, 1024, 2),
+                                       (synthetic.Q4_K, 512, 1024, 64),
+                                       (synthetic.Q4_K, 1024, 2048, 130),
+                                       (synthetic.Q6_K, 512, 1024, 96)])
+def test_emulated_four_and_eight_ranks(torch_cuda, oracle, world, fmt, n, k, m):
+    """The scaling run's group sizes: every rank stores into all 4 or 8 ranks'
+    y and publishes into all of their done words (the eight-rank case fills
+    every slot of the output description).  Ranks emulated one after the
+    other on one GPU."""
+    torch = torch_cuda
+    w = synthetic.packed_weights(fmt, n, k, seed=24)
+    x = synthetic.activations(m, k, seed=25)
+    xd = torch.from_numpy(x).cuda()
+    n_loc = n // world
+    shards = [_device_layout(torch, fmt, tp.shard_packed(fmt, w, n, k, world, r), n_loc, k)
+              for r in range(world)]
+    ys = [torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda") for _ in range(world)]
+    sync = [mgb.device_alloc(mgb.TP_SYNC_BYTES) for _ in range(world)]
+    ws_bytes = mgb.qmatmul_workspace_bytes(fmt, m, n_loc, k)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+    sp = torch.cuda.current_stream().cuda_stream
+    try:
+        for epoch in (1, 2):
+            for r in range(world):
+                out = mgb.tp_out([y.data_ptr() for y in ys], sync,
+                                 sync[r] + mgb.TP_COUNTER_OFFSET, ldy=n, col0=r * n_loc,
+                                 epoch=epoch, rank=r)
+                mgb.qmatmul_tp(fmt, shards[r].data_ptr(), n_loc, k, xd.data_ptr(), m, out,
+                               workspace_ptr=ws.data_ptr(), workspace_bytes=ws_bytes, stream=sp)
+            for r in range(world):
+                mgb.tp_wait(sync[r], world, epoch, 2000, sp)
+            torch.cuda.synchronize()
+            assert mgb.take_device_error(torch.cuda.current_device()) == 0
+            for r in range(world):
+                words = torch.as_tensor(tp._DeviceArray(sync[r], (mgb.TP_SYNC_BYTES // 4,)),
+                                        device="cuda").view(torch.int32).cpu().numpy()
+                assert list(words[:world]) == [epoch] * world
+        got = [y.cpu().numpy() for y in ys]
+    finally:
+        for q in sync:
+            mgb.device_free(q)
+    ref = _plain_shards(torch, fmt, w, n, k, xd, world)
+    for r in range(world):
+        np.testing.assert_array_equal(got[r], ref)
+    oracle.assert_close(got[0], oracle.packed_matmul(fmt, w, n, k, x),
+                        GEMV_TOL if m <= 2 else GEMM_TOL, f"tp{world} fmt {fmt} m {m}")
+
+
 @pytest.mark.parametrize("fmt,n,k,m", [(synthetic.Q4_K, 512, 1024, 64),
                                        (synthetic.Q4_K, 512, 1024, 1),
                                        (synthetic.Q6_K, 256, 16384, 2)])
