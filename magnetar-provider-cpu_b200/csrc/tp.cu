@@ -97,8 +97,8 @@ static mgb_status to_outspec(const mgb_tp_out *o, uint64_t n, OutSpec &spec) {
     spec.done_ranks[r] = o->done[r];
   }
   spec.cta_counter = o->cta_counter;
-  // epoch 0: device epochs, from this rank's epoch word (the word after its
-  // CTA counter)
+  // epoch 0: device epochs, from this rank's epoch word (the word after the
+  // reserved word `cta_counter` points at)
   spec.epoch_word = o->epoch == 0 ? o->cta_counter + 1 : nullptr;
   if (o->wait_done) {
     if (o->wait_world < 1 || o->wait_world > MGB_MAX_TP)

@@ -236,7 +236,7 @@ class FusedShardedPackedMatmul(ShardedPackedMatmul):
         """Recovery after a wait gave up (device error 1, a peer that never
         published): the ranks' epochs then disagree and every later wait would
         expire too.  Collective: every rank drains its stream, all ranks zero
-        their synchronisation words (counter, epoch word, done words) between
+        their synchronisation words (reserved word, epoch word, done words) between
         two barriers, and epochs restart from 1."""
         import torch
         import torch.distributed as dist

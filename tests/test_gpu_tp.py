@@ -108,7 +108,7 @@ def test_emulated_two_ranks_gather_every_column(torch_cuda, oracle, fmt, n, k, m
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
     sp = torch.cuda.current_stream().cuda_stream
     try:
-        for epoch in (1, 2, 3):  # the CTA counters must come back to zero each call
+        for epoch in (1, 2, 3):  # the reserved words stay zero, the done words advance
             for r in range(world):
                 out = mgb.tp_out([y.data_ptr() for y in ys], sync,
                                  sync[r] + mgb.TP_COUNTER_OFFSET, ldy=n, col0=r * (n // world),
