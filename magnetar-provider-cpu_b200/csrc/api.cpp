@@ -120,7 +120,6 @@ mgb_status run_qmatmul(int32_t format, const void *w, uint64_t n, uint64_t k, co
     if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
     return MGB_OK;
   }
-  if (k / 32 > 1024) return fail(MGB_UNSUPPORTED, "GEMV supports k <= 32768 (got %llu)", (unsigned long long)k);
   // row pairs
   for (uint64_t r = 0; r < m; r += 2) {
     const uint64_t rows = m - r < 2 ? m - r : 2;

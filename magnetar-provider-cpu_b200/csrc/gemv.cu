@@ -659,8 +659,13 @@ __global__ void __launch_bounds__(MAXT, MINB)
 }
 
 // ---- fallback kernel for k % 256 != 0 (ragged scale planes): direct loads -------------
+//
+// Thread u owns run u.  With more runs than threads (K > 32 * MAXT, MULTI) each
+// thread takes runs u, u + blockDim, ... in turn and loads each run's x inside
+// the row loop: slower, but no K is refused (a 405B-class down projection has
+// K = 53,248).
 
-template <int FMT, int MR, int R, int MAXT>
+template <int FMT, int MR, int R, int MAXT, bool MULTI>
 __global__ void __launch_bounds__(MAXT, 1)
     mgb_gemv_simple_kernel(const uint8_t *__restrict__ w, int n, int k, const float *__restrict__ x,
                        const OutSpec out, const float *__restrict__ addend, int addend_mode,
@@ -677,47 +682,53 @@ __global__ void __launch_bounds__(MAXT, 1)
     __syncthreads();
   }
   XRun xr[MR];
-  load_x<FMT, MR>(x, k, u, active, xr);
+  if (!MULTI) load_x<FMT, MR>(x, k, u, active, xr);
   uint32_t lut[4] = {0, 0, 0, 0};
   if (FMT == IQ4_NL) iq4_table(lut);
   const int r0 = blockIdx.x * rows_per_cta;
   const int r1 = min(n, r0 + rows_per_cta);
   const uint8_t *scale_plane = w + L.qs_bytes;
+  const int groups = MULTI ? (runs + (int)blockDim.x - 1) / (int)blockDim.x : 1;
   int buf = 0;
   for (int r = r0; r < r1; r += R) {
     float part[R * MR];
 #pragma unroll
-    for (int i = 0; i < R; ++i) {
-      const int row = r + i;
+    for (int i = 0; i < R * MR; ++i) part[i] = 0.f;
+    for (int gi = 0; gi < groups; ++gi) {
+      const int uu = MULTI ? u + gi * (int)blockDim.x : u;
+      const bool act = MULTI ? uu < runs : active;
+      if (MULTI) load_x<FMT, MR>(x, k, uu, act, xr);
 #pragma unroll
-      for (int m = 0; m < MR; ++m) part[i * MR + m] = 0.f;
-      if (active && row < r1) {
-        const uint8_t *qrow = w + (size_t)row * L.qs_row;
-        const uint8_t *srow = scale_plane + (size_t)row * L.sc_row;
-        uint4 qa, qb = make_uint4(0, 0, 0, 0), hd = make_uint4(0, 0, 0, 0);
-        uint32_t dh = 0;
-        if (FMT == Q8_0) {
-          qa = ld_stream_v4(qrow + (size_t)u * 32);
-          qb = ld_stream_v4(qrow + (size_t)u * 32 + 16);
-        } else if (FMT == Q6_K) {
-          qa = ld_stream_v4(qrow + q6k_nib_offset((uint64_t)u));
-          const uint2 h2 = __ldg(reinterpret_cast<const uint2 *>(qrow + q6k_high_offset((uint64_t)u)));
-          qb = make_uint4(h2.x, h2.y, 0, 0);
-        } else {
-          qa = ld_stream_v4(qrow + (size_t)u * 16);
+      for (int i = 0; i < R; ++i) {
+        const int row = r + i;
+        if (act && row < r1) {
+          const uint8_t *qrow = w + (size_t)row * L.qs_row;
+          const uint8_t *srow = scale_plane + (size_t)row * L.sc_row;
+          uint4 qa, qb = make_uint4(0, 0, 0, 0), hd = make_uint4(0, 0, 0, 0);
+          uint32_t dh = 0;
+          if (FMT == Q8_0) {
+            qa = ld_stream_v4(qrow + (size_t)uu * 32);
+            qb = ld_stream_v4(qrow + (size_t)uu * 32 + 16);
+          } else if (FMT == Q6_K) {
+            qa = ld_stream_v4(qrow + q6k_nib_offset((uint64_t)uu));
+            const uint2 h2 = __ldg(reinterpret_cast<const uint2 *>(qrow + q6k_high_offset((uint64_t)uu)));
+            qb = make_uint4(h2.x, h2.y, 0, 0);
+          } else {
+            qa = ld_stream_v4(qrow + (size_t)uu * 16);
+          }
+          if (FMT == Q4_K) hd = __ldg(reinterpret_cast<const uint4 *>(srow + (size_t)(uu >> 3) * 16));
+          else if (FMT == Q5_K) {
+            hd = __ldg(reinterpret_cast<const uint4 *>(srow + (size_t)(uu >> 3) * 48));
+            qb.x = __ldg(reinterpret_cast<const uint32_t *>(srow + (size_t)(uu >> 3) * 48 + 16 + (uu & 7) * 4));
+          } else if (FMT == Q6_K) {
+            hd = __ldg(reinterpret_cast<const uint4 *>(srow + (size_t)(uu >> 3) * 32));
+            dh = ld_nc_u16(srow + (size_t)(uu >> 3) * 32 + 16);
+          } else dh = ld_nc_u16(srow + (size_t)uu * 2);
+          float pm[MR];
+          run_partials<FMT, MR>(qa, qb, hd, dh, uu & 7, xr, lut, pm);
+#pragma unroll
+          for (int m = 0; m < MR; ++m) part[i * MR + m] = gi == 0 ? pm[m] : part[i * MR + m] + pm[m];
         }
-        if (FMT == Q4_K) hd = __ldg(reinterpret_cast<const uint4 *>(srow + (size_t)(u >> 3) * 16));
-        else if (FMT == Q5_K) {
-          hd = __ldg(reinterpret_cast<const uint4 *>(srow + (size_t)(u >> 3) * 48));
-          qb.x = __ldg(reinterpret_cast<const uint32_t *>(srow + (size_t)(u >> 3) * 48 + 16 + (u & 7) * 4));
-        } else if (FMT == Q6_K) {
-          hd = __ldg(reinterpret_cast<const uint4 *>(srow + (size_t)(u >> 3) * 32));
-          dh = ld_nc_u16(srow + (size_t)(u >> 3) * 32 + 16);
-        } else dh = ld_nc_u16(srow + (size_t)u * 2);
-        float pm[MR];
-        run_partials<FMT, MR>(qa, qb, hd, dh, u & 7, xr, lut, pm);
-#pragma unroll
-        for (int m = 0; m < MR; ++m) part[i * MR + m] = pm[m];
       }
     }
     {
@@ -849,7 +860,8 @@ static cudaError_t launch_simple(const void *w, int n, int k, const float *x, co
                                  const float *addend, int addend_mode, int *err, int sms,
                                  cudaStream_t stream) {
   const int runs = k / RUN;
-  const int threads = ((runs + 31) / 32) * 32;
+  const bool multi = runs > MAXT;  // more runs than threads: each thread takes several
+  const int threads = multi ? MAXT : ((runs + 31) / 32) * 32;
   int per_sm = 2048 / threads;
   if (per_sm < 1) per_sm = 1;
   if (per_sm > 8) per_sm = 8;
@@ -857,8 +869,12 @@ static cudaError_t launch_simple(const void *w, int n, int k, const float *x, co
   int rows = (int)ceil_div((uint64_t)n, (uint64_t)target);
   if (rows < 1) rows = 1;
   const int grid = (int)ceil_div((uint64_t)n, (uint64_t)rows);
-  mgb_gemv_simple_kernel<FMT, MR, R, MAXT><<<grid, threads, 0, stream>>>(
-      static_cast<const uint8_t *>(w), n, k, x, out, addend, addend_mode, rows, err);
+  if (multi)
+    mgb_gemv_simple_kernel<FMT, MR, R, MAXT, true><<<grid, threads, 0, stream>>>(
+        static_cast<const uint8_t *>(w), n, k, x, out, addend, addend_mode, rows, err);
+  else
+    mgb_gemv_simple_kernel<FMT, MR, R, MAXT, false><<<grid, threads, 0, stream>>>(
+        static_cast<const uint8_t *>(w), n, k, x, out, addend, addend_mode, rows, err);
   return cudaGetLastError();
 }
 

@@ -97,8 +97,11 @@ def test_dequantize_full_size_bit_exact(torch_cuda, oracle, fmt):
 
 @pytest.mark.parametrize("fmt", FORMATS)
 @pytest.mark.parametrize("m", [1, 2])
-@pytest.mark.parametrize("n,k", [(37, 512), (5, 96), (300, 8192), (64, 14336), (16, 32768)])
+@pytest.mark.parametrize("n,k", [(37, 512), (5, 96), (300, 8192), (64, 14336), (16, 32768),
+                                 (24, 40960), (9, 32800)])
 def test_gemv_parity(torch_cuda, oracle, fmt, m, n, k):
+    """Down to K = 96 and up past 1,024 runs (K = 40,960 and the ragged 32,800:
+    more runs than a CTA has threads, each thread taking several)."""
     if fmt in (mgb.Q4_K, mgb.Q5_K, mgb.Q6_K) and k % 256:
         pytest.skip("the K-quant formats need whole 256-value super-blocks")
     torch = torch_cuda
@@ -111,6 +114,19 @@ def test_gemv_parity(torch_cuda, oracle, fmt, m, n, k):
     # activations held as 16-bit integers per 32-value run (|error| <= 2^-16 of
     # the run's largest value), exact integer dots: ~2e-5, far inside 1e-3
     assert err < 1e-4
+
+
+@pytest.mark.parametrize("fmt", [mgb.Q8_0, mgb.IQ4_NL])
+def test_ragged_large_k_batch(torch_cuda, oracle, fmt):
+    """m = 3 with K = 32,800 (a multiple of 32, not of 256): no tensor-core form
+    applies, so the rows go in pairs through the direct-load GEMV, whose
+    threads each take two runs."""
+    torch = torch_cuda
+    m, n, k = 3, 40, 32800
+    w = oracle.test_packed(fmt, n, k, 23)
+    x = oracle.test_activations(m, k, 5)
+    y = _qmatmul(torch, fmt, _device_layout(torch, fmt, w, n, k), n, k, x)
+    oracle.assert_close(y, oracle.packed_matmul(fmt, w, n, k, x), GEMV_TOL, f"fmt {fmt} k {k}")
 
 
 @pytest.mark.parametrize("fmt", [mgb.Q4_K])

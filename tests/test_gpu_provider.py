@@ -275,3 +275,18 @@ def test_release_and_overwrite_during_a_download(provider):
             assert v == mgb.NOT_FOUND or v is None
             outcomes.append("gone")
     assert len(outcomes) == 6
+
+
+@pytest.mark.parametrize("fmt", [mgb.Q4_K, mgb.Q8_0])
+def test_zero_rows_and_large_k(provider, oracle, fmt):
+    """An activation of zero rows gives a [0, N] output, as the reference's
+    packed_matmul does for an empty batch (src/native/mod.rs:109-152); and a
+    K past 1,024 runs (a 405B-class down projection) is served, not refused."""
+    n, k = 16, 40960
+    w = oracle.test_packed(fmt, n, k, 31)
+    provider.write_packed_weight_tensor("w", fmt, n, k, True, w)
+    y0 = provider.matmul(np.zeros((0, k), np.float32), "w")
+    assert y0.shape == (0, n)
+    x = oracle.test_activations(2, k, 7)
+    oracle.assert_close(provider.matmul(x, "w"), oracle.packed_matmul(fmt, w, n, k, x), 1e-3,
+                        f"fmt {fmt} k {k}")
