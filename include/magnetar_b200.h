@@ -185,7 +185,11 @@ mgb_status mgb_kernel_advertisement_get(size_t index, mgb_kernel_advertisement *
 /* ---- tensor storage (`ProviderExecutionApi`, src/native/mod.rs:629-811) -------------- */
 
 /* `write_tensor` (mod.rs:629-636): stores an f32 tensor, forgetting any packed
- * weight under `id`. */
+ * weight under `id`.  Returns once `data` has been copied (the caller may reuse
+ * it).  The values go to a new device buffer and the old one is freed after
+ * the work queued before it, so a kernel submitted meanwhile from another
+ * thread reads the old or the new tensor, never a mixture; the upload runs on
+ * its own stream with the Provider's lock released while the host waits. */
 mgb_status mgb_write_tensor(mgb_provider *provider, const char *id, const uint64_t *shape,
                             int32_t rank, const float *data);
 /* `write_packed_weight_tensor` (mod.rs:638-653): copies the checkpoint's block
@@ -197,7 +201,10 @@ mgb_status mgb_write_packed_weight(mgb_provider *provider, const char *id, int32
                                    int32_t transposed, const void *bytes, uint64_t len,
                                    int32_t *stored);
 /* `read_tensor` (src/lib.rs:1615-1620): f32 values in logical shape; a packed
- * weight reads back dequantised (bit-exact to the reference `decode`).
+ * weight reads back dequantised (bit-exact to the reference `decode`).  The
+ * download runs on its own stream after the work queued before the call, with
+ * the Provider's lock released while the host waits (a release or overwrite of
+ * `id` meanwhile waits for the download before freeing its buffer).
  * shape_out has room for MGB_MAX_RANK entries; MGB_NOT_FOUND when absent. */
 mgb_status mgb_read_tensor(mgb_provider *provider, const char *id, float *out,
                            uint64_t capacity, uint64_t *shape_out, int32_t *rank_out);
