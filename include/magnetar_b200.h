@@ -280,8 +280,8 @@ mgb_status mgb_repack(int32_t format, const void *ggml_blocks, uint64_t stored_r
  * different f32 summation order than one pass, same tolerance, deterministic).
  * Any workspace of at least mgb_qmatmul_min_workspace_bytes (the bf16 copy
  * alone) also takes the tensor-core path, in one K pass (a workspace in
- * between splits fewer ways); the tensor-parallel call (mgb_qmatmul_tp)
- * always runs one K pass. */
+ * between splits fewer ways).  The tensor-parallel call (mgb_qmatmul_tp)
+ * follows the same rule for its shard. */
 uint64_t mgb_qmatmul_workspace_bytes(int32_t format, uint64_t m, uint64_t n, uint64_t k);
 uint64_t mgb_qmatmul_min_workspace_bytes(int32_t format, uint64_t m, uint64_t n, uint64_t k);
 /* y[m, n] = x[m, k] * W^T on `stream`, W (device layout, 16-byte aligned)
