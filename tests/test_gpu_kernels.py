@@ -192,12 +192,15 @@ def test_gemm_config1_sampled_columns(torch_cuda, oracle):
 @pytest.mark.parametrize("m,n,k,parts", [(3, 300, 1024, 4), (64, 8192, 4096, 2),
                                          (128, 1001, 2048, 8), (17, 64, 14336, 8),
                                          (8, 512, 1536, 2), (64, 14336, 4096, 1),
-                                         (16, 4096, 4096, 4), (200, 1000, 1024, 1)])
+                                         (16, 4096, 4096, 4), (200, 1000, 1024, 4),
+                                         (512, 1792, 4096, 4), (256, 1792, 4096, 8),
+                                         (512, 1024, 8192, 4), (512, 3584, 8192, 2),
+                                         (512, 3584, 4096, 1), (600, 1024, 8192, 1)])
 def test_gemm_split_k(torch_cuda, oracle, fmt, m, n, k, parts):
-    """With the preferred workspace a call of m <= 128 rows with narrow tiles
-    splits K over 2, 4 or 8 CTAs per tile and sums the parts in a fixed
-    order: the result is deterministic and matches the oracle, and the
-    one-pass call (minimum workspace) to within the same tolerance."""
+    """With the preferred workspace a call of m <= 512 rows with narrow tiles
+    (or, past 128 rows, a long K) splits K over 2, 4 or 8 CTAs per tile and
+    sums the parts in a fixed order: the result is deterministic and matches
+    the one-pass call (minimum workspace) to within the GEMM tolerance."""
     torch = torch_cuda
     planes = 0 if parts == 1 else parts
     assert mgb.qmatmul_workspace_bytes(fmt, m, n, k) == \
