@@ -55,7 +55,11 @@ def test_status_names_and_packed_sizes():
     assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 130, 4096, 4096) == \
         130 * 4096 * 2 + 4 * 130 * 4096 * 4
     assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 512, 3584, 4096) == 512 * 4096 * 2
-    assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 600, 1024, 8192) == 600 * 8192 * 2  # m > 512
+    assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 600, 1024, 8192) == \
+        600 * 8192 * 2 + 4 * 600 * 1024 * 4
+    assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 2048, 3584, 8192) == 2048 * 8192 * 2  # wide tiles
+    assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 2048, 128, 8192) == \
+        2048 * 8192 * 2 + 8 * 2048 * 128 * 4  # a sparse grid of narrow tiles
     assert mgb.qmatmul_workspace_bytes(mgb.Q4_K, 64, 512, 256 * 3) == 64 * 768 * 2  # k % 512
     assert mgb.qmatmul_min_workspace_bytes(mgb.Q4_K, 2, 512, 4096) == 0
 
