@@ -815,7 +815,9 @@ TileChoice choose_tiles(uint64_t m, uint64_t n, int sms) {
   TileChoice t;
   t.subs = m > 128 ? 2 : 1;
   const uint64_t mt = ceil_div(m, 128 * (uint64_t)t.subs);
-  uint64_t bn = ceil_div(n * mt, (uint64_t)sms);
+  // columns per tile so that mt rows of tiles fit one wave of `sms` CTAs
+  const uint64_t per_row = (uint64_t)sms / mt > 0 ? (uint64_t)sms / mt : 1;
+  uint64_t bn = ceil_div(n, per_row);
   bn = ceil_div(bn, 16) * 16;
   if (bn < 32) bn = 32;
   if (bn > 256) bn = 256;
@@ -850,24 +852,25 @@ uint64_t gemm_workspace_bytes(int, uint64_t m, uint64_t, uint64_t k) {
 // dequantisation and no MMAs keeps most of it), so fewer stages per CTA is
 // what shortens such a call: s CTAs per tile (s = 2, 4 or 8) each take 1/s of
 // K and a sum pass adds the s partial planes.  s is the largest that keeps
-// tiles at most 112 columns wide, each part whole 256-value blocks, one wave
-// of one CTA per SM, and the planes within 256 MB.  Up to 128 rows (128-row
-// tiles) that is the rule.  Past 128 rows (256-row tiles) a split pays only
-// where the unsplit tiles would be under 64 columns wide, or, up to 512 rows,
-// where K is 8,192 or longer; one B200, against one pass: M = 512, N 1,792,
-// K 4,096 37.2 -> 30.5 us; M = 512, N 1,024, K 8,192 67.6 -> 30.6 us; M = 512,
-// N 3,584, K 8,192 74.7 -> 63.3 us; M = 256, N 1,792 35.8 -> 23.8 us; M = 2,048,
-// K 8,192, N 128 / 256 78.6 / 79.1 -> 33.6 / 42.8 us; M = 1,024, N 256, K 8,192
-// 69.0 -> 22.7 us; while M = 512, N 3,584, K 4,096 stays one pass (42.3 against
-// 43.0 us split).  These are the narrow shards of tensor-parallel prefill.
+// tiles at most 112 columns wide (128 past 128 rows), each part whole
+// 256-value blocks, one wave of one CTA per SM, and the planes within 256 MB.
+// Up to 128 rows (128-row tiles) that is the rule.  Past 128 rows (256-row
+// tiles) a split pays only where the unsplit tiles would be under 64 columns
+// wide or K is 8,192 or longer; one B200, against one pass: M = 512, N 1,792,
+// K 4,096 37.2 -> 30.5 us; M = 512, N 1,024, K 8,192 67.6 -> 30.6 us; M = 256,
+// N 1,792 35.8 -> 23.8 us; M = 2,048, K 8,192, N 128 / 512 / 1,024 78.6 / 80.0
+// / 86.8 -> 33.8 / 54.2 / 78.4 us; M = 2,048, N 1,024, K 28,672 285.7 -> 218.3
+// us; while M = 512, N 3,584, K 4,096 stays one pass (42.3 against 43.0 us
+// split).  These are the narrow shards of tensor-parallel prefill.
 static int choose_split(uint64_t m, uint64_t n, uint64_t k, int sms) {
   int best = 1;
-  if (m > 128 && choose_tiles(m, n, sms).bn >= 64 && !(m <= 512 && k >= 8192)) return best;
+  if (m > 128 && choose_tiles(m, n, sms).bn >= 64 && k < 8192) return best;
   const uint64_t mt = ceil_div(m, m > 128 ? 256 : 128);  // row tiles
   for (int s = 2; s <= 8; s *= 2) {
     if (k % (256ull * s) != 0 || (uint64_t)s * m * n * 4 > (256ull << 20)) break;
     const TileChoice t = choose_tiles(m, n, sms / s);
-    if (t.bn > 112 || (uint64_t)s * mt * ceil_div(n, (uint64_t)t.bn) > (uint64_t)sms) break;
+    if (t.bn > (m > 128 ? 128 : 112) || (uint64_t)s * mt * ceil_div(n, (uint64_t)t.bn) > (uint64_t)sms)
+      break;
     best = s;
   }
   return best;

@@ -194,9 +194,10 @@ def test_gemm_config1_sampled_columns(torch_cuda, oracle):
                                          (8, 512, 1536, 2), (64, 14336, 4096, 1),
                                          (16, 4096, 4096, 4), (200, 1000, 1024, 4),
                                          (512, 1792, 4096, 4), (256, 1792, 4096, 8),
-                                         (512, 1024, 8192, 4), (512, 3584, 8192, 2),
+                                         (512, 1024, 8192, 8), (512, 3584, 8192, 2),
                                          (512, 3584, 4096, 1), (600, 1024, 8192, 4),
-                                         (2048, 128, 8192, 8), (2048, 512, 8192, 2),
+                                         (2048, 128, 8192, 8), (2048, 512, 8192, 4),
+                                         (2048, 1024, 28672, 2),
                                          (1024, 256, 8192, 8)])
 def test_gemm_split_k(torch_cuda, oracle, fmt, m, n, k, parts):
     """With the preferred workspace a call with narrow tiles (or, for 129..512
