@@ -54,9 +54,17 @@ struct Layout {
 // The reference's run quant value for a 4-bit index (IQ4_NL's non-linear
 // codebook; Q4_0's q - 8).  The IQ4_NL values are the ggml format constant.
 __host__ __device__ inline int iq4nl_value(int i) {
+#ifdef __CUDA_ARCH__
+  // the same 16 values as the bytes of four words, picked with byte permutes:
+  // a run-time index into a local array would go through local memory
+  const uint32_t lo = __byte_perm(0xBFAD9881u, 0xF6EADDCFu, (uint32_t)(i & 7));
+  const uint32_t hi = __byte_perm(0x26190D01u, 0x71594535u, (uint32_t)(i & 7));
+  return (int)(int8_t)((i & 8 ? hi : lo) & 0xFFu);
+#else
   const int8_t t[16] = {-127, -104, -83, -65, -49, -35, -22, -10,
                         1,    13,   25,  38,  53,  69,  89,  113};
   return t[i & 15];
+#endif
 }
 
 __device__ __forceinline__ float f16_bits_to_f32(uint32_t bits) {

@@ -218,6 +218,56 @@ __device__ __forceinline__ void decode_run(int fmt, const uint8_t *__restrict__ 
   }
 }
 
+// One element of decode_run: value i of run u of stored row `row`, as
+// scale[i / 16] * q[i] - min[i / 16] with the same roundings, decoding only
+// that element's code and its run's factors (the input-major product and the
+// embedding lookup use one value of a run at a time).
+__device__ __forceinline__ float decode_value(int fmt, const uint8_t *__restrict__ w,
+                                              const Layout &L, uint64_t row, uint64_t u, int i) {
+  const uint8_t *sc = w + L.qs_bytes + row * L.sc_row;
+  const uint8_t *qrow = w + row * L.qs_row;
+  int q;
+  float scale, mn = 0.0f;
+  if (fmt == Q6_K) {
+    const int wd = i / 8;
+    const uint32_t word = *reinterpret_cast<const uint32_t *>(qrow + q6k_nib_offset(u) + 4 * wd);
+    const uint32_t hw = *reinterpret_cast<const uint32_t *>(qrow + q6k_high_offset(u) + 4 * (wd >> 1));
+    uint32_t ev, od;
+    q6k_codes(word, hw, wd, ev, od);
+    q = (int)((((i & 1) ? od : ev) >> (8 * ((i % 8) / 2))) & 0xFF) - 32;
+    const uint8_t *hd = sc + (u / 8) * 32;
+    const float d = f16_bits_to_f32(hd[16] | (hd[17] << 8));
+    scale = __fmul_rn(d, (float)(int8_t)hd[2 * (int)(u % 8) + i / 16]);
+  } else if (fmt == Q8_0) {
+    q = (int)(int8_t)qrow[u * 32 + i];
+    scale = f16_bits_to_f32(sc[u * 2] | (sc[u * 2 + 1] << 8));
+  } else {
+    const uint32_t word = *reinterpret_cast<const uint32_t *>(qrow + u * 16 + 4 * (i / 8));
+    if (fmt == Q5_K || fmt == Q4_K) {
+      const uint8_t *hd = sc + (u / 8) * (fmt == Q5_K ? 48 : 16);
+      if (fmt == Q5_K) {
+        const uint32_t hb = *reinterpret_cast<const uint32_t *>(hd + 16 + 4 * (u % 8));
+        uint32_t ev, od;
+        q5k_codes(word, hb, i / 8, ev, od);
+        q = (int)((((i & 1) ? od : ev) >> (8 * ((i % 8) / 2))) & 0xFF);
+      } else {
+        q = (int)((word >> (4 * (i % 8))) & 0xF);
+      }
+      const uint4 h = *reinterpret_cast<const uint4 *>(hd);
+      const float d = f16_bits_to_f32(h.x), dmin = f16_bits_to_f32(h.x >> 16);
+      uint32_t s, m;
+      q4k_scale_min((int)(u % 8), h.y, h.z, h.w, s, m);
+      scale = __fmul_rn(d, (float)s);
+      mn = __fmul_rn(dmin, (float)m);
+    } else {
+      const int nib = (int)((word >> (4 * (i % 8))) & 0xF);
+      q = fmt == Q4_0 ? nib - 8 : iq4nl_value(nib);
+      scale = f16_bits_to_f32(sc[u * 2] | (sc[u * 2 + 1] << 8));
+    }
+  }
+  return __fsub_rn(__fmul_rn(scale, (float)q), mn);
+}
+
 __global__ void mgb_dequantize_kernel(int fmt, const uint8_t *__restrict__ w, uint64_t n, uint64_t k,
                                   float *__restrict__ out) {
   const Layout L(fmt, n, k);
@@ -229,6 +279,7 @@ __global__ void mgb_dequantize_kernel(int fmt, const uint8_t *__restrict__ w, ui
     float scale[2], min[2];
     decode_run(fmt, w, L, row, u, q, scale, min);
     float4 *o = reinterpret_cast<float4 *>(out + row * k + u * RUN);
+#pragma unroll
     for (int i = 0; i < 8; ++i) {
       float v[4];
       for (int e = 0; e < 4; ++e)
@@ -256,11 +307,7 @@ __global__ void mgb_input_major_kernel(int fmt, const uint8_t *__restrict__ w, u
     for (uint64_t j = 0; j < k_rows; ++j) {
       const float a = x[r * k_rows + j];
       if (a == 0.0f) continue;
-      int q[32];
-      float scale[2], min[2];
-      decode_run(fmt, w, L, j, u, q, scale, min);
-      const float v = __fsub_rn(__fmul_rn(scale[i / 16], (float)q[i]), min[i / 16]);
-      acc = __fadd_rn(acc, __fmul_rn(a, v));
+      acc = __fadd_rn(acc, __fmul_rn(a, decode_value(fmt, w, L, j, u, i)));
     }
     y[t] = acc;
   }
@@ -298,11 +345,7 @@ __global__ void mgb_embedding_kernel(int fmt, const uint8_t *__restrict__ w, uin
     }
     const uint64_t token = (uint64_t)raw;
     const uint64_t row = transposed ? j : token, col = transposed ? token : j;
-    int q[32];
-    float sc[2], mn[2];
-    decode_run(fmt, w, L, row, col / RUN, q, sc, mn);
-    const int i = (int)(col % RUN);
-    float v = __fsub_rn(__fmul_rn(sc[i / 16], (float)q[i]), mn[i / 16]);
+    float v = decode_value(fmt, w, L, row, col / RUN, (int)(col % RUN));
     if (has_scale) v = __fmul_rn(v, scale);
     out[e] = v;
   }
