@@ -303,8 +303,22 @@ __global__ void mgb_input_major_kernel(int fmt, const uint8_t *__restrict__ w, u
     const uint64_t r = t / n_cols, c = t % n_cols;
     const uint64_t u = c / RUN;
     const int i = (int)(c % RUN);
+    // eight input rows' loads in flight at a time; the products are still
+    // added one by one in row order, zero activations skipped
     float acc = 0.0f;
-    for (uint64_t j = 0; j < k_rows; ++j) {
+    uint64_t j = 0;
+    for (; j + 8 <= k_rows; j += 8) {
+      float a[8], v[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        a[t] = x[r * k_rows + j + t];
+        v[t] = decode_value(fmt, w, L, j + t, u, i);
+      }
+#pragma unroll
+      for (int t = 0; t < 8; ++t)
+        if (a[t] != 0.0f) acc = __fadd_rn(acc, __fmul_rn(a[t], v[t]));
+    }
+    for (; j < k_rows; ++j) {
       const float a = x[r * k_rows + j];
       if (a == 0.0f) continue;
       acc = __fadd_rn(acc, __fmul_rn(a, decode_value(fmt, w, L, j, u, i)));
