@@ -229,7 +229,7 @@ def test_gemm_split_k(torch_cuda, oracle, fmt, m, n, k, parts):
     assert np.array_equal(yr, (y + res).astype(np.float32))
 
 
-@pytest.mark.parametrize("m", [1, 2, 64])
+@pytest.mark.parametrize("m", [1, 2, 64, 300])
 def test_addend_epilogues(torch_cuda, oracle, m):
     torch = torch_cuda
     fmt, n, k = mgb.Q4_K, 96, 512
@@ -242,6 +242,11 @@ def test_addend_epilogues(torch_cuda, oracle, m):
     oracle.assert_close(_qmatmul(torch, fmt, wdev, n, k, x, bias), oracle.add(base, bias), tol)
     resid = oracle.test_activations(m, n, 11)
     oracle.assert_close(_qmatmul(torch, fmt, wdev, n, k, x, resid), oracle.add(resid, base), tol)
+    # fused equals unfused bit for bit, as the reference requires of matmul-bias /
+    # matmul-residual against matmul then add (src/tests.rs:740-888)
+    plain = _qmatmul(torch, fmt, wdev, n, k, x)
+    assert np.array_equal(_qmatmul(torch, fmt, wdev, n, k, x, bias), plain + bias[None, :])
+    assert np.array_equal(_qmatmul(torch, fmt, wdev, n, k, x, resid), resid + plain)
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
