@@ -557,6 +557,16 @@ def run_b200(args) -> None:
                 "timing": f"CUDA events around {reps} replays of a CUDA graph of {RV} "
                           "back-to-back launches (programmatic dependent launches)",
                 "cpu_baseline": None}
+        # the same GEMV at config 4's widest decode projection (Llama-3-70B
+        # gate/up: x[1, 8192] x W[28672 x 8192]), where the weight stream, not
+        # the launch floor, sets the time
+        l_ms, lb, LRV, lreps = graph_ms(fmt, 1, 28672, 8192, 60)
+        l_gbs = (lb + 8192 * 4 + 28672 * 4) / (l_ms * 1e-3) / 1e9
+        gemv["large"] = {"shape": "x[1,8192] x Q4_K W[28672x8192] (config 4 gate/up)",
+                         "us_per_launch": l_ms * 1e3, "gbs": l_gbs,
+                         "frac_hbm": l_gbs / pk["hbm_gbs"],
+                         "timing": f"{lreps} replays of a graph of {LRV} launches over "
+                                   f"{LRV} weight copies"}
 
         # every format the Provider executes, at config 2's shape (K = 4096,
         # N = 14336): decode GEMV (M = 1) weight GB/s and prefill step (M = 512,
