@@ -820,6 +820,26 @@ TileChoice choose_tiles(uint64_t m, uint64_t n, int sms) {
   uint64_t bn = ceil_div(n, per_row);
   bn = ceil_div(bn, 16) * 16;
   if (bn < 32) bn = 32;
+  if (bn > 256 && mt * ceil_div(n, 256) <= 4 * (uint64_t)sms) {
+    // one to four waves even at the widest tile: the width with the least
+    // waves x (fixed + width), a tile's time being about 256 columns' worth of
+    // fixed per-step cost plus its width (measured at M = 512: 60.5, 52.5, 42.3
+    // and 37.2 us for 208, 112, 64 and 32 columns over the same K).  A nearly
+    // empty last wave costs a whole tile time here (M = 2,048, K = 8,192, one
+    // B200: N 14,336 at 208 columns 542 -> 458 us, N 8,192 at 224 290 -> 282 us,
+    // and N 8,192, K 28,672 985 -> 940 us); over more waves the CTAs drift apart
+    // and the widest tile stays best (N 28,672: 973 us at 256 against 982 at 224).
+    uint64_t best = 256, best_cost = ~0ull;
+    for (uint64_t w = 256; w >= 128; w -= 16) {
+      const uint64_t waves = ceil_div(mt * ceil_div(n, w), (uint64_t)sms);
+      const uint64_t cost = waves * (256 + w);
+      if (cost < best_cost) {
+        best = w;
+        best_cost = cost;
+      }
+    }
+    bn = best;
+  }
   if (bn > 256) bn = 256;
   t.bn = (int)bn;
   return t;
