@@ -273,9 +273,11 @@ uint64_t mgb_packed_bytes(int32_t format, uint64_t stored_rows, uint64_t stored_
 mgb_status mgb_repack(int32_t format, const void *ggml_blocks, uint64_t stored_rows,
                       uint64_t stored_cols, void *out, void *stream);
 /* Scratch bytes `mgb_qmatmul` wants for this shape (0 when none): the bf16
- * copy of x and, for m <= 128 rows whose output is narrow enough (one wave of
- * tiles at most 112 columns wide with K split s ways, s = 2, 4 or 8, k a
- * multiple of 256 s), s f32 [m, n] planes: each of s CTAs per tile computes
+ * copy of x and, for a shape whose tiles would be narrow (up to 128 rows: one
+ * wave of tiles at most 112 columns wide with K split s ways; past 128 rows:
+ * unsplit tiles under 64 columns wide or K >= 8192, split tiles at most 128
+ * wide; s = 2, 4 or 8, k a multiple of 256 s, the planes within 256 MB), s f32
+ * [m, n] planes: each of s CTAs per tile computes
  * 1/s of K into its plane and a sum pass adds them in plane order (a
  * different f32 summation order than one pass, same tolerance, deterministic).
  * Any workspace of at least mgb_qmatmul_min_workspace_bytes (the bf16 copy

@@ -33,8 +33,9 @@
 //              registers, or, when every rank's y receives the tile (fused
 //              all-gather over NVLink), through shared memory in whole row
 //              segments.
-// Up to 128 activation rows, a call may split K over 2, 4 or 8 CTAs per tile
-// (blockIdx.z), each writing an f32 partial plane that mgb_splitk_sum_kernel adds.
+// A call with narrow tiles (choose_split) may split K over 2, 4 or 8 CTAs per
+// tile (blockIdx.z), each writing an f32 partial plane that mgb_splitk_sum_kernel
+// adds.
 // Every CTA loads its own tiles from this GPU's HBM (no cluster-shared loads).
 // Every wait is bounded; on expiry the kernel records ERR_WAIT_TIMEOUT, skips
 // the remaining work, waits (bounded) for its own copies and MMAs, frees TMEM

@@ -33,8 +33,8 @@ cudaError_t launch_gemv(int fmt, const void *w, uint64_t n, uint64_t k, const fl
                         int *err, int sms, cudaStream_t stream);
 
 // gemm.cu: tensor-core path (bf16 operands, f32 accumulation) for m > 2.
-// The minimum scratch is the bf16 activation copy; the preferred size adds two
-// f32 [m, n] planes with which a single-output call of m <= 128 splits K.
+// The minimum scratch is the bf16 activation copy; the preferred size adds the
+// 2, 4 or 8 f32 [m, n] planes with which a call of narrow tiles splits K.
 uint64_t gemm_workspace_bytes(int fmt, uint64_t m, uint64_t n, uint64_t k);
 uint64_t gemm_workspace_bytes_preferred(int fmt, uint64_t m, uint64_t n, uint64_t k);
 bool gemm_supported(int fmt, uint64_t m, uint64_t n, uint64_t k);
