@@ -145,3 +145,16 @@ def test_embedding_arguments_are_checked_before_device_work():
         mgb.INVALID_ARGUMENT
     assert lib.mgb_embedding(mgb.Q8_0, None, 8, 64, 0, fake, 1, 0, 1.0, fake, None, None) == \
         mgb.INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("m,n,k,parts", [
+    (16, 14336, 4096, 1), (16, 4096, 4096, 4), (16, 1024, 4096, 8),  # config 3, M = 16
+    (512, 14336, 4096, 1), (512, 7168, 4096, 1), (512, 1792, 4096, 4),  # config 1 shards
+    (2048, 8192, 8192, 1), (2048, 1024, 8192, 2), (2048, 512, 8192, 4),  # config 4, N = 1, 2
+    (2048, 128, 8192, 8), (2048, 1024, 28672, 2), (65536, 64, 4096, 1)])
+def test_split_choices(m, n, k, parts):
+    """The K split the preferred workspace provides for the benchmark shapes and
+    their tensor-parallel shards (host logic: no device work)."""
+    extra = mgb.qmatmul_workspace_bytes(mgb.Q4_K, m, n, k) - \
+        mgb.qmatmul_min_workspace_bytes(mgb.Q4_K, m, n, k)
+    assert extra == (0 if parts == 1 else parts * m * n * 4)
